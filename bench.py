@@ -1,0 +1,408 @@
+"""Benchmark of the fused Mamba-3 recurrence hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg1|cfg2]
+
+One step is one pass of the hot path over one batch: at the default
+``cfg1`` (B=16 clips, T=200, H=12, Hq=1, N=128, P=64, R=32) that is the
+``fused_recurrence`` launch — C/B RMSNorm of the raw q/k rows, the fused
+recurrence with its SiLU(z) gate, and the length mask (lengths ~ U{120..200}).
+
+Timing: W untimed eager warm-up steps; then the K timed steps run as CUDA-graph
+replays, each step on the next of S input sets whose total size exceeds the
+126 MB L2 (so every step reads its inputs from HBM), bracketed by a barrier and
+``torch.cuda.synchronize()`` and timed with CUDA events on the launching
+stream; the max over ranks is reported. Under torchrun every rank runs its own
+batch (weak scaling; no collective on the data path).
+
+``--impl reference`` times the reference's arithmetic on the host CPU (the
+oracle port under ``oracle/``, all host threads) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "trifusion-fp-kernel_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fused_mamba tokens/s + HBM GB/s vs peak; audio-sec/s at 1/2/4/8 B200"
+L2_BYTES = 126 * 2 ** 20
+FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    # name: (B, T, H, lengths spec)
+    "cfg1": dict(batch=16, time=200, heads=12, lengths=("uniform", 120, 200)),
+    "cfg2": dict(batch=2, time=3600, heads=12, lengths=("fixed", [3600, 2871])),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_lengths(spec, batch, seed=0):
+    import torch
+    from trifusion_b200.synthetic import lengths_uniform
+    if spec[0] == "uniform":
+        return lengths_uniform(batch, spec[1], spec[2], seed)
+    return torch.tensor(spec[1], dtype=torch.int64)
+
+
+def algorithmic_bytes(b, t, h, lengths, hq=1, n=128, p=64, r=32, trap_bytes=4):
+    """Bytes the masked step must move: every input row t < lengths[b] read
+    once (q/k once per group, angles once: head stride 0), every output row
+    written once (zeros past the length), plus the per-head parameters."""
+    rows = int(sum(min(int(x), t) for x in lengths))
+    return (2 * rows * hq * n * 2          # q, k
+            + 2 * rows * h * p * 2          # v, z
+            + rows * h * (4 + 4 + trap_bytes)  # adt, dt, trap
+            + rows * r * 2                  # raw angles (broadcast over heads)
+            + b * t * h * p * 2             # out (all rows)
+            + h * (2 * n + 1) * 4 + 2 * n * 4 + b * 8)  # qb, kb, d, norm weights, lengths
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons in the background."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.samples.append((time.time(), line.strip()))
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self, t0, t1):
+        rows = [s for ts, s in self.samples if t0 <= ts <= t1]
+        if not rows:  # region shorter than the sampling interval: nearest samples
+            rows = [s for ts, s in sorted(self.samples, key=lambda x: abs(x[0] - (t0 + t1) / 2))[:3]]
+        mhz, max_mhz, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in rows:
+            f = [x.strip() for x in row.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                max_mhz = float(f[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def cpu_port_time(workload, inputs_np, lengths_np, qw, kw, budget_s=12.0):
+    """Time the oracle port of the step on the host (rank 0, N=1 only)."""
+    import numpy as np
+    from oracle import mamba_oracle as O
+
+    def step():
+        a = list(inputs_np)
+        a[0] = O.rms(a[0], qw)
+        a[1] = O.rms(a[1], kw)
+        return O.mask_rows(O.fused_mamba(*a, dtype=np.float32), lengths_np)
+
+    step()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 50:
+            break
+    return n, el
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, wl):
+    """`--impl reference`: the reference arithmetic (oracle port) on host CPU."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = host_threads()
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    import numpy as np
+    import torch
+    from trifusion_b200.synthetic import recurrence_inputs, norm_weight
+    torch.set_num_threads(cores)
+    b, t, h = wl["batch"], wl["time"], wl["heads"]
+    inputs = [a.float().numpy() for a in recurrence_inputs(b, t, h, kind="baseline")]
+    lengths = make_lengths(wl["lengths"], b).numpy()
+    qw, kw = norm_weight(128, 1).numpy(), norm_weight(128, 2).numpy()
+    from oracle import mamba_oracle as O
+
+    def step():
+        a = list(inputs)
+        a[0] = O.rms(a[0], qw)
+        a[1] = O.rms(a[1], kw)
+        return O.mask_rows(O.fused_mamba(*a, dtype=np.float32), lengths)
+
+    for _ in range(max(args.warmup, 0) and 1):
+        step()
+    steps = max(1, min(args.steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    el = time.perf_counter() - t0
+    value = b * t * steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": 1, "ms_per_step": el / steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "B": b, "T": t, "H": h, "Hq": 1, "N": 128, "P": 64,
+                   "R": 32, "step": "rms(q,k) -> fused recurrence -> length mask"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps} full {args.workload} batches (B={b}, T={t}, H={h}), numpy FP32"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference arm: the oracle port of the reference arithmetic (mamba_fused.py:72-152, "
+                "native.py:8-39, masking.py:10-11) on the host cores; the reference itself is Triton "
+                "for sm_89 and has no CPU implementation of this path",
+    }
+    if args.steps != steps:
+        line["note"] += f"; steps capped at {steps} of {args.steps} to bound CPU time"
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+        return
+    import torch
+    import torch.distributed as dist
+    from trifusion_b200 import fused_recurrence
+    from trifusion_b200.synthetic import recurrence_inputs, norm_weight
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    b, t, h = wl["batch"], wl["time"], wl["heads"]
+    lengths_cpu = make_lengths(wl["lengths"], b, seed=rank)
+    base = recurrence_inputs(b, t, h, kind="baseline", seed=rank)
+    qw_cpu, kw_cpu = norm_weight(128, 1), norm_weight(128, 2)
+    qw, kw = qw_cpu.to(dev), kw_cpu.to(dev)
+    step_bytes = algorithmic_bytes(b, t, h, lengths_cpu.tolist())
+    full_set_bytes = sum(x.numel() * x.element_size() for i, x in enumerate(base) if i != 8) + \
+        b * t * 32 * 2 + b * t * h * 64 * 2  # + shared angles + the output buffer
+    nsets = max(2, math.ceil(3 * L2_BYTES / full_set_bytes))
+    sets = []
+    for s in range(nsets):
+        dev_args = [x.to(dev) if i != 8 else None for i, x in enumerate(base)]
+        ang_src = base[8][:, :, :1].contiguous().to(dev)  # [B,T,1,32]; heads share it
+        dev_args[8] = ang_src.expand(b, t, h, 32)
+        sets.append(dict(args=dev_args, ang=ang_src, lengths=lengths_cpu.to(dev),
+                         out=torch.empty(b, t, h, 64, dtype=torch.bfloat16, device=dev)))
+
+    def step(i):
+        st = sets[i % nsets]
+        fused_recurrence(*st["args"], q_norm=qw, k_norm=kw, lengths=st["lengths"], out=st["out"])
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 0)):
+            step(i)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(nsets):
+                step(i)
+        rest = args.steps % nsets
+        # load phase so clock samples reflect a busy GPU
+        sampler = ClockSampler(local)
+        sampler.start()
+        tl0 = time.time()
+        while time.time() - tl0 < 0.6:
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        tw0 = time.time()
+        ev0.record(stream)
+        for _ in range(args.steps // nsets):
+            graph.replay()
+        for i in range(rest):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        tw1 = time.time()
+        if world > 1:
+            dist.barrier()
+        sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_per_step = ms / max(args.steps, 1)
+    value = world * b * t / (ms_per_step / 1e3)
+    hbm_peak, peak_kind = peaks()
+    achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+
+    # End to end through the public call with host buffers: pinned host inputs
+    # copied in, the call, the output copied back, every step.
+    host_in = [x.pin_memory() if i != 8 else x[:, :, :1].contiguous().pin_memory()
+               for i, x in enumerate(base)]
+    host_len = lengths_cpu.pin_memory()
+    host_out = torch.empty(b, t, h, 64, dtype=torch.bfloat16).pin_memory()
+    e = sets[0]
+    dst = [x if i != 8 else e["ang"] for i, x in enumerate(e["args"])]
+    h2d = sum(x.numel() * x.element_size() for x in host_in) + host_len.numel() * 8
+    d2h = host_out.numel() * 2
+    with torch.cuda.stream(stream):
+        def e2e_step():
+            for x, y in zip(host_in, dst):
+                y.copy_(x, non_blocking=True)
+            e["lengths"].copy_(host_len, non_blocking=True)
+            fused_recurrence(*e["args"], q_norm=qw, k_norm=kw, lengths=e["lengths"], out=e["out"])
+            host_out.copy_(e["out"], non_blocking=True)
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    e_ms = e0.elapsed_time(e1) / max(args.e2e_steps, 1)
+    if world > 1:
+        tt = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    e2e_value = world * b * t / (e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import numpy as np
+        np_in = [x.float().numpy() for x in base]
+        n, el = cpu_port_time(args.workload, np_in, lengths_cpu.numpy(), qw_cpu.numpy(), kw_cpu.numpy())
+        cpu = {"value": b * t * n / el, "unit": "tokens/s", "cores": host_threads(), "kind": "port",
+               "sample": f"{n} full {args.workload} batches through the numpy oracle (FP32), {el:.1f} s"}
+
+    if world > 1:
+        dist.barrier()
+        del graph
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    clocks = sampler.summary(tl0, tw1)
+    traffic = measured_traffic(args.workload)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "B": b, "T": t, "H": h, "Hq": 1, "N": 128, "P": 64,
+                   "R": 32, "lengths": lengths_cpu.tolist(),
+                   "step": "RMSNorm(q,k) + fused recurrence + SiLU(z) gate + length mask, one launch",
+                   "l2": f"inputs cycled over {nsets} sets ({nsets * full_set_bytes / 2**20:.0f} MiB > L2)",
+                   "parallelism": f"replicas x{world} (one batch per GPU)"},
+        "hbm_gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": step_bytes},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def measured_traffic(workload):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    path = ROOT / "profiles" / "traffic.txt"
+    if not path.exists():
+        return None
+    for row in path.read_text().splitlines():
+        f = row.split()
+        if len(f) >= 3 and f[0] == workload:
+            try:
+                return float(f[2])
+            except ValueError:
+                return None
+    return None
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,78 @@
+"""C-ABI library checks that need no GPU: it loads, exports every symbol the
+public header declares, and rejects bad arguments before touching a device."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from trifusion_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "trifusion_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tf_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_symbols()
+    assert "tf_fused_mamba_fwd" in names and len(names) >= 5
+    for name in names:
+        assert hasattr(lib, name), name
+    # The ctypes table covers the header exactly.
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    lib = _lib.lib()
+    assert lib.tf_status_string(0) == b"ok"
+    assert lib.tf_status_string(1).decode() == _lib.SHAPE_MESSAGE
+    assert lib.tf_version() >= 100
+
+
+def test_invalid_arguments_rejected_without_a_device():
+    lib = _lib.lib()
+    strides = _lib.int64_array([0] * 33)
+    # Null strides, bad dtype, groups not dividing heads: validated on the host.
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), None, 1, 1, 4, 1, None) == _lib.TF_ERR_ARG
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 7, *([None] * 6), strides, 1, 1, 4, 1, None) == _lib.TF_ERR_ARG
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), strides, 1, 1, 4, 3, None) == _lib.TF_ERR_ARG
+    # Empty problems are a no-op success.
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), strides, 0, 5, 4, 1, None) == _lib.TF_OK
+    with pytest.raises(ValueError):
+        _lib.check(_lib.TF_ERR_ARG)
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.TF_ERR_LAUNCH)
+
+
+def test_python_shape_gate_matches_reference_message():
+    from trifusion_b200 import fused_mamba
+    from trifusion_b200.synthetic import recurrence_inputs
+    args = list(recurrence_inputs(1, 4, 2))
+    args[0] = args[0][..., :64].contiguous()
+    with pytest.raises(ValueError, match=r"^L4 recurrence requires state=128, head=64, rotary=32$"):
+        fused_mamba(*args)
+
+
+def test_cpu_tensors_fail_loudly_no_fallback():
+    from trifusion_b200 import fused_mamba
+    from trifusion_b200.synthetic import recurrence_inputs
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        fused_mamba(*recurrence_inputs(1, 4, 2))
+
+
+def test_lazy_import_keeps_torch_out():
+    import subprocess
+    import sys
+    root = Path(__file__).resolve().parent.parent / "trifusion-fp-kernel_b200"
+    code = ("import sys; sys.path.insert(0, %r); import trifusion_b200 as t; "
+            "assert 'torch' not in sys.modules; assert t.__version__ == '0.1.0'; "
+            "assert {'configure_runtime','load_student','InferenceEngine','fused_mamba'} <= set(dir(t))"
+            % str(root))
+    subprocess.run([sys.executable, "-c", code], check=True)

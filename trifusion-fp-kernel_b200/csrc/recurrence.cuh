@@ -1,0 +1,35 @@
+// Parameters of the fused Mamba-3 recurrence launch (shared by the kernels and
+// the C-ABI launcher).
+#pragma once
+
+#include "tf_common.cuh"
+
+namespace tf {
+
+struct RecurrenceParams {
+  const bf16* q;       // [B,T,Hq,128]
+  const bf16* k;       // [B,T,Hq,128]
+  const bf16* v;       // [B,T,H,64]
+  const bf16* z;       // [B,T,H,64]
+  const bf16* ang;     // [B,T,H,32] raw angle controls
+  const float* adt;    // [B,H,T]
+  const float* dt;     // [B,H,T]
+  const void* trap;    // [B,H,T] f32 or bf16, pre-sigmoid
+  const float* qb;     // [H,128]
+  const float* kb;     // [H,128]
+  const float* d;      // [H]
+  const float* qw;     // [128] C_norm weight, or null
+  const float* kw;     // [128] B_norm weight, or null
+  const int64_t* lengths;  // [B] or null
+  bf16* out;           // [B,T,H,64]
+  int64_t sq[4], sk[4], sv[4], sz[4], sa[4], so[4];
+  int64_t sadt[3], sdt[3], str[3];
+  float eps;
+  int trap_bf16;
+  int B, T, H, Hq;
+};
+
+// Launch the recurrence on `stream`; returns a tf_status code.
+int launch_recurrence(const RecurrenceParams& p, cudaStream_t stream);
+
+}  // namespace tf

@@ -1,0 +1,142 @@
+// C ABI of trifusion_b200: argument validation, status codes and launches.
+// Declarations and the reference interface each entry point replaces are in
+// include/trifusion_b200.h.
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/trifusion_b200.h"
+#include "recurrence.cuh"
+
+namespace tf {
+namespace {
+
+thread_local char g_last_error[256] = "";
+
+// Per-device "is sm_100" cache: 0 = unknown, 1 = yes, 2 = no. Filled on the
+// first call for a device; later calls only read it (safe under graph capture).
+constexpr int kMaxDevices = 64;
+int g_arch_ok[kMaxDevices] = {0};
+
+int check_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    snprintf(g_last_error, sizeof g_last_error, "%s", cudaGetErrorString(e));
+    return TF_ERR_DEVICE;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return TF_ERR_DEVICE;
+  if (g_arch_ok[dev] == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    g_arch_ok[dev] = (major == 10 && minor == 0) ? 1 : 2;
+  }
+  return g_arch_ok[dev] == 1 ? TF_OK : TF_ERR_DEVICE;
+}
+
+int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return TF_OK;
+  snprintf(g_last_error, sizeof g_last_error, "%s", cudaGetErrorString(e));
+  return TF_ERR_LAUNCH;
+}
+
+int recurrence_entry(const void* q, const void* k, const void* v, const float* adt,
+                     const float* dt, const void* trap, int trap_dtype, const float* qb,
+                     const float* kb, const void* angles, const float* d, const void* z,
+                     void* out, const int64_t* strides, int batch, int seqlen, int heads,
+                     int groups, const float* qw, const float* kw, float eps,
+                     const int64_t* lengths, void* stream) {
+  if (!strides || batch < 0 || seqlen < 0 || heads < 0 || groups <= 0) return TF_ERR_ARG;
+  if (trap_dtype != TF_F32 && trap_dtype != TF_BF16) return TF_ERR_ARG;
+  if (heads % groups != 0) return TF_ERR_ARG;
+  if (batch == 0 || seqlen == 0 || heads == 0) return TF_OK;  // empty launch grid
+  if (!q || !k || !v || !adt || !dt || !trap || !qb || !kb || !angles || !d || !z || !out)
+    return TF_ERR_ARG;
+  RecurrenceParams p{};
+  p.q = static_cast<const bf16*>(q);
+  p.k = static_cast<const bf16*>(k);
+  p.v = static_cast<const bf16*>(v);
+  p.z = static_cast<const bf16*>(z);
+  p.ang = static_cast<const bf16*>(angles);
+  p.adt = adt;
+  p.dt = dt;
+  p.trap = trap;
+  p.trap_bf16 = trap_dtype == TF_BF16;
+  p.qb = qb;
+  p.kb = kb;
+  p.d = d;
+  p.qw = qw;
+  p.kw = kw;
+  p.eps = eps;
+  p.lengths = lengths;
+  p.out = static_cast<bf16*>(out);
+  const int64_t* s = strides;
+  for (int i = 0; i < 4; ++i) p.sq[i] = s[i];
+  for (int i = 0; i < 4; ++i) p.sk[i] = s[4 + i];
+  for (int i = 0; i < 4; ++i) p.sv[i] = s[8 + i];
+  for (int i = 0; i < 3; ++i) p.sadt[i] = s[12 + i];
+  for (int i = 0; i < 3; ++i) p.sdt[i] = s[15 + i];
+  for (int i = 0; i < 3; ++i) p.str[i] = s[18 + i];
+  for (int i = 0; i < 4; ++i) p.sa[i] = s[21 + i];
+  for (int i = 0; i < 4; ++i) p.sz[i] = s[25 + i];
+  for (int i = 0; i < 4; ++i) p.so[i] = s[29 + i];
+  // The innermost dimension of q, k, v, z and out must be contiguous.
+  if (p.sq[3] != 1 || p.sk[3] != 1 || p.sv[3] != 1 || p.sz[3] != 1 || p.so[3] != 1)
+    return TF_ERR_LAYOUT;
+  p.B = batch;
+  p.T = seqlen;
+  p.H = heads;
+  p.Hq = groups;
+  int st = check_device();
+  if (st != TF_OK) return st;
+  st = launch_recurrence(p, static_cast<cudaStream_t>(stream));
+  if (st != TF_OK) return st;
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace tf
+
+extern "C" {
+
+const char* tf_status_string(int status) {
+  switch (status) {
+    case TF_OK: return "ok";
+    case TF_ERR_SHAPE: return "L4 recurrence requires state=128, head=64, rotary=32";
+    case TF_ERR_ARG: return "invalid argument";
+    case TF_ERR_LAYOUT: return "unsupported tensor layout (innermost dimension must be contiguous)";
+    case TF_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) GPU";
+    case TF_ERR_LAUNCH: return "CUDA launch failed";
+    case TF_ERR_SIZE: return "size exceeds the documented maximum";
+    default: return "unknown status";
+  }
+}
+
+int tf_version(void) { return 100; }
+
+const char* tf_last_cuda_error(void) { return tf::g_last_error; }
+
+int tf_fused_mamba_fwd(const void* q, const void* k, const void* v, const float* adt,
+                       const float* dt, const void* trap, int trap_dtype, const float* qb,
+                       const float* kb, const void* angles, const float* d, const void* z,
+                       void* out, const int64_t* strides, int batch, int seqlen, int heads,
+                       int groups, void* stream) {
+  return tf::recurrence_entry(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out,
+                              strides, batch, seqlen, heads, groups, nullptr, nullptr, 1e-5f,
+                              nullptr, stream);
+}
+
+int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v, const float* adt,
+                            const float* dt, const void* trap, int trap_dtype, const float* qb,
+                            const float* kb, const void* angles, const float* d, const void* z,
+                            void* out, const int64_t* strides, int batch, int seqlen,
+                            int heads, int groups, const float* q_norm_w,
+                            const float* k_norm_w, float eps, const int64_t* lengths,
+                            void* stream) {
+  return tf::recurrence_entry(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out,
+                              strides, batch, seqlen, heads, groups, q_norm_w, k_norm_w, eps,
+                              lengths, stream);
+}
+
+}  // extern "C"

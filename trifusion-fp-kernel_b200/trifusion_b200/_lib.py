@@ -1,0 +1,70 @@
+"""ctypes binding of the C-ABI library ``libtrifusion_b200.so``.
+
+The library is the product's only compute path: if it is missing or the
+current device is not a B200, calls raise; nothing falls back to PyTorch or
+the CPU. Signatures mirror ``include/trifusion_b200.h``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_native" / "libtrifusion_b200.so"
+
+TF_OK, TF_ERR_SHAPE, TF_ERR_ARG, TF_ERR_LAYOUT, TF_ERR_DEVICE, TF_ERR_LAUNCH, TF_ERR_SIZE = range(7)
+TF_F32, TF_BF16 = 0, 1
+SHAPE_MESSAGE = "L4 recurrence requires state=128, head=64, rotary=32"
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+
+# name -> argtypes; every function returns int unless listed in _RESTYPES.
+SIGNATURES = {
+    "tf_status_string": [_i],
+    "tf_version": [],
+    "tf_last_cuda_error": [],
+    "tf_fused_mamba_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
+                           _i, _i, _i, _i, _p],
+    "tf_mamba_recurrence_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
+                                _i, _i, _i, _i, _p, _p, _f, _p, _p],
+}
+_RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p}
+
+_lib = None
+
+
+def lib():
+    """Load (once) and return the library, with argument types declared."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"trifusion_b200 native library not built ({LIB_PATH}); run "
+                "`python trifusion-fp-kernel_b200/build.py` (needs nvcc, no GPU)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, args in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _lib = handle
+    return _lib
+
+
+def check(status):
+    """Raise the reference-compatible exception for a non-zero status."""
+    if status == TF_OK:
+        return
+    if status == TF_ERR_SHAPE:
+        raise ValueError(SHAPE_MESSAGE)
+    text = lib().tf_status_string(status).decode()
+    detail = lib().tf_last_cuda_error().decode()
+    if status == TF_ERR_ARG:
+        raise ValueError(f"trifusion_b200: {text}")
+    raise RuntimeError(f"trifusion_b200: {text}" + (f" ({detail})" if detail else ""))
+
+
+def int64_array(values):
+    values = list(values)
+    return (ctypes.c_int64 * len(values))(*values)

@@ -1,0 +1,114 @@
+"""Fused Mamba-3 SISO recurrence on B200 — drop-in for
+``trifusion_l4.mamba_fused.fused_mamba`` (reference ``mamba_fused.py:155-191``).
+
+The tensor contract is the reference's (``docs/api.md:61-74``); the work runs
+in the CUDA kernels of ``libtrifusion_b200.so`` on the current stream, with no
+host synchronisation, so calls can be captured in CUDA graphs.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_BF16_ARGS = ("q", "k", "v", "angles", "z")
+
+
+def _prep(q, k, v, adt, dt, trap, qb, kb, angles, d, z):
+    b, t, h, p = v.shape
+    n = q.shape[-1]
+    r = angles.shape[-1]
+    if n != 128 or p != 64 or r != 32:  # mamba_fused.py:159-160
+        raise ValueError(_lib.SHAPE_MESSAGE)
+    named = dict(q=q, k=k, v=v, angles=angles, z=z)
+    for name, x in named.items():
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"fused_mamba: {name} must be bfloat16, got {x.dtype}")
+    if q.shape != k.shape or q.shape[:2] != (b, t) or q.dim() != 4:
+        raise ValueError("fused_mamba: q and k must be [B,T,Hq,128] matching v")
+    if z.shape != v.shape or angles.shape[:3] != (b, t, h):
+        raise ValueError("fused_mamba: z must match v and angles must be [B,T,H,32]")
+    hq = q.shape[2]
+    if hq < 1 or h % hq:
+        raise ValueError("fused_mamba: H must be divisible by Hq")
+    for name, x in dict(adt=adt, dt=dt, trap=trap).items():
+        if tuple(x.shape) != (b, h, t):
+            raise ValueError(f"fused_mamba: {name} must be [B,H,T]")
+    if trap.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("fused_mamba: trap must be float32 or bfloat16")
+    dev = v.device
+    tensors = (q, k, v, adt, dt, trap, qb, kb, angles, d, z)
+    if dev.type != "cuda" or any(x.device != dev for x in tensors):
+        raise RuntimeError("fused_mamba: all tensors must be CUDA tensors on one device")
+    # Kernel requirement: unit stride in the innermost dimension of BF16 rows.
+    q, k, v, z = (x if x.stride(-1) == 1 else x.contiguous() for x in (q, k, v, z))
+    adt, dt = (x if x.dtype == torch.float32 else x.float() for x in (adt, dt))
+    qb, kb, d = (x.float().contiguous() for x in (qb, kb, d))
+    if qb.shape != (h, 128) or kb.shape != (h, 128) or d.numel() != h:
+        raise ValueError("fused_mamba: qb, kb must be [H,128] and d must be [H]")
+    return (q, k, v, adt, dt, trap, qb, kb, angles, d, z), (b, t, h, hq)
+
+
+def _strides(q, k, v, adt, dt, trap, angles, z, out):
+    s = []
+    for x in (q, k, v, adt, dt, trap, angles, z, out):
+        s.extend(x.stride())
+    return _lib.int64_array(s)
+
+
+def fused_mamba(q, k, v, adt, dt, trap, qb, kb, angles, d, z, warps=8):
+    """Fused recurrence; returns a fresh contiguous ``[B,T,H,64]`` BF16 tensor.
+
+    ``warps`` is accepted for signature compatibility; the CUDA kernel fixes
+    its own launch shape.
+    """
+    del warps
+    (q, k, v, adt, dt, trap, qb, kb, angles, d, z), (b, t, h, hq) = _prep(
+        q, k, v, adt, dt, trap, qb, kb, angles, d, z)
+    out = torch.empty_like(v, memory_format=torch.contiguous_format)
+    stream = torch.cuda.current_stream(v.device).cuda_stream
+    with torch.cuda.device(v.device):
+        _lib.check(_lib.lib().tf_fused_mamba_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(), dt.data_ptr(),
+            trap.data_ptr(), _lib.TF_BF16 if trap.dtype == torch.bfloat16 else _lib.TF_F32,
+            qb.data_ptr(), kb.data_ptr(), angles.data_ptr(), d.data_ptr(), z.data_ptr(),
+            out.data_ptr(), _strides(q, k, v, adt, dt, trap, angles, z, out),
+            b, t, h, hq, stream))
+    return out
+
+
+def fused_recurrence(q, k, v, adt, dt, trap, qb, kb, angles, d, z, *, q_norm=None,
+                     k_norm=None, lengths=None, eps=1e-5, out=None):
+    """The recurrence with the work around it fused into the same launch.
+
+    ``q_norm``/``k_norm`` ([128] FP32 weights) apply the C/B RMSNorm of the raw
+    q/k rows (reference ``mamba.py:56-57``); ``lengths`` ([B] int64, on the
+    device) zeroes output rows ``t >= lengths[b]`` (the length mask of
+    ``model.py:174``) and stops the scan there. ``out`` may be given to write
+    into a preallocated contiguous buffer.
+    """
+    (q, k, v, adt, dt, trap, qb, kb, angles, d, z), (b, t, h, hq) = _prep(
+        q, k, v, adt, dt, trap, qb, kb, angles, d, z)
+    if out is None:
+        out = torch.empty_like(v, memory_format=torch.contiguous_format)
+    qw = None if q_norm is None else q_norm.float().contiguous()
+    kw = None if k_norm is None else k_norm.float().contiguous()
+    for w in (qw, kw):
+        if w is not None and (w.numel() != 128 or w.device != v.device):
+            raise ValueError("fused_recurrence: norm weights must be [128] on the same device")
+    if lengths is not None:
+        if lengths.dtype != torch.int64 or lengths.numel() != b or lengths.device != v.device:
+            raise ValueError("fused_recurrence: lengths must be int64 [B] on the same device")
+        lengths = lengths.contiguous()
+    stream = torch.cuda.current_stream(v.device).cuda_stream
+    with torch.cuda.device(v.device):
+        _lib.check(_lib.lib().tf_mamba_recurrence_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(), dt.data_ptr(),
+            trap.data_ptr(), _lib.TF_BF16 if trap.dtype == torch.bfloat16 else _lib.TF_F32,
+            qb.data_ptr(), kb.data_ptr(), angles.data_ptr(), d.data_ptr(), z.data_ptr(),
+            out.data_ptr(), _strides(q, k, v, adt, dt, trap, angles, z, out),
+            b, t, h, hq, None if qw is None else qw.data_ptr(),
+            None if kw is None else kw.data_ptr(), float(eps),
+            None if lengths is None else lengths.data_ptr(), stream))
+    return out

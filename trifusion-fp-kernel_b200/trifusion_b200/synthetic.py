@@ -1,0 +1,118 @@
+"""Seeded synthetic inputs for the fused Mamba-3 recurrence and its satellites.
+
+Two recipes exist:
+
+* ``"reftest"`` follows the reference's parity test generator
+  (``tests/test_recurrence.py:15-31``): q/k ``randn*0.2`` BF16 ``[B,T,1,128]``;
+  v, z and angles are strided views of one ``[B,T,H*128+32]`` BF16 buffer;
+  dt ~ U(0.01, 0.11); adt = -dt*U(0.2, 2.2); trap ~ N(0,1); qb, kb ~ N(1, 0.1);
+  d = 1.
+* ``"baseline"`` follows the benchmark configurations: q/k ~ N(0,1)/sqrt(128);
+  v, z ~ N(0,1); raw angles ~ U(-pi, pi) shared by all heads (head stride 0);
+  dt = exp(U(ln 1e-3, ln 1e-1)); A = -exp(U(ln 1, ln 16)) per head; adt = A*dt;
+  trap ~ N(0,1); D ~ N(0,1); qb, kb = 1 + N(0, 0.1).
+
+Everything is drawn on the CPU from one ``torch.Generator`` so the values are
+identical on every machine, then moved to ``device``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+STATE, HEAD, ROTARY = 128, 64, 32
+
+
+def recurrence_inputs(batch, time, heads, *, groups=1, kind="baseline", seed=None,
+                      distinct_angles=False, trap_dtype=torch.float32, strided=None,
+                      device="cpu"):
+    """Return the 11 ``fused_mamba`` arguments as a tuple, in reference order:
+    ``(q, k, v, adt, dt, trap, qb, kb, angles, d, z)``."""
+    if seed is None:
+        seed = 121 + time if kind == "reftest" else 0
+    if strided is None:
+        strided = kind == "reftest"
+    g = torch.Generator().manual_seed(seed)
+    b, t, h = batch, time, heads
+    bf = torch.bfloat16
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g)
+
+    def rand(*shape):
+        return torch.rand(*shape, generator=g)
+
+    if kind == "reftest":
+        q = (randn(b, t, groups, STATE).to(bf) * 0.2)
+        k = (randn(b, t, groups, STATE).to(bf) * 0.2)
+        raw_v = randn(b, t, h * HEAD).to(bf) * 0.2
+        raw_z = randn(b, t, h * HEAD).to(bf) * 0.2
+        raw_a = randn(b, t, (h if distinct_angles else 1) * ROTARY).to(bf) * 0.2
+        dt = rand(b, h, t) * 0.1 + 0.01
+        adt = -dt * (rand(b, h, t) * 2 + 0.2)
+        trap = randn(b, h, t)
+        qb = randn(h, STATE) * 0.1 + 1
+        kb = randn(h, STATE) * 0.1 + 1
+        d = torch.ones(h)
+    elif kind == "baseline":
+        q = (randn(b, t, groups, STATE) / math.sqrt(STATE)).to(bf)
+        k = (randn(b, t, groups, STATE) / math.sqrt(STATE)).to(bf)
+        raw_v = randn(b, t, h * HEAD).to(bf)
+        raw_z = randn(b, t, h * HEAD).to(bf)
+        raw_a = ((rand(b, t, (h if distinct_angles else 1) * ROTARY) * 2 - 1) * math.pi).to(bf)
+        dt = torch.exp(math.log(1e-3) + rand(b, h, t) * (math.log(1e-1) - math.log(1e-3)))
+        a_head = -torch.exp(rand(h) * math.log(16.0))
+        adt = a_head[None, :, None] * dt
+        trap = randn(b, h, t)
+        qb = 1 + 0.1 * randn(h, STATE)
+        kb = 1 + 0.1 * randn(h, STATE)
+        d = randn(h)
+    else:
+        raise ValueError(kind)
+    if trap_dtype != torch.float32:
+        trap = trap.to(trap_dtype)
+    ha = h if distinct_angles else 1
+    if strided:
+        # One packed projection row per token, like the reference test's buffer.
+        width = 2 * h * HEAD + ha * ROTARY
+        buf = torch.cat([raw_v, raw_z, raw_a], -1).reshape(b, t, width)
+        v = buf[:, :, : h * HEAD].reshape(b, t, h, HEAD)
+        z = buf[:, :, h * HEAD: 2 * h * HEAD].reshape(b, t, h, HEAD)
+        ang = buf[:, :, 2 * h * HEAD:].reshape(b, t, ha, ROTARY)
+    else:
+        v = raw_v.reshape(b, t, h, HEAD).contiguous()
+        z = raw_z.reshape(b, t, h, HEAD).contiguous()
+        ang = raw_a.reshape(b, t, ha, ROTARY).contiguous()
+    angles = ang if distinct_angles else ang.expand(b, t, h, ROTARY)
+    args = (q, k, v, adt, dt, trap, qb, kb, angles, d, z)
+    if device != "cpu":
+        args = tuple(_to_device(a, device) for a in args)
+    return args
+
+
+def _to_device(x, device):
+    """Move a (possibly strided / expanded) view to `device`, keeping its strides."""
+    if x.is_contiguous():
+        return x.to(device)
+    base = x
+    while base._base is not None:
+        base = base._base
+    # Re-create the same view on a device copy of the underlying storage.
+    storage = torch.empty(0, dtype=x.dtype)
+    storage.set_(x.untyped_storage())
+    dev = storage.to(device)
+    return dev.as_strided(x.shape, x.stride(), x.storage_offset())
+
+
+def lengths_uniform(batch, low, high, seed=0):
+    """Lengths ~ U{low..high} (int64), seeded."""
+    g = torch.Generator().manual_seed(seed + 7)
+    return torch.randint(low, high + 1, (batch,), generator=g, dtype=torch.int64)
+
+
+def norm_weight(width, seed=0):
+    """RMSNorm weights ~ 1 + N(0, 0.02) (benchmark configuration 1)."""
+    g = torch.Generator().manual_seed(seed + 11)
+    return 1 + 0.02 * torch.randn(width, generator=g)

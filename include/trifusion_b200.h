@@ -46,6 +46,11 @@ int tf_version(void);
 /* Last CUDA error string recorded by this thread (static storage). */
 const char* tf_last_cuda_error(void);
 
+/* Device-side error word of the current device: non-zero after a kernel's
+ * bounded wait on the tensor core gave up (the kernel then returns instead of
+ * hanging). Synchronous; `reset` != 0 clears it. */
+int tf_device_error(int reset);
+
 /* ------------------------------------------------------------------------
  * Fused Mamba-3 SISO recurrence — drop-in for
  *   trifusion_l4.mamba_fused.fused_mamba(q, k, v, adt, dt, trap, qb, kb,

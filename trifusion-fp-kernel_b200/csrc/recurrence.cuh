@@ -29,7 +29,13 @@ struct RecurrenceParams {
   int B, T, H, Hq;
 };
 
-// Launch the recurrence on `stream`; returns a tf_status code.
-int launch_recurrence(const RecurrenceParams& p, cudaStream_t stream);
+// Serial-chunk kernel (any T): one CTA per (batch, head). Returns 0 on success.
+int launch_recurrence_serial(const RecurrenceParams& p, cudaStream_t stream);
+// Chunk-parallel tensor-core kernel: one CTA per 64-step chunk, one cluster
+// per (batch, head); needs ceil(T/64) <= 8. Returns 0 on success.
+bool cluster_path_supported(const RecurrenceParams& p);
+int launch_recurrence_cluster(const RecurrenceParams& p, cudaStream_t stream);
+// Device error word set by kernels whose bounded waits gave up (synchronous read).
+int read_device_error(int reset);
 
 }  // namespace tf

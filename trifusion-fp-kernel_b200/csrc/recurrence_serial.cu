@@ -426,7 +426,7 @@ bool aligned4(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3u) 
 
 }  // namespace
 
-int launch_recurrence(const RecurrenceParams& p, cudaStream_t stream) {
+int launch_recurrence_serial(const RecurrenceParams& p, cudaStream_t stream) {
   // The vectorised path reads BF16 pairs as 32-bit words: every BF16 tensor
   // needs 4-byte aligned rows (even strides, aligned base).
   bool al = aligned4(p.q) && aligned4(p.k) && aligned4(p.v) && aligned4(p.z) && aligned4(p.out);

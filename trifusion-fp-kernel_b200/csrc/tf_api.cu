@@ -90,8 +90,12 @@ int recurrence_entry(const void* q, const void* k, const void* v, const float* a
   p.Hq = groups;
   int st = check_device();
   if (st != TF_OK) return st;
-  st = launch_recurrence(p, static_cast<cudaStream_t>(stream));
-  if (st != TF_OK) return st;
+  const cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  st = cluster_path_supported(p) ? launch_recurrence_cluster(p, cs) : launch_recurrence_serial(p, cs);
+  if (st != 0) {
+    const int ls = launch_status();
+    return ls != TF_OK ? ls : TF_ERR_LAUNCH;
+  }
   return launch_status();
 }
 
@@ -116,6 +120,8 @@ const char* tf_status_string(int status) {
 int tf_version(void) { return 100; }
 
 const char* tf_last_cuda_error(void) { return tf::g_last_error; }
+
+int tf_device_error(int reset) { return tf::read_device_error(reset); }
 
 int tf_fused_mamba_fwd(const void* q, const void* k, const void* v, const float* adt,
                        const float* dt, const void* trap, int trap_dtype, const float* qb,

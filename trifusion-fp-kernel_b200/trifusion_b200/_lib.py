@@ -25,6 +25,7 @@ SIGNATURES = {
     "tf_status_string": [_i],
     "tf_version": [],
     "tf_last_cuda_error": [],
+    "tf_device_error": [_i],
     "tf_fused_mamba_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
                            _i, _i, _i, _i, _p],
     "tf_mamba_recurrence_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,

@@ -6,10 +6,16 @@
  * Every entry point takes plain device pointers, element strides and sizes,
  * launches on the given CUDA stream (a `cudaStream_t` passed as `void*`; NULL
  * is the legacy default stream), never synchronises, never allocates device
- * memory, and returns a tf_status code. Calls are re-entrant: the library
- * keeps no mutable global state besides a per-device attribute cache filled
- * on first use, so the calls can be captured in CUDA graphs once each device
- * has seen one call.
+ * memory, and returns a tf_status code. The library keeps no mutable host
+ * state besides a per-device attribute cache filled on first use, so the calls
+ * can be captured in CUDA graphs once each device has seen one call.
+ *
+ * Workspace. The recurrence kernels exchange chunk states through a caller-
+ * owned device workspace (size from tf_recurrence_workspace_size). It must be
+ * zero-filled once before its first use and then passed back unchanged: the
+ * kernels leave it ready for the next launch themselves (launch-epoch tags, no
+ * clearing). Launches that share a workspace must not overlap in time; give
+ * each concurrently running stream its own workspace.
  *
  * Strides are in ELEMENTS, in the order of the reference tensor's dimensions.
  * BF16 tensors are raw 16-bit bfloat16 values.
@@ -17,6 +23,7 @@
 #ifndef TRIFUSION_B200_H
 #define TRIFUSION_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -51,6 +58,10 @@ const char* tf_last_cuda_error(void);
  * hanging). Synchronous; `reset` != 0 clears it. */
 int tf_device_error(int reset);
 
+/* Bytes of workspace the recurrence needs for [batch, seqlen, heads]
+ * (0 for an empty problem). */
+size_t tf_recurrence_workspace_size(int batch, int seqlen, int heads);
+
 /* ------------------------------------------------------------------------
  * Fused Mamba-3 SISO recurrence — drop-in for
  *   trifusion_l4.mamba_fused.fused_mamba(q, k, v, adt, dt, trap, qb, kb,
@@ -71,7 +82,7 @@ int tf_fused_mamba_fwd(const void* q, const void* k, const void* v,
                        const float* qb, const float* kb, const void* angles,
                        const float* d, const void* z, void* out,
                        const int64_t* strides, int batch, int seqlen, int heads,
-                       int groups, void* stream);
+                       int groups, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * The same recurrence with the work around it fused in (no counterpart as one
@@ -90,7 +101,8 @@ int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v,
                             const void* angles, const float* d, const void* z, void* out,
                             const int64_t* strides, int batch, int seqlen, int heads,
                             int groups, const float* q_norm_w, const float* k_norm_w,
-                            float eps, const int64_t* lengths, void* stream);
+                            float eps, const int64_t* lengths, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

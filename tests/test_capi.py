@@ -40,11 +40,14 @@ def test_invalid_arguments_rejected_without_a_device():
     lib = _lib.lib()
     strides = _lib.int64_array([0] * 33)
     # Null strides, bad dtype, groups not dividing heads: validated on the host.
-    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), None, 1, 1, 4, 1, None) == _lib.TF_ERR_ARG
-    assert lib.tf_fused_mamba_fwd(*([None] * 6), 7, *([None] * 6), strides, 1, 1, 4, 1, None) == _lib.TF_ERR_ARG
-    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), strides, 1, 1, 4, 3, None) == _lib.TF_ERR_ARG
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), None, 1, 1, 4, 1, None, 0, None) == _lib.TF_ERR_ARG
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 7, *([None] * 6), strides, 1, 1, 4, 1, None, 0, None) == _lib.TF_ERR_ARG
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), strides, 1, 1, 4, 3, None, 0, None) == _lib.TF_ERR_ARG
     # Empty problems are a no-op success.
-    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), strides, 0, 5, 4, 1, None) == _lib.TF_OK
+    assert lib.tf_fused_mamba_fwd(*([None] * 6), 0, *([None] * 6), strides, 0, 5, 4, 1, None, 0, None) == _lib.TF_OK
+    # Workspace size query: grows with the number of 64-step chunk units.
+    assert lib.tf_recurrence_workspace_size(0, 5, 4) == 0
+    assert lib.tf_recurrence_workspace_size(16, 200, 12) > lib.tf_recurrence_workspace_size(16, 64, 12) > 0
     with pytest.raises(ValueError):
         _lib.check(_lib.TF_ERR_ARG)
     with pytest.raises(RuntimeError):

@@ -29,13 +29,13 @@ struct RecurrenceParams {
   int B, T, H, Hq;
 };
 
-// Serial-chunk kernel (any T): one CTA per (batch, head). Returns 0 on success.
-int launch_recurrence_serial(const RecurrenceParams& p, cudaStream_t stream);
-// Chunk-parallel tensor-core kernel: one CTA per 64-step chunk, one cluster
-// per (batch, head); needs ceil(T/64) <= 8. Returns 0 on success.
-bool cluster_path_supported(const RecurrenceParams& p);
-int launch_recurrence_cluster(const RecurrenceParams& p, cudaStream_t stream);
-// Device error word set by kernels whose bounded waits gave up (synchronous read).
+// Persistent chunk-parallel tensor-core kernel (any T). `workspace` must hold
+// recurrence_workspace_bytes(B, T, H) bytes, zero-filled before its first use
+// and then reused unchanged. Returns 0 on success.
+size_t recurrence_workspace_bytes(int B, int T, int H);
+int launch_recurrence_persistent(const RecurrenceParams& p, void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream);
+// Device error word set when a kernel's bounded wait gave up (synchronous read).
 int read_device_error(int reset);
 
 }  // namespace tf

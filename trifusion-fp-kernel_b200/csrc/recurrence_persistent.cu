@@ -1,0 +1,1025 @@
+// Fused Mamba-3 SISO recurrence on the sm_100 tensor cores: persistent,
+// chunk-parallel, warp-specialised.
+//
+// Work units. A unit is one 64-step chunk c of one (batch b, head h) row. Units
+// are numbered chunk-major, u = (c*B + b)*H + h, and handed out in increasing
+// order by an atomic ticket, so a unit only ever depends on units already held
+// by running CTAs: the kernel cannot deadlock, whether or not every CTA of the
+// grid is resident.
+//
+// Chunk-local frames. Each unit rotates q and k by the phase accumulated from
+// its own chunk start, so its scores and its state contribution
+//   dS_c^T = kr_c^T (v_c * scale * 2^(total_c - cs))              (n x p)
+// need nothing from earlier chunks. Because q and k of a pair rotate by the
+// same angle, the state entering chunk c, in chunk c's frame, is
+//   S(0) = 0,   S(x+1) = R(-theta_x) (2^total_x S(x) + dS_x),
+// with theta_x chunk x's summed angle increment and R the rotation of the
+// first 32 (even, odd) pairs of the state's n axis. In real arithmetic this is
+// the reference's serial recurrence (mamba_fused.py:93-152).
+//
+// Exchange through L2. After its first MMAs a unit publishes dS_c (FP16 with a
+// power-of-two exponent per half row), theta_c and 2^total_c in the workspace
+// and raises its flag. A later unit folds its predecessors' contributions.
+// For long rows (more than 8 chunks) every unit also publishes its outgoing
+// state S(c+1) (FP32) once known, and a successor looks back only to the
+// nearest predecessor whose outgoing state is available (decoupled look-back).
+// Flags carry a launch epoch, so the workspace needs no clearing between
+// launches; the last CTA to finish advances the epoch and resets the ticket.
+//
+// Roles inside a CTA (512 threads, one CTA per SM, two pipeline slots):
+//   warps 0-7   producer: ticket, loads, controls, phases, FP16 operand tiles,
+//               then the scores / state MMAs (MMA 1);
+//   warps 8-15  epilogue (two warps per TMEM lane quarter, one per 32-column
+//               half): export dS, decayed scores -> P tiles, MMA 2 (P v),
+//               fold -> S tile, MMA 3 (q S^T), gated output, release the slot.
+//
+// Tensor-core work per unit (tcgen05.mma kind::f16, FP16 operands in
+// 128B-swizzled shared memory, FP32 accumulators in tensor memory):
+//   scores  D_s  = q16 k16^T              M=64  N=64 K=128
+//   state   D_d  = k16^T (vs_hi + vs_lo)  M=128 N=64 K=64 x2  (k16 read MN-major)
+//   values  D_pv = (P_hi + P_lo) v16      M=64  N=64 K=64 x2
+//   inter   D_i  = q16 S^T                M=64  N=64 K=128
+// Precision: FP16 operands carry per-row power-of-two exponents (undone exactly
+// after the MMA); the decayed scores P and the decay-weighted values vs are
+// split into FP16 hi + lo halves; sums accumulate in FP32. qk (the D-skip dot
+// product, mamba_fused.py:124) is the score diagonal, since rotating q and k by
+// the same angle preserves their dot product; (D + qk) v rides on P's diagonal.
+#include "recurrence.cuh"
+#include "sm100.cuh"
+
+namespace tf {
+namespace {
+
+using namespace sm100;
+
+constexpr int kThreads = 512;
+constexpr int kProducerThreads = 256;  // warps 0-7
+constexpr int kEpilogueThreads = 256;  // warps 8-15
+constexpr int kBarProducer = 1, kBarEpilogue = 2, kBarPair = 3;  // kBarPair + quarter: 3..6
+constexpr int kLookbackChunks = 8;     // rows with more chunks publish outgoing states
+
+// ---- shared memory --------------------------------------------------------------
+// Per slot (bytes from the slot base, 1024-aligned).
+constexpr uint32_t kSlotQ = 0;        // q16  K-major  [2 K-blocks][64 rows][128 B]
+constexpr uint32_t kSlotK = 16384;    // k16  K-major  [2 K-blocks][64 rows][128 B]
+constexpr uint32_t kSlotV = 32768;    // v16  MN-major [64 rows][128 B]
+constexpr uint32_t kSlotVH = 40960;   // vs hi MN-major
+constexpr uint32_t kSlotVL = 49152;   // vs lo MN-major
+constexpr uint32_t kSlotPH = 57344;   // P hi K-major [64 rows][128 B]
+constexpr uint32_t kSlotPL = 65536;   // P lo
+constexpr uint32_t kSlotS = 73728;    // S^T MN-major [128 rows][128 B]
+constexpr uint32_t kSlotZ = 90112;    // z in / out staging, BF16 [64 rows][128 B]
+constexpr uint32_t kSlotBytes = 98304;
+// Producer scratch and barriers after the two slots.
+constexpr uint32_t kOffPhase = 2 * kSlotBytes;        // FP32 [64][33]
+constexpr uint32_t kOffMisc = kOffPhase + 64 * 33 * 4;
+
+struct SlotHeader {
+  int unit;  // -1: no more work
+  int b, h, c, nv;
+  float cs[kChunk];     // decay cumsum (log2 units)
+  float gamma[kChunk];
+  float qe[kChunk];     // q16 row exponents
+  float ke[kChunk];     // k16 row exponents
+  float kcoef[kChunk];  // scale_j * 2^-ke_j
+  float pe[kChunk];     // P row exponents (epilogue)
+  float pmax[2][kChunk];  // per column half (epilogue)
+  float theta[kRotary];
+  float gtot;
+  float sinv;           // 2^-(state tile exponent) (epilogue)
+};
+struct Misc {
+  SlotHeader hdr[2];
+  float scale[kChunk];  // producer scratch
+  float dtc[kChunk];
+  float seg[8][kRotary];
+  float wsum[2];
+  float ered[8];        // epilogue reductions
+  int ticket;
+  int next_ticket;
+  int lookback_start;
+  uint32_t epoch;
+  uint32_t tmem_base;
+  uint64_t ready[2], freed[2], mma1[2], mma2[2], mma3[2];
+};
+constexpr uint32_t kSmemBytes = kOffMisc + sizeof(Misc) + 1024;
+
+constexpr uint32_t kColS = 0, kColD = 64, kColPV = 128, kColI = 192, kSlotCols = 256, kTmemCols = 512;
+
+constexpr uint32_t kIdScore = idesc_f16_f32(64, 64, false, false);
+constexpr uint32_t kIdState = idesc_f16_f32(128, 64, true, true);
+constexpr uint32_t kIdPV = idesc_f16_f32(64, 64, false, true);
+constexpr uint32_t kIdInter = idesc_f16_f32(64, 64, false, true);
+
+// ---- workspace ------------------------------------------------------------------
+// [header: epoch | ticket | done, each on its own 128-byte line]
+// per unit: [flag (128 B line)] [theta 32 + gtot (256 B)] [half-row exponent
+// factors 2x128 FP32 (1 KB)] [dS^T FP16 128x64 (16 KB)] [S(c+1)^T FP32 128x64 (32 KB)]
+constexpr size_t kWsHeader = 384;
+constexpr size_t kUnitFlag = 0, kUnitTheta = 128, kUnitExp = 384, kUnitAgg = 1408, kUnitIncl = 1408 + 16384;
+constexpr size_t kUnitBytes = kUnitIncl + 32768;
+constexpr uint32_t kFlagAgg = 1, kFlagIncl = 2, kEpochStep = 2;
+
+// ---- helpers --------------------------------------------------------------------
+template <int kVec>
+__device__ __forceinline__ uint4 load16(const bf16* p) {
+  if constexpr (kVec == 16) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+  } else if constexpr (kVec == 8) {
+    const uint2 a = __ldg(reinterpret_cast<const uint2*>(p));
+    const uint2 b = __ldg(reinterpret_cast<const uint2*>(p + 4));
+    return make_uint4(a.x, a.y, b.x, b.y);
+  } else {
+    const unsigned short* s = reinterpret_cast<const unsigned short*>(p);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = static_cast<uint32_t>(s[2 * i]) | (static_cast<uint32_t>(s[2 * i + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+template <int kVec>
+__device__ __forceinline__ void store16(bf16* p, uint4 v) {
+  if constexpr (kVec == 16) {
+    *reinterpret_cast<uint4*>(p) = v;
+  } else if constexpr (kVec == 8) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(v.x, v.y);
+    *reinterpret_cast<uint2*>(p + 4) = make_uint2(v.z, v.w);
+  } else {
+    unsigned short* s = reinterpret_cast<unsigned short*>(p);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      s[2 * i] = static_cast<unsigned short>(w[i] & 0xffffu);
+      s[2 * i + 1] = static_cast<unsigned short>(w[i] >> 16);
+    }
+  }
+}
+__device__ __forceinline__ void unpack8(uint4 u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = unpack_bf16x2(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t a) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(a) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+// 16 TMEM lanes x 32 columns in the m16n8 fragment order: thread t gets lanes
+// t/4 and t/4+8, columns 8k + 2(t%4) + {0,1} (k = 0..3) as r[4k+0..1] (lane
+// t/4) and r[4k+2..3] (lane t/4+8).
+__device__ __forceinline__ void tmem_ld_16x256_x4(uint32_t taddr, float (&r)[16]) {
+  uint32_t* u = reinterpret_cast<uint32_t*>(r);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+        "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void bar_sync_n(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ float load_trap(const RecurrenceParams& p, const char* base, int64_t off) {
+  return p.trap_bf16 ? bf2f(reinterpret_cast<const bf16*>(base)[off]) : reinterpret_cast<const float*>(base)[off];
+}
+__device__ __forceinline__ int ilog2_or(float max_abs, int if_zero) {
+  if (!(max_abs > 0.f)) return if_zero;
+  return static_cast<int>((__float_as_uint(max_abs) >> 23) & 0xffu) - 127;
+}
+__device__ __forceinline__ float silu_tanh(float z) {
+  const float hz = 0.5f * z;
+  return fmaf(hz, tanh_approx(hz), hz);  // z * sigmoid(z) = hz (1 + tanh(hz))
+}
+
+__device__ int g_device_error = 0;  // set when a bounded wait gives up
+
+struct Shape {
+  int B, H, nck, units;
+};
+__device__ __forceinline__ void decode_unit(int u, const Shape& s, int& b, int& h, int& c) {
+  h = u % s.H;
+  const int rest = u / s.H;
+  b = rest % s.B;
+  c = rest / s.B;
+}
+__device__ __forceinline__ unsigned char* unit_ws(unsigned char* ws, int u) {
+  return ws + kWsHeader + static_cast<size_t>(u) * kUnitBytes;
+}
+// Spin (bounded in time) until a unit's flag reaches `want` in this launch's epoch.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, uint32_t want, uint32_t& seen) {
+  seen = ld_acquire_u32(flag);
+  if (static_cast<int>(seen - epoch) >= static_cast<int>(want)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    __nanosleep(64);
+    seen = ld_acquire_u32(flag);
+    if (static_cast<int>(seen - epoch) >= static_cast<int>(want)) return true;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+}
+
+// =====================================================================================
+template <int kVec>
+__global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(RecurrenceParams p,
+                                                                              unsigned char* ws) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  unsigned char* smem = smem_raw + (base - raw_addr);
+  Misc& mi = *reinterpret_cast<Misc*>(smem + kOffMisc);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint32_t* ws_epoch = reinterpret_cast<uint32_t*>(ws);
+  int* ws_ticket = reinterpret_cast<int*>(ws + 128);
+  int* ws_done = reinterpret_cast<int*>(ws + 256);
+  const Shape shp{p.B, p.H, (p.T + kChunk - 1) / kChunk, ((p.T + kChunk - 1) / kChunk) * p.B * p.H};
+  const bool lookback = shp.nck > kLookbackChunks;
+
+  if (warp == 0) {
+    tmem_alloc(&mi.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&mi.ready[s], 1);
+      mbar_init(&mi.freed[s], 1);
+      mbar_init(&mi.mma1[s], 1);
+      mbar_init(&mi.mma2[s], 1);
+      mbar_init(&mi.mma3[s], 1);
+    }
+    fence_mbar_init();
+    mi.epoch = ld_acquire_u32(ws_epoch);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem0 = mi.tmem_base;
+  const uint32_t epoch = mi.epoch;
+  bool ok = true;
+
+  if (warp < 8) {
+    // =========================== producer ===========================
+    const int t = tid >> 2, s4 = tid & 3;  // row, sub-slot (4 threads per row)
+    int k = 0;                             // slot uses so far
+    if (tid == 0) mi.next_ticket = atomicAdd(ws_ticket, 1);
+    for (;;) {
+      bar_sync_n(kBarProducer, kProducerThreads);
+      const int u = mi.next_ticket;
+      bar_sync_n(kBarProducer, kProducerThreads);  // everyone has read the ticket
+      // Request the following unit now; the atomic stays in flight while this
+      // unit is prepared and its result is stored only at the end.
+      int my_next = 0;
+      if (tid == 0 && u < shp.units) my_next = atomicAdd(ws_ticket, 1);
+      const int slot = k & 1;
+      SlotHeader& hd = mi.hdr[slot];
+      if (u >= shp.units) {
+        // Tell the epilogue there is no more work, through the next slot.
+        if (k >= 2) ok &= mbar_wait(&mi.freed[slot], ((k >> 1) - 1) & 1);
+        if (tid == 0) {
+          hd.unit = -1;
+          mbar_arrive(&mi.ready[slot]);
+        }
+        break;
+      }
+      int b, h, c;
+      decode_unit(u, shp, b, h, c);
+      int T_eff = p.T;
+      if (p.lengths) {
+        const int64_t len = p.lengths[b];
+        T_eff = static_cast<int>(len < 0 ? 0 : (len > p.T ? p.T : len));
+      }
+      const int c0 = c * kChunk;
+      const int nv = max(0, min(kChunk, T_eff - c0));
+      if (nv == 0) {
+        // Whole chunk past the length: zero rows, no tensor work, no slot.
+        // (Every later chunk of this row is empty too, so nobody reads its state.)
+        if (c0 + t < p.T) {
+          bf16* orow = p.out + b * p.so[0] + static_cast<int64_t>(c0 + t) * p.so[1] + h * p.so[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) store16<kVec>(orow + 32 * i + 8 * s4, make_uint4(0, 0, 0, 0));
+        }
+        if (tid == 0) mi.next_ticket = my_next;
+        continue;
+      }
+      const bool row_ok = t < nv;
+      // ---- loads ------------------------------------------------------------------
+      uint4 qraw[4], kraw[4], vraw[2], zraw[2];
+      {
+        const int64_t pos = c0 + t;
+        const bf16* qrow = p.q + b * p.sq[0] + pos * p.sq[1] + (h / (p.H / p.Hq)) * p.sq[2];
+        const bf16* krow = p.k + b * p.sk[0] + pos * p.sk[1] + (h / (p.H / p.Hq)) * p.sk[2];
+        const bf16* vrow = p.v + b * p.sv[0] + pos * p.sv[1] + h * p.sv[2];
+        const bf16* zrow = p.z + b * p.sz[0] + pos * p.sz[1] + h * p.sz[2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int e = 32 * i + 8 * s4;
+          qraw[i] = row_ok ? load16<kVec>(qrow + e) : make_uint4(0, 0, 0, 0);
+          kraw[i] = row_ok ? load16<kVec>(krow + e) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int e = 32 * i + 8 * s4;
+          vraw[i] = row_ok ? load16<kVec>(vrow + e) : make_uint4(0, 0, 0, 0);
+          zraw[i] = row_ok ? load16<kVec>(zrow + e) : make_uint4(0, 0, 0, 0);
+        }
+      }
+      float c_dt = 0.f, c_dn = 0.f, c_tr = 0.f, c_tn = 0.f, c_adt = 0.f;
+      if (tid < kChunk) {
+        const float* dtbase = p.dt + b * p.sdt[0] + h * p.sdt[1];
+        const float* adtbase = p.adt + b * p.sadt[0] + h * p.sadt[1];
+        const char* trbase =
+            static_cast<const char*>(p.trap) + (b * p.str[0] + h * p.str[1]) * (p.trap_bf16 ? 2 : 4);
+        const int64_t tt = c0 + tid;
+        if (tid < nv) {
+          c_dt = dtbase[tt * p.sdt[2]];
+          c_tr = load_trap(p, trbase, tt * p.str[2]);
+          c_adt = adtbase[tt * p.sadt[2]];
+        }
+        if (tt + 1 < T_eff) {
+          c_dn = dtbase[(tt + 1) * p.sdt[2]];
+          c_tn = load_trap(p, trbase, (tt + 1) * p.str[2]);
+        }
+      }
+      float araw[8];
+      {
+        const bf16* abase = p.ang + b * p.sa[0] + h * p.sa[2];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int tt = warp * 8 + i;
+          araw[i] = tt < nv ? bf2f(abase[static_cast<int64_t>(c0 + tt) * p.sa[1] + lane * p.sa[3]]) : 0.f;
+        }
+      }
+      // The slot's previous unit must be fully retired before it is rewritten.
+      if (k >= 2) ok &= mbar_wait(&mi.freed[slot], ((k >> 1) - 1) & 1);
+      const uint32_t sb = base + slot * kSlotBytes;
+      // ---- controls and the decay cumsum ----------------------------------------
+      if (tid < kChunk) {
+        const float gm = c_dt * sigmoidf_fast(c_tr);
+        float x = c_adt * kLog2e;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        if (lane == 31) mi.wsum[warp] = x;
+        mi.dtc[tid] = c_dt;
+        hd.gamma[tid] = gm;
+        mi.scale[tid] = c_dn * (1.f - sigmoidf_fast(c_tn)) + gm;
+        hd.cs[tid] = x;
+      }
+      bar_sync_n(kBarProducer, kProducerThreads);
+      if (tid >= 32 && tid < kChunk) hd.cs[tid] += mi.wsum[0];
+      // ---- local angle phases: lane = pair r, warp = 8-step segment ------------
+      float* phase = reinterpret_cast<float*>(smem + kOffPhase);
+      {
+        float run = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int tt = warp * 8 + i;
+          run = fmaf(tanh_approx(araw[i]) * kPi, mi.dtc[tt], run);
+          phase[tt * 33 + lane] = run;
+        }
+        mi.seg[warp][lane] = run;
+      }
+      bar_sync_n(kBarProducer, kProducerThreads);
+      {
+        float off = 0.f;
+        for (int q = 0; q < warp; ++q) off += mi.seg[q][lane];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float ph = phase[(warp * 8 + i) * 33 + lane] + off;
+          phase[(warp * 8 + i) * 33 + lane] = ph - kTwoPi * floorf(ph * (1.f / kTwoPi));
+        }
+        if (warp == 0) {
+          float th = 0.f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) th += mi.seg[q][lane];
+          hd.theta[lane] = th - kTwoPi * floorf(th * (1.f / kTwoPi));
+        }
+      }
+      bar_sync_n(kBarProducer, kProducerThreads);
+      const float total = hd.cs[kChunk - 1];
+      // ---- rows -> FP16 operand tiles (q, k, v, vs hi/lo) and the z tile -------
+      {
+        const float* qbh = p.qb + h * kState;
+        const float* kbh = p.kb + h * kState;
+        float cn[8], sn[8];  // this thread's 8 rotating pairs: 4s..4s+3, 16+4s..16+4s+3
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+          __sincosf(phase[t * 33 + (m < 4 ? 4 * s4 + m : 12 + 4 * s4 + m)], &sn[m], &cn[m]);
+        float x[32];
+        // q: optional C_norm, bias, rotation, row exponent.
+#pragma unroll
+        for (int i = 0; i < 4; ++i) unpack8(qraw[i], &x[8 * i]);
+        if (p.qw) {  // RMSNorm, FP32 statistics, BF16 result (native.py:8-39)
+          float ss = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ss = fmaf(x[e], x[e], ss);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+          const float rr = rsqrtf(ss * (1.f / kState) + p.eps);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[8 * i + e] = bf16_round((x[8 * i + e] * rr) * p.qw[32 * i + 8 * s4 + e]);
+        }
+        float qmax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          {
+            const float4 b0 = __ldg(reinterpret_cast<const float4*>(qbh + 32 * i + 8 * s4));
+            const float4 b1 = __ldg(reinterpret_cast<const float4*>(qbh + 32 * i + 8 * s4 + 4));
+            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[8 * i + e] = row_ok ? x[8 * i + e] + bb[e] : 0.f;
+          }
+          if (i < 2) {
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              const float a0 = x[8 * i + 2 * m], a1 = x[8 * i + 2 * m + 1];
+              const float cc = cn[4 * i + m], ssn = sn[4 * i + m];
+              x[8 * i + 2 * m] = a0 * cc - a1 * ssn;
+              x[8 * i + 2 * m + 1] = a0 * ssn + a1 * cc;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qmax = fmaxf(qmax, fabsf(x[8 * i + e]));
+        }
+        qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
+        qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));
+        const int qe = pow2_scale_exponent(qmax);
+        {
+          const float qs = exp2i(qe);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e0 = 32 * i + 8 * s4;
+            st_shared_v4(sb + kSlotQ + (e0 >> 6) * 8192u + sw128_offset(t, e0 & 63),
+                         pack_f16x2(x[8 * i] * qs, x[8 * i + 1] * qs), pack_f16x2(x[8 * i + 2] * qs, x[8 * i + 3] * qs),
+                         pack_f16x2(x[8 * i + 4] * qs, x[8 * i + 5] * qs),
+                         pack_f16x2(x[8 * i + 6] * qs, x[8 * i + 7] * qs));
+          }
+        }
+        // k: optional B_norm, bias, rotation.
+#pragma unroll
+        for (int i = 0; i < 4; ++i) unpack8(kraw[i], &x[8 * i]);
+        if (p.kw) {
+          float ss = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ss = fmaf(x[e], x[e], ss);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+          const float rr = rsqrtf(ss * (1.f / kState) + p.eps);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[8 * i + e] = bf16_round((x[8 * i + e] * rr) * p.kw[32 * i + 8 * s4 + e]);
+        }
+        float kmax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          {
+            const float4 b0 = __ldg(reinterpret_cast<const float4*>(kbh + 32 * i + 8 * s4));
+            const float4 b1 = __ldg(reinterpret_cast<const float4*>(kbh + 32 * i + 8 * s4 + 4));
+            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[8 * i + e] = row_ok ? x[8 * i + e] + bb[e] : 0.f;
+          }
+          if (i < 2) {
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              const float a0 = x[8 * i + 2 * m], a1 = x[8 * i + 2 * m + 1];
+              const float cc = cn[4 * i + m], ssn = sn[4 * i + m];
+              x[8 * i + 2 * m] = a0 * cc - a1 * ssn;
+              x[8 * i + 2 * m + 1] = a0 * ssn + a1 * cc;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) kmax = fmaxf(kmax, fabsf(x[8 * i + e]));
+        }
+        kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, 1));
+        kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, 2));
+        float vf[16];
+        unpack8(vraw[0], &vf[0]);
+        unpack8(vraw[1], &vf[8]);
+        float vmax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) vmax = fmaxf(vmax, fabsf(vf[e]));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+        const float sc = mi.scale[t];
+        const float sw = row_ok ? sc * ex2_approx(total - hd.cs[t]) : 0.f;
+        // Split 2^ka between k16 = kr 2^ka (also the score operand) and
+        // vs = v scale w 2^-ka near the geometric mean of their magnitudes, but
+        // keep the k16 row maximum >= 2^-6 so the scores keep FP16's full
+        // precision; a vs row pushed below that carries a negligible state
+        // contribution. Both stay below 2^15.
+        const int kl = ilog2_or(kmax, 1000), vl = ilog2_or(vmax * sw, 1000);
+        int ka = 0;
+        if (kl != 1000) {
+          ka = vl != 1000 ? ((vl - kl) >> 1) : 14 - kl;
+          ka = max(ka, -6 - kl);
+          if (vl != 1000) ka = max(ka, vl - 14);
+          ka = min(ka, 14 - kl);
+          ka = ka < -60 ? -60 : (ka > 60 ? 60 : ka);
+        }
+        {
+          const float ks = exp2i(ka);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e0 = 32 * i + 8 * s4;
+            st_shared_v4(sb + kSlotK + (e0 >> 6) * 8192u + sw128_offset(t, e0 & 63),
+                         pack_f16x2(x[8 * i] * ks, x[8 * i + 1] * ks), pack_f16x2(x[8 * i + 2] * ks, x[8 * i + 3] * ks),
+                         pack_f16x2(x[8 * i + 4] * ks, x[8 * i + 5] * ks),
+                         pack_f16x2(x[8 * i + 6] * ks, x[8 * i + 7] * ks));
+          }
+          const float vsc = sw * exp2i(-ka);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint32_t off = sw128_offset(t, 32 * i + 8 * s4);
+            uint32_t hv[4], hh[4], hl[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              const float a0 = vf[8 * i + 2 * m], a1 = vf[8 * i + 2 * m + 1];
+              hv[m] = pack_f16x2(a0, a1);
+              const float w0 = a0 * vsc, w1 = a1 * vsc;
+              hh[m] = pack_f16x2(w0, w1);
+              const float2 back = unpack_f16x2(hh[m]);
+              hl[m] = pack_f16x2(w0 - back.x, w1 - back.y);
+            }
+            st_shared_v4(sb + kSlotV + off, hv[0], hv[1], hv[2], hv[3]);
+            st_shared_v4(sb + kSlotVH + off, hh[0], hh[1], hh[2], hh[3]);
+            st_shared_v4(sb + kSlotVL + off, hl[0], hl[1], hl[2], hl[3]);
+            st_shared_v4(sb + kSlotZ + off, zraw[i].x, zraw[i].y, zraw[i].z, zraw[i].w);
+          }
+        }
+        if (s4 == 0) {
+          hd.qe[t] = static_cast<float>(qe);
+          hd.ke[t] = static_cast<float>(ka);
+          hd.kcoef[t] = sc * exp2i(-ka);
+        }
+      }
+      if (tid == 0) {
+        hd.unit = u;
+        hd.b = b;
+        hd.h = h;
+        hd.c = c;
+        hd.nv = nv;
+        hd.gtot = ex2_approx(total);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      bar_sync_n(kBarProducer, kProducerThreads);
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t tm = tmem0 + slot * kSlotCols;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t koff = (kk >> 2) * 8192u + (kk & 3) * 32u;
+          umma_f16(tm + kColS, desc_sw128(sb + kSlotQ + koff, 0, 1024), desc_sw128(sb + kSlotK + koff, 0, 1024),
+                   kIdScore, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tm + kColD, desc_sw128(sb + kSlotK + kk * 2048u, 8192, 1024),
+                   desc_sw128(sb + kSlotVH + kk * 2048u, 8192, 1024), kIdState, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tm + kColD, desc_sw128(sb + kSlotK + kk * 2048u, 8192, 1024),
+                   desc_sw128(sb + kSlotVL + kk * 2048u, 8192, 1024), kIdState, 1);
+        umma_commit(&mi.mma1[slot]);
+        mbar_arrive(&mi.ready[slot]);
+        mi.next_ticket = my_next;
+      }
+      ++k;
+    }
+  } else {
+    // =========================== epilogue ===========================
+    const int et = tid - kProducerThreads;  // 0..255
+    const int q4 = warp & 3;                // TMEM lane quarter
+    const int chalf = (warp - 8) >> 2;      // 32-column half
+    const int g = lane >> 2, c4 = lane & 3;
+    const int i0 = 16 * q4 + g, i1 = i0 + 8;   // rows of the M=64 accumulators
+    const uint32_t n = 32 * q4 + lane;          // row of the M=128 accumulator / state
+    for (int k = 0;; ++k) {
+      const int slot = k & 1;
+      const uint32_t ph = (k >> 1) & 1;
+      SlotHeader& hd = mi.hdr[slot];
+      ok &= mbar_wait(&mi.ready[slot], ph);
+      const int u = hd.unit;
+      if (u < 0) break;
+      const int b = hd.b, h = hd.h, c = hd.c;
+      const uint32_t sb = base + slot * kSlotBytes;
+      const uint32_t tm = tmem0 + slot * kSlotCols;
+      unsigned char* uws = unit_ws(ws, u);
+      ok &= mbar_wait(&mi.mma1[slot], ph);
+      tc_fence_after();
+      // ---- export dS^T (row n, this thread's 32-column half) -----------------------
+      {
+        float r[32];
+        tmem_ld16(tmem_addr(tm, 32 * q4, kColD + 32 * chalf), *reinterpret_cast<float(*)[16]>(&r[0]));
+        tmem_ld16(tmem_addr(tm, 32 * q4, kColD + 32 * chalf + 16), *reinterpret_cast<float(*)[16]>(&r[16]));
+        tmem_wait_ld();
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(r[j]));
+        const int ae = pow2_scale_exponent(m);
+        const float as = exp2i(ae);
+        __half* agg = reinterpret_cast<__half*>(uws + kUnitAgg) + n * 64 + 32 * chalf;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float* rr = &r[8 * q];
+          *reinterpret_cast<uint4*>(agg + 8 * q) =
+              make_uint4(pack_f16x2(rr[0] * as, rr[1] * as), pack_f16x2(rr[2] * as, rr[3] * as),
+                         pack_f16x2(rr[4] * as, rr[5] * as), pack_f16x2(rr[6] * as, rr[7] * as));
+        }
+        reinterpret_cast<float*>(uws + kUnitExp)[128 * chalf + n] = exp2i(-ae);
+        if (et < kRotary) reinterpret_cast<float*>(uws + kUnitTheta)[et] = hd.theta[et];
+        if (et == 0) reinterpret_cast<float*>(uws + kUnitTheta)[kRotary] = hd.gtot;
+      }
+      // ---- decayed scores P (+ the D-skip diagonal) -> FP16 hi/lo tiles ---------
+      {
+        float sc[16];
+        tmem_ld_16x256_x4(tmem_addr(tm, 32 * q4, kColS + 32 * chalf), sc);
+        tmem_wait_ld();
+        const float d = p.d[h];
+        const float rq0 = hd.cs[i0] - hd.qe[i0], rq1 = hd.cs[i1] - hd.qe[i1];
+        const float dg0 = exp2i(-static_cast<int>(hd.qe[i0]) - static_cast<int>(hd.ke[i0])) * hd.gamma[i0];
+        const float dg1 = exp2i(-static_cast<int>(hd.qe[i1]) - static_cast<int>(hd.ke[i1])) * hd.gamma[i1];
+        float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = 32 * chalf + 8 * kk + 2 * c4 + e;
+            const float kc = hd.kcoef[j], csj = hd.cs[j];
+            float v0 = sc[4 * kk + e], v1 = sc[4 * kk + 2 + e];
+            v0 = j < i0 ? v0 * kc * ex2_approx(rq0 - csj) : (j == i0 ? d + v0 * dg0 : 0.f);
+            v1 = j < i1 ? v1 * kc * ex2_approx(rq1 - csj) : (j == i1 ? d + v1 * dg1 : 0.f);
+            sc[4 * kk + e] = v0;
+            sc[4 * kk + 2 + e] = v1;
+            m0 = fmaxf(m0, fabsf(v0));
+            m1 = fmaxf(m1, fabsf(v1));
+          }
+        }
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+        if (c4 == 0) {
+          hd.pmax[chalf][i0] = m0;
+          hd.pmax[chalf][i1] = m1;
+        }
+        bar_sync_n(kBarPair + q4, 64);  // the two warps sharing this TMEM quarter
+        m0 = fmaxf(hd.pmax[0][i0], hd.pmax[1][i0]);
+        m1 = fmaxf(hd.pmax[0][i1], hd.pmax[1][i1]);
+        const int pe0 = pow2_scale_exponent(m0), pe1 = pow2_scale_exponent(m1);
+        if (chalf == 0 && c4 == 0) {
+          hd.pe[i0] = static_cast<float>(pe0);
+          hd.pe[i1] = static_cast<float>(pe1);
+        }
+        const float ps0 = exp2i(pe0), ps1 = exp2i(pe1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int j = 32 * chalf + 8 * kk + 2 * c4;
+          const float a0 = sc[4 * kk] * ps0, a1 = sc[4 * kk + 1] * ps0;
+          const float b0 = sc[4 * kk + 2] * ps1, b1 = sc[4 * kk + 3] * ps1;
+          const uint32_t h0 = pack_f16x2(a0, a1), h1 = pack_f16x2(b0, b1);
+          const float2 f0 = unpack_f16x2(h0), f1 = unpack_f16x2(h1);
+          st_shared_u32(sb + kSlotPH + sw128_offset(i0, j), h0);
+          st_shared_u32(sb + kSlotPH + sw128_offset(i1, j), h1);
+          st_shared_u32(sb + kSlotPL + sw128_offset(i0, j), pack_f16x2(a0 - f0.x, a1 - f0.y));
+          st_shared_u32(sb + kSlotPL + sw128_offset(i1, j), pack_f16x2(b0 - f1.x, b1 - f1.y));
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __threadfence();  // the dS export has drained meanwhile; make it visible
+      bar_sync_n(kBarEpilogue, kEpilogueThreads);
+      if (et == 0) {
+        st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tm + kColPV, desc_sw128(sb + kSlotPH + kk * 32u, 0, 1024),
+                   desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tm + kColPV, desc_sw128(sb + kSlotPL + kk * 32u, 0, 1024),
+                   desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, 1);
+        umma_commit(&mi.mma2[slot]);
+      }
+      // ---- fold the predecessors' state contributions (row n, 32-column half) ---
+      // One step: st = R(-theta) (g st + dS), dS from a published unit.
+      auto fold_step = [&](float (&st)[32], const uint4 (&w)[4], float f, float gx, float th) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t ww[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
+#pragma unroll
+          for (int mm = 0; mm < 4; ++mm) {
+            const float2 v = unpack_f16x2(ww[mm]);
+            st[8 * q + 2 * mm] = fmaf(gx, st[8 * q + 2 * mm], v.x * f);
+            st[8 * q + 2 * mm + 1] = fmaf(gx, st[8 * q + 2 * mm + 1], v.y * f);
+          }
+        }
+        if (q4 < 2) {  // rows n < 64 hold the 32 rotating pairs (2r, 2r+1)
+          float snx, cnx;
+          __sincosf(th, &snx, &cnx);
+          const float sgn = (n & 1u) ? -snx : snx;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float other = __shfl_xor_sync(0xffffffffu, st[j], 1);
+            st[j] = fmaf(st[j], cnx, other * sgn);  // R(-theta)
+          }
+        }
+      };
+      auto fetch = [&](int x, uint4 (&w)[4], float& f, float& gx, float& th) {
+        const unsigned char* xws = unit_ws(ws, (x * shp.B + b) * shp.H + h);
+        uint32_t seen = 0;
+        ok &= wait_flag(reinterpret_cast<const uint32_t*>(xws + kUnitFlag), epoch, kFlagAgg, seen);
+        const __half* agg = reinterpret_cast<const __half*>(xws + kUnitAgg) + n * 64 + 32 * chalf;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w[q] = ld_cg_v4(agg + 8 * q);
+        f = __ldcg(reinterpret_cast<const float*>(xws + kUnitExp) + 128 * chalf + n);
+        gx = __ldcg(reinterpret_cast<const float*>(xws + kUnitTheta) + kRotary);
+        th = __ldcg(reinterpret_cast<const float*>(xws + kUnitTheta) + ((n >> 1) & 31u));
+      };
+      if (c > 0) {
+        float st[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) st[j] = 0.f;
+        int start = 0;
+        if (lookback) {
+          // Nearest predecessor with a published outgoing state (one thread decides).
+          if (et == 0) {
+            int y = c - 1;
+            for (; y >= 0; --y) {
+              uint32_t seen = 0;
+              const int ub = (y * shp.B + b) * shp.H + h;
+              ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, ub) + kUnitFlag), epoch, kFlagAgg, seen);
+              if (static_cast<int>(seen - epoch) >= static_cast<int>(kFlagIncl)) break;
+            }
+            mi.lookback_start = y;  // -1: none
+          }
+          bar_sync_n(kBarEpilogue, kEpilogueThreads);
+          const int y = mi.lookback_start;
+          if (y >= 0) {
+            const unsigned char* yws = unit_ws(ws, (y * shp.B + b) * shp.H + h);
+            (void)ld_acquire_u32(reinterpret_cast<const uint32_t*>(yws + kUnitFlag));
+            const float* incl = reinterpret_cast<const float*>(yws + kUnitIncl) + n * 64 + 32 * chalf;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint4 w = ld_cg_v4(incl + 4 * q);
+              st[4 * q] = __uint_as_float(w.x);
+              st[4 * q + 1] = __uint_as_float(w.y);
+              st[4 * q + 2] = __uint_as_float(w.z);
+              st[4 * q + 3] = __uint_as_float(w.w);
+            }
+            start = y + 1;
+          }
+        }
+        if (start < c) {
+          uint4 wa[4];
+          float fa, ga, ta;
+          fetch(start, wa, fa, ga, ta);
+          for (int x = start; x < c; ++x) {
+            uint4 wb[4];
+            float fb = 0.f, gb = 0.f, tb = 0.f;
+            if (x + 1 < c) fetch(x + 1, wb, fb, gb, tb);  // in flight while x is folded
+            fold_step(st, wa, fa, ga, ta);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) wa[q] = wb[q];
+            fa = fb;
+            ga = gb;
+            ta = tb;
+          }
+        }
+        // FP16 S^T tile with one power-of-two exponent.
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(st[j]));
+        m = warp_max(m);
+        if (lane == 0) mi.ered[warp - 8] = m;
+        bar_sync_n(kBarEpilogue, kEpilogueThreads);
+#pragma unroll
+        for (int w8 = 0; w8 < 8; ++w8) m = fmaxf(m, mi.ered[w8]);
+        const int se = pow2_scale_exponent(m);
+        const float ss = exp2i(se);
+        if (et == 0) hd.sinv = exp2i(-se);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          st_shared_v4(sb + kSlotS + sw128_offset(n, 32 * chalf + 8 * q), pack_f16x2(st[8 * q] * ss, st[8 * q + 1] * ss),
+                       pack_f16x2(st[8 * q + 2] * ss, st[8 * q + 3] * ss), pack_f16x2(st[8 * q + 4] * ss, st[8 * q + 5] * ss),
+                       pack_f16x2(st[8 * q + 6] * ss, st[8 * q + 7] * ss));
+        fence_async_smem();
+        tc_fence_before();
+        bar_sync_n(kBarEpilogue, kEpilogueThreads);
+        if (et == 0) {
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t koff = (kk >> 2) * 8192u + (kk & 3) * 32u;
+            umma_f16(tm + kColI, desc_sw128(sb + kSlotQ + koff, 0, 1024),
+                     desc_sw128(sb + kSlotS + kk * 2048u, 8192, 1024), kIdInter, kk > 0);
+          }
+          umma_commit(&mi.mma3[slot]);
+        }
+        // Outgoing state S(c+1) = R(-theta_c) (2^total_c S(c) + dS_c) for look-back.
+        if (lookback && c + 1 < shp.nck) {
+          uint4 w[4];
+          const __half* agg = reinterpret_cast<const __half*>(uws + kUnitAgg) + n * 64 + 32 * chalf;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) w[q] = ld_cg_v4(agg + 8 * q);
+          fold_step(st, w, reinterpret_cast<const float*>(uws + kUnitExp)[128 * chalf + n], hd.gtot,
+                    hd.theta[(n >> 1) & 31u]);
+          float* incl = reinterpret_cast<float*>(uws + kUnitIncl) + n * 64 + 32 * chalf;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(st[4 * q], st[4 * q + 1], st[4 * q + 2], st[4 * q + 3]);
+          __threadfence();
+          bar_sync_n(kBarEpilogue, kEpilogueThreads);
+          if (et == 0) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
+        }
+      } else {
+        if (et == 0) mbar_arrive(&mi.mma3[slot]);  // no inter-chunk MMA; keep the phase in step
+        if (lookback && shp.nck > 1) {
+          // Chunk 0: its outgoing state is R(-theta_0) dS_0.
+          float st[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) st[j] = 0.f;
+          uint4 w[4];
+          const __half* agg = reinterpret_cast<const __half*>(uws + kUnitAgg) + n * 64 + 32 * chalf;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) w[q] = ld_cg_v4(agg + 8 * q);
+          fold_step(st, w, reinterpret_cast<const float*>(uws + kUnitExp)[128 * chalf + n], 1.f,
+                    hd.theta[(n >> 1) & 31u]);
+          float* incl = reinterpret_cast<float*>(uws + kUnitIncl) + n * 64 + 32 * chalf;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(st[4 * q], st[4 * q + 1], st[4 * q + 2], st[4 * q + 3]);
+          __threadfence();
+          bar_sync_n(kBarEpilogue, kEpilogueThreads);
+          if (et == 0) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
+        }
+      }
+      // ---- output: combine, gate, stage in the z tile, coalesced stores ----------
+      ok &= mbar_wait(&mi.mma2[slot], ph);
+      ok &= mbar_wait(&mi.mma3[slot], ph);
+      tc_fence_after();
+      {
+        float pv[16], it[16];
+        tmem_ld_16x256_x4(tmem_addr(tm, 32 * q4, kColPV + 32 * chalf), pv);
+        if (c > 0) tmem_ld_16x256_x4(tmem_addr(tm, 32 * q4, kColI + 32 * chalf), it);
+        tmem_wait_ld();
+        const float u0 = exp2i(-static_cast<int>(hd.pe[i0])), u1 = exp2i(-static_cast<int>(hd.pe[i1]));
+        const float w0 = c > 0 ? ex2_approx(hd.cs[i0] - hd.qe[i0]) * hd.sinv : 0.f;
+        const float w1 = c > 0 ? ex2_approx(hd.cs[i1] - hd.qe[i1]) * hd.sinv : 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int j = 32 * chalf + 8 * kk + 2 * c4;
+          const uint32_t a0 = sb + kSlotZ + sw128_offset(i0, j), a1 = sb + kSlotZ + sw128_offset(i1, j);
+          const float2 z0 = unpack_bf16x2(ld_shared_u32(a0)), z1 = unpack_bf16x2(ld_shared_u32(a1));
+          const float o0 = pv[4 * kk] * u0 + (c > 0 ? it[4 * kk] * w0 : 0.f);
+          const float o1 = pv[4 * kk + 1] * u0 + (c > 0 ? it[4 * kk + 1] * w0 : 0.f);
+          const float o2 = pv[4 * kk + 2] * u1 + (c > 0 ? it[4 * kk + 2] * w1 : 0.f);
+          const float o3 = pv[4 * kk + 3] * u1 + (c > 0 ? it[4 * kk + 3] * w1 : 0.f);
+          st_shared_u32(a0, pack_bf16x2(o0 * silu_tanh(z0.x), o1 * silu_tanh(z0.y)));
+          st_shared_u32(a1, pack_bf16x2(o2 * silu_tanh(z1.x), o3 * silu_tanh(z1.y)));
+        }
+      }
+      tc_fence_before();
+      bar_sync_n(kBarEpilogue, kEpilogueThreads);
+      {
+        const int c0 = c * kChunk, nv = hd.nv;
+        // 64 rows x 8 16-byte chunks over 256 threads: row et/4, chunks 2*(et&3), +1.
+        const int r = et >> 2;
+        if (c0 + r < p.T) {
+          bf16* orow = p.out + b * p.so[0] + static_cast<int64_t>(c0 + r) * p.so[1] + h * p.so[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int e = 8 * (2 * (et & 3) + q);
+            const uint4 val = r < nv ? ld_shared_v4(sb + kSlotZ + sw128_offset(r, e)) : make_uint4(0, 0, 0, 0);
+            store16<kVec>(orow + e, val);
+          }
+        }
+      }
+      bar_sync_n(kBarEpilogue, kEpilogueThreads);
+      if (et == 0) mbar_arrive(&mi.freed[slot]);
+    }
+  }
+
+  // ---- teardown: free TMEM; the last CTA advances the epoch -----------------------
+  if (!ok) atomicExch(&g_device_error, 1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem0, kTmemCols);
+  }
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(ws_done, 1) == static_cast<int>(gridDim.x) - 1) {
+      *ws_ticket = 0;
+      *ws_done = 0;
+      __threadfence();
+      st_release_u32(ws_epoch, epoch + kEpochStep);
+    }
+  }
+}
+
+int alignment_class(const RecurrenceParams& p) {
+  auto rows_aligned = [](const void* ptr, const int64_t* st, int nd, int bytes) {
+    if (reinterpret_cast<uintptr_t>(ptr) % bytes) return false;
+    for (int i = 0; i < nd; ++i)
+      if ((st[i] * 2) % bytes) return false;
+    return true;
+  };
+  for (int bytes : {16, 8}) {
+    if (rows_aligned(p.q, p.sq, 3, bytes) && rows_aligned(p.k, p.sk, 3, bytes) &&
+        rows_aligned(p.v, p.sv, 3, bytes) && rows_aligned(p.z, p.sz, 3, bytes) &&
+        rows_aligned(p.out, p.so, 3, bytes))
+      return bytes;
+  }
+  return 2;
+}
+
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices] = {0};
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sm_count[dev] = n > 0 ? n : 148;
+  }
+  return g_sm_count[dev];
+}
+
+template <int kVec>
+int launch(const RecurrenceParams& p, unsigned char* ws, cudaStream_t stream) {
+  auto kernel = recurrence_persistent_kernel<kVec>;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+  const int units = ((p.T + kChunk - 1) / kChunk) * p.B * p.H;
+  const int grid = units < sm_count() ? units : sm_count();
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, ws);
+  return 0;
+}
+
+}  // namespace
+
+size_t recurrence_workspace_bytes(int B, int T, int H) {
+  const size_t units = static_cast<size_t>((T + kChunk - 1) / kChunk) * B * H;
+  return kWsHeader + units * kUnitBytes;
+}
+
+int launch_recurrence_persistent(const RecurrenceParams& p, void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream) {
+  if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H)) return 1;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  switch (alignment_class(p)) {
+    case 16: return launch<16>(p, ws, stream);
+    case 8: return launch<8>(p, ws, stream);
+    default: return launch<2>(p, ws, stream);
+  }
+}
+
+int read_device_error(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (reset) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace tf

@@ -26,13 +26,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with `parity` to complete, giving up after `limit`
-// polls (each poll may suspend the thread for a while). Returns false on
-// timeout so the caller can record an error instead of hanging.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = 1u << 22) {
-  for (uint32_t i = 0; i < limit; ++i)
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Every wait in these kernels gives up after this long (the kernel then records
+// an error and returns instead of hanging).
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+
+// Waits for the phase with `parity` to complete. Returns false on timeout so
+// the caller can record an error instead of hanging.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
 }
 
 // ---- fences ----------------------------------------------------------------

@@ -1,6 +1,7 @@
 // C ABI of trifusion_b200: argument validation, status codes and launches.
 // Declarations and the reference interface each entry point replaces are in
 // include/trifusion_b200.h.
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 
@@ -46,7 +47,7 @@ int recurrence_entry(const void* q, const void* k, const void* v, const float* a
                      const float* kb, const void* angles, const float* d, const void* z,
                      void* out, const int64_t* strides, int batch, int seqlen, int heads,
                      int groups, const float* qw, const float* kw, float eps,
-                     const int64_t* lengths, void* stream) {
+                     const int64_t* lengths, void* workspace, size_t workspace_bytes, void* stream) {
   if (!strides || batch < 0 || seqlen < 0 || heads < 0 || groups <= 0) return TF_ERR_ARG;
   if (trap_dtype != TF_F32 && trap_dtype != TF_BF16) return TF_ERR_ARG;
   if (heads % groups != 0) return TF_ERR_ARG;
@@ -90,8 +91,10 @@ int recurrence_entry(const void* q, const void* k, const void* v, const float* a
   p.Hq = groups;
   int st = check_device();
   if (st != TF_OK) return st;
+  if (!workspace) return TF_ERR_ARG;
+  if (workspace_bytes < recurrence_workspace_bytes(batch, seqlen, heads)) return TF_ERR_SIZE;
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  st = cluster_path_supported(p) ? launch_recurrence_cluster(p, cs) : launch_recurrence_serial(p, cs);
+  st = launch_recurrence_persistent(p, workspace, workspace_bytes, cs);
   if (st != 0) {
     const int ls = launch_status();
     return ls != TF_OK ? ls : TF_ERR_LAUNCH;
@@ -123,14 +126,19 @@ const char* tf_last_cuda_error(void) { return tf::g_last_error; }
 
 int tf_device_error(int reset) { return tf::read_device_error(reset); }
 
+size_t tf_recurrence_workspace_size(int batch, int seqlen, int heads) {
+  if (batch <= 0 || seqlen <= 0 || heads <= 0) return 0;
+  return tf::recurrence_workspace_bytes(batch, seqlen, heads);
+}
+
 int tf_fused_mamba_fwd(const void* q, const void* k, const void* v, const float* adt,
                        const float* dt, const void* trap, int trap_dtype, const float* qb,
                        const float* kb, const void* angles, const float* d, const void* z,
                        void* out, const int64_t* strides, int batch, int seqlen, int heads,
-                       int groups, void* stream) {
+                       int groups, void* workspace, size_t workspace_bytes, void* stream) {
   return tf::recurrence_entry(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out,
                               strides, batch, seqlen, heads, groups, nullptr, nullptr, 1e-5f,
-                              nullptr, stream);
+                              nullptr, workspace, workspace_bytes, stream);
 }
 
 int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v, const float* adt,
@@ -139,10 +147,10 @@ int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v, const f
                             void* out, const int64_t* strides, int batch, int seqlen,
                             int heads, int groups, const float* q_norm_w,
                             const float* k_norm_w, float eps, const int64_t* lengths,
-                            void* stream) {
+                            void* workspace, size_t workspace_bytes, void* stream) {
   return tf::recurrence_entry(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out,
                               strides, batch, seqlen, heads, groups, q_norm_w, k_norm_w, eps,
-                              lengths, stream);
+                              lengths, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -19,6 +19,7 @@ SHAPE_MESSAGE = "L4 recurrence requires state=128, head=64, rotary=32"
 _p = ctypes.c_void_p
 _i = ctypes.c_int
 _f = ctypes.c_float
+_z = ctypes.c_size_t
 
 # name -> argtypes; every function returns int unless listed in _RESTYPES.
 SIGNATURES = {
@@ -26,12 +27,14 @@ SIGNATURES = {
     "tf_version": [],
     "tf_last_cuda_error": [],
     "tf_device_error": [_i],
+    "tf_recurrence_workspace_size": [_i, _i, _i],
     "tf_fused_mamba_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
-                           _i, _i, _i, _i, _p],
+                           _i, _i, _i, _i, _p, _z, _p],
     "tf_mamba_recurrence_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
-                                _i, _i, _i, _i, _p, _p, _f, _p, _p],
+                                _i, _i, _i, _i, _p, _p, _f, _p, _p, _z, _p],
 }
-_RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p}
+_RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p,
+             "tf_recurrence_workspace_size": ctypes.c_size_t}
 
 _lib = None
 
@@ -69,3 +72,24 @@ def check(status):
 def int64_array(values):
     values = list(values)
     return (ctypes.c_int64 * len(values))(*values)
+
+
+_workspaces = {}
+
+
+def workspace(device, nbytes):
+    """Zero-filled device workspace of at least `nbytes`, cached per device.
+
+    The kernels keep it consistent between launches themselves, so it is
+    zeroed only when (re)allocated. Launches sharing it must not overlap in
+    time, which holds for calls issued from one stream, or serialised across
+    streams, as the reference requires of its callers (docs/api.md:47-48).
+    """
+    import torch
+
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _workspaces.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[idx] = buf
+    return buf

@@ -69,12 +69,15 @@ def fused_mamba(q, k, v, adt, dt, trap, qb, kb, angles, d, z, warps=8):
     out = torch.empty_like(v, memory_format=torch.contiguous_format)
     stream = torch.cuda.current_stream(v.device).cuda_stream
     with torch.cuda.device(v.device):
-        _lib.check(_lib.lib().tf_fused_mamba_fwd(
+        lib = _lib.lib()
+        nws = lib.tf_recurrence_workspace_size(b, t, h)
+        ws = _lib.workspace(v.device, nws)
+        _lib.check(lib.tf_fused_mamba_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(), dt.data_ptr(),
             trap.data_ptr(), _lib.TF_BF16 if trap.dtype == torch.bfloat16 else _lib.TF_F32,
             qb.data_ptr(), kb.data_ptr(), angles.data_ptr(), d.data_ptr(), z.data_ptr(),
             out.data_ptr(), _strides(q, k, v, adt, dt, trap, angles, z, out),
-            b, t, h, hq, stream))
+            b, t, h, hq, ws.data_ptr(), ws.numel(), stream))
     return out
 
 
@@ -103,12 +106,15 @@ def fused_recurrence(q, k, v, adt, dt, trap, qb, kb, angles, d, z, *, q_norm=Non
         lengths = lengths.contiguous()
     stream = torch.cuda.current_stream(v.device).cuda_stream
     with torch.cuda.device(v.device):
-        _lib.check(_lib.lib().tf_mamba_recurrence_fwd(
+        lib = _lib.lib()
+        nws = lib.tf_recurrence_workspace_size(b, t, h)
+        ws = _lib.workspace(v.device, nws)
+        _lib.check(lib.tf_mamba_recurrence_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(), dt.data_ptr(),
             trap.data_ptr(), _lib.TF_BF16 if trap.dtype == torch.bfloat16 else _lib.TF_F32,
             qb.data_ptr(), kb.data_ptr(), angles.data_ptr(), d.data_ptr(), z.data_ptr(),
             out.data_ptr(), _strides(q, k, v, adt, dt, trap, angles, z, out),
             b, t, h, hq, None if qw is None else qw.data_ptr(),
             None if kw is None else kw.data_ptr(), float(eps),
-            None if lengths is None else lengths.data_ptr(), stream))
+            None if lengths is None else lengths.data_ptr(), ws.data_ptr(), ws.numel(), stream))
     return out

@@ -104,6 +104,30 @@ int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v,
                             float eps, const int64_t* lengths, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * tf_mamba_recurrence_fwd without a caller workspace; it allocates nothing.
+ * No counterpart in the reference (which always allocates through PyTorch).
+ *
+ * For callers that cannot allocate device memory: plugin hosts that own all
+ * GPU memory through their own pool and expose no allocation hook, and
+ * latency-critical services that forbid cudaMalloc after start-up. The
+ * workspace is a 64 MiB array inside the library, held on every GPU that loads
+ * it until exit; problems needing more (tf_recurrence_workspace_size) return
+ * TF_ERR_SIZE without launching. The first call on a device sets up that
+ * device's array address and must come before any stream capture. Every call
+ * clears the array's header and chunk flags on `stream` before the launch;
+ * calls that overlap on the GPU share the array and race, so serialise them.
+ * Same arguments and results as tf_mamba_recurrence_fwd otherwise.
+ * ------------------------------------------------------------------------ */
+int tf_mamba_recurrence_fwd_static(const void* q, const void* k, const void* v,
+                                   const float* adt, const float* dt, const void* trap,
+                                   int trap_dtype, const float* qb, const float* kb,
+                                   const void* angles, const float* d, const void* z,
+                                   void* out, const int64_t* strides, int batch, int seqlen,
+                                   int heads, int groups, const float* q_norm_w,
+                                   const float* k_norm_w, float eps, const int64_t* lengths,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

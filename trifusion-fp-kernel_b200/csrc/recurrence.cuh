@@ -37,5 +37,9 @@ int launch_recurrence_persistent(const RecurrenceParams& p, void* workspace, siz
                                  cudaStream_t stream);
 // Device error word set when a kernel's bounded wait gave up (synchronous read).
 int read_device_error(int reset);
+// The library's own workspace array (see recurrence_persistent.cu): capacity,
+// and per-call preparation (device-address set-up on first use, clearing).
+size_t static_workspace_capacity();
+int prepare_static_workspace(int B, int T, int H, cudaStream_t stream, void** ws, size_t* bytes);
 
 }  // namespace tf

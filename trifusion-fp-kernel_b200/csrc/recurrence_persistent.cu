@@ -1023,3 +1023,69 @@ int read_device_error(int reset) {
 }
 
 }  // namespace tf
+
+// ===================================================================================
+// Entry point that allocates nothing.
+//
+// Some callers of this library cannot allocate device memory: plugin hosts that
+// own all GPU memory through their own pool and give plugins no allocation hook,
+// and latency-critical services that forbid cudaMalloc after start-up (it can
+// synchronise the device and take milliseconds). They call
+// tf_mamba_recurrence_fwd_static, whose workspace is the file-scope array below
+// instead of a caller buffer.
+//
+// Limits and rules:
+//   - The array holds kStaticWorkspaceBytes (64 MiB). Every GPU that loads this
+//     library keeps that much device memory until the process exits. Problems
+//     whose workspace (tf_recurrence_workspace_size) exceeds it are rejected with
+//     TF_ERR_SIZE before anything is launched.
+//   - The first call on a device looks up the array's device address there
+//     (cudaGetSymbolAddress, with that device current) and caches it; make that
+//     first call before any stream capture.
+//   - All calls on a device share the one array. Each call first clears what
+//     the kernel needs at zero (the workspace header and every chunk flag), so
+//     a call never depends on what an earlier call left behind, but calls that
+//     overlap on the GPU race with each other: serialise them.
+// ===================================================================================
+namespace tf {
+namespace {
+
+constexpr size_t kStaticWorkspaceBytes = size_t{64} << 20;
+__device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
+
+void* g_static_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_static_workspace on the current device (set up once).
+int static_workspace(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  if (g_static_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_workspace) != cudaSuccess || ptr == nullptr) return -1;
+    g_static_ptr[dev] = ptr;
+  }
+  *out = g_static_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
+// Clears the static workspace's header and chunk flags on `stream`, then
+// returns its address and capacity; nonzero when the set-up failed.
+int prepare_static_workspace(int B, int T, int H, cudaStream_t stream, void** ws, size_t* bytes) {
+  void* ptr = nullptr;
+  if (static_workspace(&ptr) != 0) return -1;
+  const size_t units = static_cast<size_t>((T + kChunk - 1) / kChunk) * B * H;
+  unsigned char* base = static_cast<unsigned char*>(ptr);
+  if (cudaMemsetAsync(base, 0, kWsHeader, stream) != cudaSuccess) return -1;
+  if (units > 0 && cudaMemset2DAsync(base + kWsHeader + kUnitFlag, kUnitBytes, 0, sizeof(uint32_t), units,
+                                     stream) != cudaSuccess)
+    return -1;
+  *ws = ptr;
+  *bytes = kStaticWorkspaceBytes;
+  return 0;
+}
+
+size_t static_workspace_capacity() { return kStaticWorkspaceBytes; }
+
+}  // namespace tf

@@ -9,7 +9,6 @@
 #include "recurrence.cuh"
 
 namespace tf {
-namespace {
 
 thread_local char g_last_error[256] = "";
 
@@ -102,7 +101,6 @@ int recurrence_entry(const void* q, const void* k, const void* v, const float* a
   return launch_status();
 }
 
-}  // namespace
 }  // namespace tf
 
 extern "C" {
@@ -139,6 +137,31 @@ int tf_fused_mamba_fwd(const void* q, const void* k, const void* v, const float*
   return tf::recurrence_entry(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out,
                               strides, batch, seqlen, heads, groups, nullptr, nullptr, 1e-5f,
                               nullptr, workspace, workspace_bytes, stream);
+}
+
+int tf_mamba_recurrence_fwd_static(const void* q, const void* k, const void* v, const float* adt,
+                                   const float* dt, const void* trap, int trap_dtype,
+                                   const float* qb, const float* kb, const void* angles,
+                                   const float* d, const void* z, void* out,
+                                   const int64_t* strides, int batch, int seqlen, int heads,
+                                   int groups, const float* q_norm_w, const float* k_norm_w,
+                                   float eps, const int64_t* lengths, void* stream) {
+  if (batch < 0 || seqlen < 0 || heads < 0) return TF_ERR_ARG;
+  if (batch == 0 || seqlen == 0 || heads == 0) return TF_OK;
+  if (tf::recurrence_workspace_bytes(batch, seqlen, heads) > tf::static_workspace_capacity()) {
+    snprintf(tf::g_last_error, sizeof tf::g_last_error,
+             "problem needs %zu workspace bytes; the static workspace holds %zu",
+             tf::recurrence_workspace_bytes(batch, seqlen, heads), tf::static_workspace_capacity());
+    return TF_ERR_SIZE;
+  }
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  void* ws = nullptr;
+  size_t bytes = 0;
+  if (tf::prepare_static_workspace(batch, seqlen, heads, static_cast<cudaStream_t>(stream), &ws, &bytes) != 0)
+    return tf::launch_status() != TF_OK ? TF_ERR_LAUNCH : TF_ERR_DEVICE;
+  return tf::recurrence_entry(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out, strides, batch,
+                              seqlen, heads, groups, q_norm_w, k_norm_w, eps, lengths, ws, bytes, stream);
 }
 
 int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v, const float* adt,

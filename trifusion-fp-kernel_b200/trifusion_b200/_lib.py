@@ -32,6 +32,8 @@ SIGNATURES = {
                            _i, _i, _i, _i, _p, _z, _p],
     "tf_mamba_recurrence_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
                                 _i, _i, _i, _i, _p, _p, _f, _p, _p, _z, _p],
+    "tf_mamba_recurrence_fwd_static": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
+                                       _i, _i, _i, _i, _p, _p, _f, _p, _p],
 }
 _RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p,
              "tf_recurrence_workspace_size": ctypes.c_size_t}

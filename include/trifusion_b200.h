@@ -128,6 +128,77 @@ int tf_mamba_recurrence_fwd_static(const void* q, const void* k, const void* v,
                                    const float* k_norm_w, float eps, const int64_t* lengths,
                                    void* stream);
 
+/* ========================================================================
+ * Satellite operators on the recurrence path. Contiguous row-major tensors
+ * (the reference wrappers call .contiguous() first); `dtype` is TF_F32 or
+ * TF_BF16; arithmetic is FP32 with one rounding to the output type; copy and
+ * index operators move raw bits (bit-exact). Lengths are int64 device arrays;
+ * values outside [0, T] are clamped to it.
+ * ======================================================================== */
+
+/* A6 RMSNorm: y = x * rsqrt(mean(x^2) + eps) * w over rows of `width`; y has
+ * x's dtype, w is FP32. Replaces kernels/native.py:69-70 `rms` (its `_norm`
+ * MODE 0, native.py:8-39) and RMSNorm.forward (kernels/__init__.py:23-27). */
+int tf_rms_fwd(const void* x, int dtype, const float* w, void* y, int64_t rows, int width,
+               float eps, void* stream);
+
+/* Evidence norm: rows with mask != 0 take x + value * 2 sigmoid(gate), others 0;
+ * then RMSNorm; FP32 out. Replaces kernels/native.py:73-74 `evidence_norm`
+ * (`_norm` MODE 1, native.py:28-34). */
+int tf_evidence_norm_fwd(const void* x, int x_dtype, const void* value, const void* gate,
+                         int vg_dtype, const float* w, const uint8_t* mask, float* y,
+                         int64_t rows, int width, float eps, void* stream);
+
+/* A10 mean_norm of the bidirectional pair: y = RMSNorm((a + b) / 2) * w, FP32 out.
+ * Replaces kernels/native.py:77-78 `mean_norm` (`_norm` MODE 2, native.py:35-37). */
+int tf_mean_norm_fwd(const void* a, const void* b, int dtype, const float* w, float* y,
+                     int64_t rows, int width, float eps, void* stream);
+
+/* A7 controls: A = min(-(max(a,0) + 1/(1 - min(a,0))), -a_floor),
+ * dt = softplus(ddt + dt_bias[h]) (identity above 20), adt = A * dt; inputs
+ * [B,T,H] with strides {a: b,t,h, ddt: b,t,h} (h stride must be 1), outputs
+ * [B,H,T] FP32 contiguous. Replaces kernels/buffers.py:82-101 `mamba_controls`
+ * (`_controls`, kernels/primitives.py:190-216). */
+int tf_mamba_controls_fwd(const void* a, const void* ddt, int dtype, const int64_t* strides,
+                          const float* dt_bias, float a_floor, float* adt, float* dt, int batch,
+                          int seqlen, int heads, void* stream);
+
+/* A8 length mask: row r of y = row r of x where mask[r] != 0, else zero bytes.
+ * Replaces kernels/buffers.py:6-10 `mask_buffer` (`_mask`, primitives.py:65-70). */
+int tf_mask_rows_fwd(const void* x, const uint8_t* mask, void* y, int64_t rows,
+                     int64_t row_bytes, void* stream);
+
+/* A9 valid-prefix reversal: y[b,t] = x[b, len-1-t] for t < len, else zero bytes.
+ * Replaces kernels/__init__.py:43-54 `reverse_valid` (`_reverse`, primitives.py:40-47). */
+int tf_reverse_valid_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
+                         int64_t row_bytes, void* stream);
+
+/* A11 SwiGLU: x [rows, 2d] -> y[r,c] = silu(x[r,c]) * x[r,d+c], x's dtype.
+ * Replaces kernels/__init__.py:30-40 `swiglu` (`_swiglu`, primitives.py:25-37). */
+int tf_swiglu_fwd(const void* x, int dtype, void* y, int64_t rows, int d, void* stream);
+
+/* A12 branch gate: x [rows, 3d], gate [rows, 3] -> y[r,j,:] = x[r,j,:] * 2 sigmoid(gate[r,j]).
+ * Replaces kernels/__init__.py:57-81 `gated_concat` (`_gate`, primitives.py:50-62). */
+int tf_gated_concat_fwd(const void* x, int dtype, const void* gate, int gate_dtype, void* y,
+                        int64_t rows, int d, void* stream);
+
+/* A13 Pool4: x [B,T,D] -> y [B,ceil(T/4),D], the mean of the valid frames of each
+ * group of 4 (divisor max(min(len - 4g, 4), 1)); bit-identical to the reference
+ * kernel. Replaces kernels/buffers.py:35-43 `Pool4.apply` (`_pool4`,
+ * primitives.py:90-113) and masking.py:59-69 `Grids.pool`. */
+int tf_pool4_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int batch, int seqlen,
+                 int width, void* stream);
+
+/* A13 masked time mean: y[b,:] = sum_{t<len} x[b,t,:] / len, FP32 [B,D].
+ * Replaces decoder.py:60-62 (`(x.float() * mask).sum(1) / lengths`). */
+int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* y, int batch,
+                       int seqlen, int width, void* stream);
+
+/* A13 end gather: y[b] = x[b, len-1] (len = 0 reads row T-1, like PyTorch's -1 index).
+ * Replaces decoder.py:63 (`mf[arange(b), lengths - 1]`). */
+int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
+                      int64_t row_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

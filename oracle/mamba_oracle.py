@@ -323,6 +323,34 @@ def pool4(x, lengths, out_bf16=True):
     return bf16_round(y) if out_bf16 else y
 
 
+def pool4_f32(x, lengths, out_bf16=True):
+    """Pool4 in the reference kernel's own arithmetic (``primitives.py:104-111``):
+    FP32 accumulator starting at 0, valid frames added in order k = 0..3, one
+    IEEE FP32 divide by the count. Bit-exact statement of the kernel."""
+    xf = np.asarray(x, np.float32)
+    b, t, dd = xf.shape
+    lt = (t + 3) // 4
+    lengths = np.minimum(np.maximum(np.asarray(lengths, np.int64), 0), t)
+    acc = np.zeros((b, lt, dd), np.float32)
+    for k in range(4):
+        src = 4 * np.arange(lt) + k
+        ok = src[None, :] < lengths[:, None]
+        rows = np.take(xf, np.minimum(src, t - 1), axis=1)
+        acc = np.where(ok[..., None], acc + rows, acc).astype(np.float32)
+    y = (acc / pool4_counts(lengths, t).astype(np.float32)[..., None]).astype(np.float32)
+    return bf16_round(y) if out_bf16 else y
+
+
+def evidence_norm(x, value, gate, weight, mask, eps=1e-5):
+    """``native.py:28-34,73-74`` (MODE 1): rows with mask set take
+    x + value * 2 sigmoid(gate), other rows are zero; then RMSNorm; FP32 out."""
+    xf = np.asarray(x, np.float64) + np.asarray(value, np.float64) * (
+        2 * _sigmoid(np.asarray(gate, np.float64)))
+    xf = np.where(np.asarray(mask, bool)[..., None], xf, 0.0)
+    ms = (xf ** 2).mean(-1, keepdims=True)
+    return (xf / np.sqrt(ms + eps) * np.asarray(weight, np.float64)).astype(np.float32)
+
+
 def pool4_counts(lengths, t):
     """Integer divisors of `pool4`: clamp(min(len - 4g, 4), 1) (``primitives.py:294``)."""
     g = np.arange((t + 3) // 4)[None, :]

@@ -163,6 +163,14 @@ def make_satellites():
     wm = 1 + 0.02 * torch.randn(dim, generator=g)
     out["mn_a"], out["mn_b"], out["mn_w"] = mf.float().numpy(), mb.float().numpy(), wm.numpy()
     out["mean_norm_triton"] = native.mean_norm(mf, mb, wm, 1e-5).numpy()
+    # Evidence norm (MODE 1): FP32 residual + BF16 value/gate, masked rows.
+    xe = torch.randn(b, t, dim, generator=g)
+    ve = torch.randn(b, t, dim, generator=g).to(bf)
+    ge = torch.randn(b, t, dim, generator=g).to(bf)
+    me = time_mask(lengths, t)
+    out["ev_x"], out["ev_v"], out["ev_g"], out["ev_mask"] = (
+        xe.numpy(), ve.float().numpy(), ge.float().numpy(), me.numpy())
+    out["evidence_norm_triton"] = native.evidence_norm(xe, ve, ge, wm, me, 1e-5).numpy()
     # A/dt controls from strided BF16 projection views.
     p = torch.randn(b, t, 3 * h + 5, generator=g).to(bf) * 4
     a, ddt = p[..., :h], p[..., h:2 * h]

@@ -79,3 +79,49 @@ def test_lazy_import_keeps_torch_out():
             "assert {'configure_runtime','load_student','InferenceEngine','fused_mamba'} <= set(dir(t))"
             % str(root))
     subprocess.run([sys.executable, "-c", code], check=True)
+
+
+def test_satellite_entry_points_validate_on_the_host():
+    lib = _lib.lib()
+    # Bad dtype codes and negative sizes are argument errors; empty work is a no-op.
+    assert lib.tf_rms_fwd(None, 7, None, None, 4, 128, 1e-5, None) == _lib.TF_ERR_ARG
+    assert lib.tf_rms_fwd(None, _lib.TF_BF16, None, None, 0, 128, 1e-5, None) == _lib.TF_OK
+    assert lib.tf_mean_norm_fwd(None, None, _lib.TF_BF16, None, None, 4, 0, 1e-5, None) == _lib.TF_ERR_ARG
+    assert lib.tf_evidence_norm_fwd(None, 0, None, None, 3, None, None, None, 1, 8, 1e-5, None) == _lib.TF_ERR_ARG
+    assert lib.tf_swiglu_fwd(None, _lib.TF_BF16, None, -1, 8, None) == _lib.TF_ERR_ARG
+    assert lib.tf_swiglu_fwd(None, _lib.TF_BF16, None, 0, 8, None) == _lib.TF_OK
+    assert lib.tf_gated_concat_fwd(None, 0, None, 9, None, 1, 8, None) == _lib.TF_ERR_ARG
+    assert lib.tf_mask_rows_fwd(None, None, None, 0, 16, None) == _lib.TF_OK
+    assert lib.tf_reverse_valid_fwd(None, None, None, 2, 3, 16, None) == _lib.TF_ERR_ARG
+    assert lib.tf_pool4_fwd(None, 1, None, None, 0, 10, 8, None) == _lib.TF_OK
+    assert lib.tf_masked_mean_fwd(None, 5, None, None, 1, 10, 8, None) == _lib.TF_ERR_ARG
+    assert lib.tf_end_gather_fwd(None, None, None, 2, 0, 16, None) == _lib.TF_ERR_ARG
+    strides = _lib.int64_array([24, 12, 1, 24, 12, 2])  # ddt innermost stride 2: layout error
+    assert lib.tf_mamba_controls_fwd(None, None, 1, strides, None, 1e-4, None, None, 1, 2, 3,
+                                     None) == _lib.TF_ERR_ARG
+    buf = ctypes.c_void_p(1)
+    assert lib.tf_mamba_controls_fwd(buf, buf, 1, strides, buf, 1e-4, buf, buf, 1, 2, 3,
+                                     None) == _lib.TF_ERR_LAYOUT
+
+
+def test_satellite_wrappers_reject_cpu_tensors():
+    from trifusion_b200.kernels import gated_concat, reverse_valid, swiglu
+    from trifusion_b200.kernels import native
+    from trifusion_b200.kernels.buffers import Pool4, mamba_controls, mask_buffer
+
+    x = torch.zeros(2, 8, 16, dtype=torch.bfloat16)
+    lengths = torch.tensor([8, 3])
+    calls = [
+        lambda: swiglu(x),
+        lambda: reverse_valid(x, lengths),
+        lambda: gated_concat(torch.zeros(2, 8, 48, dtype=torch.bfloat16), torch.zeros(2, 8, 3)),
+        lambda: native.rms(x, torch.ones(16)),
+        lambda: native.mean_norm(x, x, torch.ones(16)),
+        lambda: native.masked_mean(x, lengths),
+        lambda: Pool4.apply(x, lengths),
+        lambda: mask_buffer(x, torch.ones(2, 8, dtype=torch.bool)),
+        lambda: mamba_controls(x[..., :4], x[..., 4:8], torch.zeros(4), 1e-4),
+    ]
+    for call in calls:
+        with pytest.raises(RuntimeError, match="CUDA tensors"):
+            call()

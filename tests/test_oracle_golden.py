@@ -152,3 +152,19 @@ def test_pool_oracle(sat):
 def test_masked_mean_oracle(sat):
     y = O.masked_mean(sat["x"], sat["lengths"])
     np.testing.assert_allclose(y, sat["masked_mean_torch"], rtol=1e-5, atol=1e-6)
+
+
+def test_pool4_f32_is_the_reference_arithmetic(sat):
+    # The FP32 sequential statement equals the PyTorch formula bit for bit, and
+    # truncating it to BF16 reproduces the interpreter's stored output exactly.
+    x, lengths = sat["x"], sat["lengths"]
+    assert np.array_equal(O.pool4_f32(x, lengths), sat["pool_torch"])
+    raw = O.pool4_f32(x, lengths, out_bf16=False)
+    truncated = (raw.view(np.uint32) & 0xFFFF0000).view(np.float32)
+    assert np.array_equal(truncated, sat["pool_triton"])
+
+
+def test_evidence_norm_oracle(sat):
+    y = O.evidence_norm(sat["ev_x"], sat["ev_v"], sat["ev_g"], sat["mn_w"], sat["ev_mask"])
+    np.testing.assert_allclose(y, sat["evidence_norm_triton"], rtol=2e-6, atol=2e-6)
+    assert (sat["evidence_norm_triton"][~sat["ev_mask"]] == 0).all()

@@ -1,0 +1,257 @@
+"""GPU parity of the satellite operators (rows A6-A13 around the recurrence).
+
+Each CUDA operator is called through its drop-in Python wrapper (which calls
+the C ABI) and compared with the reference's own outputs (golden vectors from
+``tests/golden/satellites.npz``) and with the CPU oracle at model sizes.
+Index and copy operators must match bit for bit; arithmetic ones within one
+BF16 ulp (BF16 outputs) or 2e-6 relative (FP32 outputs).
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mamba_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from trifusion_b200.kernels import gated_concat, reverse_valid, swiglu  # noqa: E402
+from trifusion_b200.kernels import native  # noqa: E402
+from trifusion_b200.kernels.buffers import Pool4, mamba_controls, mask_buffer  # noqa: E402
+
+DEV = "cuda"
+BF = torch.bfloat16
+GOLDEN = Path(__file__).resolve().parent / "golden" / "satellites.npz"
+BF16_ULP = 2.0 ** -7  # relative spacing bound of BF16 values
+
+
+@pytest.fixture(scope="module")
+def sat():
+    return dict(np.load(GOLDEN))
+
+
+def gpu(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    return t.to(dtype) if dtype is not None else t
+
+
+def host(t):
+    return t.float().cpu().numpy()
+
+
+def within_bf16_ulp(y, ref, ulps=1):
+    return np.all(np.abs(y - ref) <= ulps * BF16_ULP * np.abs(ref) + 1e-30)
+
+
+# ---------------------------------------------------------------- golden vectors
+
+def test_rms_matches_reference_formula(sat):
+    y = host(native.rms(gpu(sat["rms_x"], BF), gpu(sat["rms_w"])))
+    assert within_bf16_ulp(y, sat["rms_torch"])
+    assert (y != sat["rms_torch"]).mean() < 0.01
+
+
+def test_mean_norm_matches_reference_kernel(sat):
+    y = native.mean_norm(gpu(sat["mn_a"], BF), gpu(sat["mn_b"], BF), gpu(sat["mn_w"]))
+    assert y.dtype == torch.float32
+    np.testing.assert_allclose(host(y), sat["mean_norm_triton"], rtol=2e-6, atol=2e-6)
+
+
+def test_evidence_norm_matches_reference_kernel(sat):
+    y = native.evidence_norm(gpu(sat["ev_x"]), gpu(sat["ev_v"], BF), gpu(sat["ev_g"], BF),
+                             gpu(sat["mn_w"]), gpu(sat["ev_mask"]))
+    np.testing.assert_allclose(host(y), sat["evidence_norm_triton"], rtol=2e-6, atol=2e-6)
+
+
+def test_controls_match_reference_kernel(sat):
+    # Strided views of one projection row, as the model passes them.
+    b, t, h = sat["ctl_a"].shape
+    p = torch.zeros(b, t, 3 * h + 5, dtype=BF, device=DEV)
+    p[..., :h] = gpu(sat["ctl_a"], BF)
+    p[..., h:2 * h] = gpu(sat["ctl_ddt"], BF)
+    adt, dt = mamba_controls(p[..., :h], p[..., h:2 * h], gpu(sat["ctl_bias"]), 1e-4)
+    np.testing.assert_allclose(host(dt), sat["ctl_dt"], rtol=2e-6, atol=1e-7)
+    np.testing.assert_allclose(host(adt), sat["ctl_adt"], rtol=2e-6, atol=1e-7)
+
+
+def test_index_ops_bit_exact(sat):
+    x, lengths = gpu(sat["x"], BF), gpu(sat["lengths"])
+    mask = torch.arange(x.shape[1], device=DEV)[None, :] < lengths[:, None]
+    assert np.array_equal(host(mask_buffer(x, mask)), sat["mask_triton"])
+    assert np.array_equal(host(reverse_valid(x, lengths)), sat["reverse_torch"])
+    assert np.array_equal(host(native.end_gather(x, lengths)), sat["end_torch"])
+
+
+def test_swiglu_and_gate_match_reference(sat):
+    y = host(swiglu(gpu(sat["sw_x"], BF)))
+    assert within_bf16_ulp(y, sat["swiglu_torch"])
+    assert (y != sat["swiglu_torch"]).mean() < 0.01
+    y = host(gated_concat(gpu(sat["gate_x"], BF), gpu(sat["gate_g"], BF)))
+    assert within_bf16_ulp(y, sat["gate_torch"])
+    assert (y != sat["gate_torch"]).mean() < 0.01
+
+
+def test_pool4_bit_exact_with_reference(sat):
+    y = host(Pool4.apply(gpu(sat["x"], BF), gpu(sat["lengths"])))
+    assert np.array_equal(y, sat["pool_torch"])
+
+
+def test_masked_mean_matches_reference(sat):
+    y = native.masked_mean(gpu(sat["x"], BF), gpu(sat["lengths"]))
+    np.testing.assert_allclose(host(y), sat["masked_mean_torch"], rtol=1e-5, atol=1e-6)
+
+
+# ---------------------------------------------------------------- model sizes
+
+def seeded(shape, seed, scale=1.0, dtype=BF):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(dtype)
+
+
+LENGTHS = [200, 137, 1, 0, 64, 199, 3, 200]
+
+
+@pytest.mark.parametrize("dtype", [BF, torch.float32])
+def test_index_ops_model_size(dtype):
+    b, t, d = len(LENGTHS), 200, 768
+    x = seeded((b, t, d), 1, dtype=dtype)
+    lengths = torch.tensor(LENGTHS)
+    xd, ld = x.to(DEV), lengths.to(DEV)
+    mask = torch.arange(t)[None, :] < lengths[:, None]
+    bits = torch.int16 if dtype == BF else torch.int32
+    xn = x.view(bits).numpy()
+    got = mask_buffer(xd, mask.to(DEV)).cpu()
+    assert np.array_equal(got.view(bits).numpy(), O.mask_rows(xn, LENGTHS))
+    got = reverse_valid(xd, ld).cpu()
+    assert np.array_equal(got.view(bits).numpy(), O.reverse_valid(xn, LENGTHS))
+    # Reversing twice restores the valid prefix and keeps the tail zero.
+    twice = reverse_valid(reverse_valid(xd, ld), ld)
+    assert torch.equal(twice, mask_buffer(xd, mask.to(DEV)))
+
+
+def test_index_ops_odd_row_sizes_and_views():
+    # 3 BF16 per row (6 bytes): no 16/8/4-byte vectors fit; offset base pointer.
+    b, t = 4, 33
+    base = seeded((b * t * 3 + 1,), 2).to(DEV)
+    x = base[1:].view(b, t, 3)  # base pointer 2 bytes past an allocation boundary
+    lengths = torch.tensor([33, 0, 17, 1])
+    mask = (torch.arange(t)[None, :] < lengths[:, None]).to(DEV)
+    ref = O.mask_rows(x.cpu().view(torch.int16).numpy(), lengths.numpy())
+    assert np.array_equal(mask_buffer(x, mask).cpu().view(torch.int16).numpy(), ref)
+    ref = O.reverse_valid(x.cpu().view(torch.int16).numpy(), lengths.numpy())
+    assert np.array_equal(reverse_valid(x, lengths.to(DEV)).cpu().view(torch.int16).numpy(), ref)
+    end = native.end_gather(x, lengths.to(DEV)).cpu()
+    # length 0 reads index -1 (the last row), as PyTorch indexing does
+    assert torch.equal(end, x.cpu()[torch.arange(b), lengths - 1])
+
+
+@pytest.mark.parametrize("t", [200, 401, 3, 4])
+def test_pool4_model_size_bit_exact(t):
+    b, d = 8, 384
+    x = seeded((b, t, d), 3)
+    lengths = torch.tensor([min(v, t) for v in LENGTHS])
+    y = Pool4.apply(x.to(DEV), lengths.to(DEV)).cpu().float().numpy()
+    assert np.array_equal(y, O.pool4_f32(x.float().numpy(), lengths.numpy()))
+
+
+@pytest.mark.parametrize("dtype", [BF, torch.float32])
+@pytest.mark.parametrize("width", [128, 384, 1024, 36])
+def test_rms_model_size(dtype, width):
+    x = seeded((16, 101, width), 4, scale=3.0, dtype=dtype)
+    w = 1 + 0.02 * torch.randn(width, generator=torch.Generator().manual_seed(5))
+    y = native.rms(x.to(DEV), w.to(DEV)).cpu()
+    assert y.dtype == dtype
+    ref = O.rms(x.float().numpy(), w.numpy(), out_bf16=dtype == BF)
+    if dtype == BF:
+        assert within_bf16_ulp(y.float().numpy(), ref)
+    else:
+        np.testing.assert_allclose(y.numpy(), ref, rtol=2e-6, atol=1e-6)
+
+
+def test_norm_family_model_size():
+    b, t, d = 16, 101, 384
+    lengths = torch.tensor([101, 50, 1, 0] * 4)
+    mask = torch.arange(t)[None, :] < lengths[:, None]
+    x = seeded((b, t, d), 6, dtype=torch.float32)
+    v, g = seeded((b, t, d), 7), seeded((b, t, d), 8)
+    w = 1 + 0.02 * torch.randn(d, generator=torch.Generator().manual_seed(9))
+    y = native.evidence_norm(x.to(DEV), v.to(DEV), g.to(DEV), w.to(DEV), mask.to(DEV)).cpu().numpy()
+    ref = O.evidence_norm(x.numpy(), v.float().numpy(), g.float().numpy(), w.numpy(), mask.numpy())
+    np.testing.assert_allclose(y, ref, rtol=2e-6, atol=2e-6)
+    a, c = seeded((b, t, d), 10), seeded((b, t, d), 11)
+    y = native.mean_norm(a.to(DEV), c.to(DEV), w.to(DEV)).cpu().numpy()
+    np.testing.assert_allclose(y, O.mean_norm(a.float().numpy(), c.float().numpy(), w.numpy()),
+                               rtol=2e-6, atol=2e-6)
+
+
+def test_swiglu_gate_model_size():
+    x = seeded((16, 101, 2 * 1536), 12, scale=2.0)
+    y = swiglu(x.to(DEV)).cpu().float().numpy()
+    assert within_bf16_ulp(y, O.swiglu(x.float().numpy()))
+    xg, g = seeded((16, 101, 3 * 384), 13), seeded((16, 101, 3), 14, scale=2.0)
+    y = gated_concat(xg.to(DEV), g.to(DEV)).cpu().float().numpy()
+    assert within_bf16_ulp(y, O.gated_concat(xg.float().numpy(), g.float().numpy()))
+    # FP32 gate against BF16 branches (the model's Linear output under autocast may be either)
+    y32 = gated_concat(xg.to(DEV), g.float().to(DEV)).cpu().float().numpy()
+    assert np.array_equal(y32, y)
+
+
+def test_controls_model_layout():
+    # [B, T, 1860] in_proj output of a dim-384 block: a and ddt are 12-wide views.
+    b, t, h = 16, 200, 12
+    p = seeded((b, t, 1860), 15, scale=4.0).to(DEV)
+    ddt, a = p[..., 1792:1804], p[..., 1804:1816]
+    bias = torch.full((h,), -4.0) + torch.randn(h, generator=torch.Generator().manual_seed(16))
+    adt, dt = mamba_controls(a, ddt, bias.to(DEV), 1e-4)
+    radt, rdt = O.mamba_controls(a.float().cpu().numpy(), ddt.float().cpu().numpy(), bias.numpy())
+    np.testing.assert_allclose(dt.cpu().numpy(), rdt, rtol=2e-6, atol=1e-7)
+    np.testing.assert_allclose(adt.cpu().numpy(), radt, rtol=2e-6, atol=1e-7)
+
+
+def test_masked_mean_and_end_gather_model_size():
+    b, t, d = 16, 101, 384
+    lengths = torch.tensor([101, 50, 1, 7] * 4)
+    x = seeded((b, t, d), 17)
+    y = native.masked_mean(x.to(DEV), lengths.to(DEV)).cpu().numpy()
+    np.testing.assert_allclose(y, O.masked_mean(x.float().numpy(), lengths.numpy()), rtol=1e-5, atol=1e-6)
+    e = native.end_gather(x.to(DEV), lengths.to(DEV)).cpu()
+    assert torch.equal(e, x[torch.arange(b), lengths - 1])
+
+
+def test_empty_inputs():
+    x = torch.zeros(0, 5, 8, dtype=BF, device=DEV)
+    lengths = torch.zeros(0, dtype=torch.int64, device=DEV)
+    assert reverse_valid(x, lengths).shape == x.shape
+    assert Pool4.apply(x, lengths).shape == (0, 2, 8)
+    assert native.rms(torch.zeros(0, 128, device=DEV), torch.ones(128, device=DEV)).shape == (0, 128)
+    assert swiglu(torch.zeros(0, 16, dtype=BF, device=DEV)).shape == (0, 8)
+
+
+def test_capture_in_cuda_graph_matches_eager():
+    b, t, d = 4, 64, 384
+    x = seeded((b, t, d), 18).to(DEV)
+    lengths = torch.tensor([64, 30, 1, 0], device=DEV)
+    w = torch.ones(d, device=DEV)
+
+    def step():
+        r = reverse_valid(x, lengths)
+        return native.mean_norm(r, x, w), Pool4.apply(r, lengths), swiglu(torch.cat((x, r), -1))
+
+    eager = step()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = step()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, c in zip(eager, captured):
+        assert torch.equal(a, c)

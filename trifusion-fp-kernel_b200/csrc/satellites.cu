@@ -1,0 +1,616 @@
+// Satellite operators around the recurrence: row norms, controls, length
+// masking and reversal, SwiGLU, branch gate, pooling and decoder reads.
+//
+// All are HBM-bound element or row passes. Design rules used throughout:
+//   * rows are contiguous; each warp (or thread) moves 16-byte vectors when the
+//     row size and the base pointers allow it, else 8-, 4- or 2-byte ones;
+//   * grids are sized to a few waves of the SM count and loop (grid-stride);
+//   * arithmetic is FP32, results are rounded once to the output type;
+//   * index and copy operators move raw bits (bit-exact by construction).
+// The reference formula each kernel follows is cited at the kernel.
+#include <cstdint>
+#include <cstdio>
+
+#include "../../include/trifusion_b200.h"
+#include "tf_common.cuh"
+#include "tf_host.cuh"
+
+namespace tf {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ float load_f(const T* p);
+template <>
+__device__ __forceinline__ float load_f<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float load_f<bf16>(const bf16* p) { return __bfloat162float(*p); }
+
+template <typename T>
+__device__ __forceinline__ void store_f(T* p, float v);
+template <>
+__device__ __forceinline__ void store_f<float>(float* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void store_f<bf16>(bf16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// 4 consecutive elements as FP32 (8- or 16-byte load; caller guarantees alignment).
+__device__ __forceinline__ float4 load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 load4(const bf16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void store4(bf16* p, float4 v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
+
+// IEEE sigmoid in FP32: 1 / (1 + e^-x), with expf and a correctly rounded divide.
+__device__ __forceinline__ float sigmoid_ieee(float x) { return 1.f / (1.f + expf(-x)); }
+
+int grid_for(int64_t work_items, int per_block) {
+  const int64_t blocks = (work_items + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  return static_cast<int>(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
+}
+
+bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+// ---------------------------------------------------------------------------
+// Row RMSNorm family (kernels/native.py:8-39 `_norm`; kernels/primitives.py:8-22
+// `_rms_fwd`). One warp per row:
+//   kMode 0 (rms):           y = x * rsqrt(mean(x^2) + eps) * w      (y type = x type)
+//   kMode 1 (evidence_norm): x' = x + a * 2 sigmoid(b) on rows whose mask is set,
+//                            0 elsewhere; y = rms(x') * w            (FP32 out)
+//   kMode 2 (mean_norm):     x' = (x + a) / 2; y = rms(x') * w       (FP32 out)
+// The row is read twice (sum of squares, then scale); the second read hits L1.
+// ---------------------------------------------------------------------------
+template <int kMode, typename TX, typename TA, typename TY, bool kVec4>
+__global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict__ x,
+                                                            const TA* __restrict__ a,
+                                                            const TA* __restrict__ b,
+                                                            const float* __restrict__ w,
+                                                            const uint8_t* __restrict__ mask,
+                                                            TY* __restrict__ y, int64_t rows,
+                                                            int width, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  auto value = [&](int64_t off) -> float {
+    float v = load_f(x + off);
+    if (kMode == 1) v = v + load_f(a + off) * (2.f * sigmoid_ieee(load_f(b + off)));
+    if (kMode == 2) v = (v + load_f(a + off)) * 0.5f;
+    return v;
+  };
+  auto value4 = [&](int64_t off) -> float4 {
+    float4 v = load4(x + off);
+    if (kMode == 1) {
+      const float4 av = load4(a + off), bv = load4(b + off);
+      v.x += av.x * (2.f * sigmoid_ieee(bv.x));
+      v.y += av.y * (2.f * sigmoid_ieee(bv.y));
+      v.z += av.z * (2.f * sigmoid_ieee(bv.z));
+      v.w += av.w * (2.f * sigmoid_ieee(bv.w));
+    }
+    if (kMode == 2) {
+      const float4 av = load4(a + off);
+      v = make_float4((v.x + av.x) * 0.5f, (v.y + av.y) * 0.5f, (v.z + av.z) * 0.5f,
+                      (v.w + av.w) * 0.5f);
+    }
+    return v;
+  };
+  for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t base = row * width;
+    const bool live = kMode != 1 || mask[row] != 0;
+    float ss = 0.f;
+    if (live) {
+      if (kVec4) {
+        for (int c = lane * 4; c < width; c += 128) {
+          const float4 v = value4(base + c);
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+      } else {
+        for (int c = lane; c < width; c += 32) {
+          const float v = value(base + c);
+          ss += v * v;
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / static_cast<float>(width) + eps);
+    if (kVec4) {
+      for (int c = lane * 4; c < width; c += 128) {
+        float4 v = live ? value4(base + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 wv = load4(w + c);
+        v = make_float4(v.x * r * wv.x, v.y * r * wv.y, v.z * r * wv.z, v.w * r * wv.w);
+        store4(y + base + c, v);
+      }
+    } else {
+      for (int c = lane; c < width; c += 32) {
+        const float v = live ? value(base + c) : 0.f;
+        store_f(y + base + c, v * r * w[c]);
+      }
+    }
+  }
+}
+
+template <int kMode, typename TX, typename TA, typename TY>
+int launch_row_norm(const void* x, const void* a, const void* b, const float* w,
+                    const uint8_t* mask, void* y, int64_t rows, int width, float eps,
+                    cudaStream_t s) {
+  const bool v4 = width % 4 == 0 && aligned(x, 4 * sizeof(TX)) && aligned(y, 4 * sizeof(TY)) &&
+                  aligned(w, 16) && (kMode == 0 || aligned(a, 4 * sizeof(TA))) &&
+                  (kMode != 1 || aligned(b, 4 * sizeof(TA)));
+  const int grid = grid_for(rows, kThreads / 32);
+  auto X = static_cast<const TX*>(x);
+  auto A = static_cast<const TA*>(a);
+  auto B = static_cast<const TA*>(b);
+  auto Y = static_cast<TY*>(y);
+  if (v4)
+    row_norm_kernel<kMode, TX, TA, TY, true><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps);
+  else
+    row_norm_kernel<kMode, TX, TA, TY, false><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps);
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Mamba controls (kernels/primitives.py:190-216 `_controls`, called from
+// kernels/buffers.py:82-101; the PyTorch form is mamba.py:58-63):
+//   A   = min(-(max(a, 0) + 1 / (1 - min(a, 0))), -floor)
+//   dt  = softplus(ddt + bias[h])   (identity above 20)
+//   out: adt = A * dt and dt, transposed from [B, T, H] to [B, H, T].
+// One thread per output element, t fastest, so the stores are coalesced; the
+// strided reads of the projection view are a few bytes per token.
+// ---------------------------------------------------------------------------
+template <typename TI>
+__global__ void __launch_bounds__(kThreads) controls_kernel(const TI* __restrict__ a,
+                                                            const TI* __restrict__ ddt,
+                                                            int64_t sab, int64_t sat,
+                                                            int64_t sdb, int64_t sdtt,
+                                                            const float* __restrict__ bias,
+                                                            float floor_, float* __restrict__ adt,
+                                                            float* __restrict__ dt, int B, int T,
+                                                            int H) {
+  const int64_t total = static_cast<int64_t>(B) * H * T;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int t = static_cast<int>(i % T);
+    const int64_t bh = i / T;
+    const int h = static_cast<int>(bh % H);
+    const int b = static_cast<int>(bh / H);
+    const float av = load_f(a + b * sab + t * sat + h);
+    const float dv = load_f(ddt + b * sdb + t * sdtt + h);
+    const float control = fminf(-(fmaxf(av, 0.f) + 1.f / (1.f - fminf(av, 0.f))), -floor_);
+    const float v = dv + bias[h];
+    const float step = v > 20.f ? v : log1pf(expf(v));
+    dt[i] = step;
+    adt[i] = control * step;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Raw-bit row operators. `V` is the vector type (uint4/uint2/uint32_t/uint16_t)
+// that divides the row size and both base pointers.
+// ---------------------------------------------------------------------------
+
+// Length mask (kernels/primitives.py:65-70 `_mask`, kernels/buffers.py:6-10;
+// masking.py:10-11): y[r] = x[r] where mask[r] != 0, else zero bits.
+template <typename V>
+__global__ void __launch_bounds__(kThreads) mask_rows_kernel(const V* __restrict__ x,
+                                                             const uint8_t* __restrict__ mask,
+                                                             V* __restrict__ y, int64_t rows,
+                                                             int64_t per_row) {
+  const int64_t total = rows * per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t r = i / per_row;
+    V v{};
+    if (mask[r]) v = x[i];
+    y[i] = v;
+  }
+}
+
+__device__ __forceinline__ int64_t clamp_len(int64_t len, int T) {
+  return len < 0 ? 0 : (len > T ? T : len);
+}
+
+// Valid-prefix reversal (kernels/primitives.py:40-47 `_reverse`;
+// kernels/__init__.py:43-54): y[b, t] = x[b, len-1-t] for t < len, else zero.
+// Lengths outside [0, T] are clamped to it.
+template <typename V>
+__global__ void __launch_bounds__(kThreads) reverse_valid_kernel(const V* __restrict__ x,
+                                                                 const int64_t* __restrict__ lengths,
+                                                                 V* __restrict__ y, int B, int T,
+                                                                 int64_t per_row) {
+  const int64_t total = static_cast<int64_t>(B) * T * per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t c = i % per_row;
+    const int64_t bt = i / per_row;
+    const int t = static_cast<int>(bt % T);
+    const int b = static_cast<int>(bt / T);
+    const int64_t len = clamp_len(lengths[b], T);
+    V v{};
+    if (t < len) v = x[(static_cast<int64_t>(b) * T + (len - 1 - t)) * per_row + c];
+    y[i] = v;
+  }
+}
+
+// Last valid row of every batch entry (decoder.py:63, `mf[arange(b), lengths-1]`):
+// y[b] = x[b, len-1]; like PyTorch indexing, len = 0 reads row T-1 (index -1).
+template <typename V>
+__global__ void __launch_bounds__(kThreads) end_gather_kernel(const V* __restrict__ x,
+                                                              const int64_t* __restrict__ lengths,
+                                                              V* __restrict__ y, int B, int T,
+                                                              int64_t per_row) {
+  const int64_t total = static_cast<int64_t>(B) * per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int b = static_cast<int>(i / per_row);
+    int64_t t = lengths[b] - 1;
+    if (t < 0) t += T;
+    if (t < 0) t = 0;
+    if (t >= T) t = T - 1;
+    y[i] = x[(static_cast<int64_t>(b) * T + t) * per_row + i % per_row];
+  }
+}
+
+int vector_bytes(int64_t row_bytes, const void* x, const void* y) {
+  for (int v : {16, 8, 4, 2})
+    if (row_bytes % v == 0 && aligned(x, v) && aligned(y, v)) return v;
+  return 1;
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU (kernels/primitives.py:25-37 `_swiglu`; kernels/__init__.py:30-40):
+// y[r, c] = silu(x[r, c]) * x[r, d + c], FP32 math, rounded to the input type.
+// ---------------------------------------------------------------------------
+template <typename T, bool kVec4>
+__global__ void __launch_bounds__(kThreads) swiglu_kernel(const T* __restrict__ x,
+                                                          T* __restrict__ y, int64_t rows,
+                                                          int d) {
+  const int step = kVec4 ? 4 : 1;
+  const int64_t per_row = d / step;
+  const int64_t total = rows * per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t r = i / per_row;
+    const int c = static_cast<int>(i % per_row) * step;
+    const T* src = x + r * 2 * d + c;
+    T* dst = y + r * d + c;
+    if (kVec4) {
+      const float4 g = load4(src), u = load4(src + d);
+      store4(dst, make_float4(g.x * sigmoid_ieee(g.x) * u.x, g.y * sigmoid_ieee(g.y) * u.y,
+                              g.z * sigmoid_ieee(g.z) * u.z, g.w * sigmoid_ieee(g.w) * u.w));
+    } else {
+      const float g = load_f(src), u = load_f(src + d);
+      store_f(dst, g * sigmoid_ieee(g) * u);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Branch gate (kernels/primitives.py:50-62 `_gate`; kernels/__init__.py:57-81):
+// x = [..., 3 * d] split in three branches, y[..., j, :] = x[..., j, :] * 2 sigmoid(g[..., j]).
+// ---------------------------------------------------------------------------
+template <typename T, typename TG, bool kVec4>
+__global__ void __launch_bounds__(kThreads) gated_concat_kernel(const T* __restrict__ x,
+                                                                const TG* __restrict__ gate,
+                                                                T* __restrict__ y, int64_t rows,
+                                                                int d) {
+  const int step = kVec4 ? 4 : 1;
+  const int64_t per_branch = d / step;
+  const int64_t total = rows * 3 * per_branch;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t branch_row = i / per_branch;  // r * 3 + j
+    const int c = static_cast<int>(i % per_branch) * step;
+    const float s = 2.f * sigmoid_ieee(load_f(gate + branch_row));
+    const int64_t off = branch_row * d + c;
+    if (kVec4) {
+      const float4 v = load4(x + off);
+      store4(y + off, make_float4(v.x * s, v.y * s, v.z * s, v.w * s));
+    } else {
+      store_f(y + off, load_f(x + off) * s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pool4 (kernels/primitives.py:90-113 `_pool4` forward; masking.py:59-69):
+// y[b, g] = (sum of x[b, 4g + k] over k < 4 with 4g + k < len) / max(min(len - 4g, 4), 1).
+// The sum runs in the reference's order (k = 0..3, FP32) and the divide is
+// IEEE, so the result equals the reference kernel's bit for bit.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kThreads) pool4_kernel(const T* __restrict__ x,
+                                                         const int64_t* __restrict__ lengths,
+                                                         T* __restrict__ y, int B, int T_, int LT,
+                                                         int D) {
+  const int64_t total = static_cast<int64_t>(B) * LT * D;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int c = static_cast<int>(i % D);
+    const int64_t bg = i / D;
+    const int g = static_cast<int>(bg % LT);
+    const int b = static_cast<int>(bg / LT);
+    const int64_t len = clamp_len(lengths[b], T_);
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t src = 4 * static_cast<int64_t>(g) + k;
+      if (src < len) acc += load_f(x + (static_cast<int64_t>(b) * T_ + src) * D + c);
+    }
+    int64_t count = len - 4 * static_cast<int64_t>(g);
+    count = count > 4 ? 4 : (count < 1 ? 1 : count);
+    store_f(y + i, acc / static_cast<float>(count));
+  }
+}
+
+// Masked time mean (decoder.py:60-62): y[b, c] = sum_{t < len} x[b, t, c] / len, FP32.
+// Sums run in time order in FP32; len = 0 gives 0/0 as the reference does.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) masked_mean_kernel(const T* __restrict__ x,
+                                                               const int64_t* __restrict__ lengths,
+                                                               float* __restrict__ y, int B, int T_,
+                                                               int D) {
+  const int64_t total = static_cast<int64_t>(B) * D;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int c = static_cast<int>(i % D);
+    const int b = static_cast<int>(i / D);
+    const int64_t raw = lengths[b];
+    const int64_t len = clamp_len(raw, T_);
+    const T* p = x + static_cast<int64_t>(b) * T_ * D + c;
+    float acc = 0.f;
+    for (int64_t t = 0; t < len; ++t) acc += load_f(p + t * D);
+    y[i] = acc / static_cast<float>(raw);
+  }
+}
+
+}  // namespace
+
+int launch_mask_rows(const void* x, const uint8_t* mask, void* y, int64_t rows, int64_t row_bytes,
+                     cudaStream_t s) {
+  const int vb = vector_bytes(row_bytes, x, y);
+  const int64_t per_row = row_bytes / vb;
+  const int grid = grid_for(rows * per_row, kThreads);
+  switch (vb) {
+    case 16: mask_rows_kernel<uint4><<<grid, kThreads, 0, s>>>(static_cast<const uint4*>(x), mask, static_cast<uint4*>(y), rows, per_row); break;
+    case 8: mask_rows_kernel<uint2><<<grid, kThreads, 0, s>>>(static_cast<const uint2*>(x), mask, static_cast<uint2*>(y), rows, per_row); break;
+    case 4: mask_rows_kernel<uint32_t><<<grid, kThreads, 0, s>>>(static_cast<const uint32_t*>(x), mask, static_cast<uint32_t*>(y), rows, per_row); break;
+    case 2: mask_rows_kernel<uint16_t><<<grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), mask, static_cast<uint16_t*>(y), rows, per_row); break;
+    default: mask_rows_kernel<uint8_t><<<grid, kThreads, 0, s>>>(static_cast<const uint8_t*>(x), mask, static_cast<uint8_t*>(y), rows, per_row); break;
+  }
+  return launch_status();
+}
+
+int launch_reverse_valid(const void* x, const int64_t* lengths, void* y, int B, int T,
+                         int64_t row_bytes, cudaStream_t s) {
+  const int vb = vector_bytes(row_bytes, x, y);
+  const int64_t per_row = row_bytes / vb;
+  const int grid = grid_for(static_cast<int64_t>(B) * T * per_row, kThreads);
+  switch (vb) {
+    case 16: reverse_valid_kernel<uint4><<<grid, kThreads, 0, s>>>(static_cast<const uint4*>(x), lengths, static_cast<uint4*>(y), B, T, per_row); break;
+    case 8: reverse_valid_kernel<uint2><<<grid, kThreads, 0, s>>>(static_cast<const uint2*>(x), lengths, static_cast<uint2*>(y), B, T, per_row); break;
+    case 4: reverse_valid_kernel<uint32_t><<<grid, kThreads, 0, s>>>(static_cast<const uint32_t*>(x), lengths, static_cast<uint32_t*>(y), B, T, per_row); break;
+    case 2: reverse_valid_kernel<uint16_t><<<grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), lengths, static_cast<uint16_t*>(y), B, T, per_row); break;
+    default: reverse_valid_kernel<uint8_t><<<grid, kThreads, 0, s>>>(static_cast<const uint8_t*>(x), lengths, static_cast<uint8_t*>(y), B, T, per_row); break;
+  }
+  return launch_status();
+}
+
+int launch_end_gather(const void* x, const int64_t* lengths, void* y, int B, int T,
+                      int64_t row_bytes, cudaStream_t s) {
+  const int vb = vector_bytes(row_bytes, x, y);
+  const int64_t per_row = row_bytes / vb;
+  const int grid = grid_for(static_cast<int64_t>(B) * per_row, kThreads);
+  switch (vb) {
+    case 16: end_gather_kernel<uint4><<<grid, kThreads, 0, s>>>(static_cast<const uint4*>(x), lengths, static_cast<uint4*>(y), B, T, per_row); break;
+    case 8: end_gather_kernel<uint2><<<grid, kThreads, 0, s>>>(static_cast<const uint2*>(x), lengths, static_cast<uint2*>(y), B, T, per_row); break;
+    case 4: end_gather_kernel<uint32_t><<<grid, kThreads, 0, s>>>(static_cast<const uint32_t*>(x), lengths, static_cast<uint32_t*>(y), B, T, per_row); break;
+    case 2: end_gather_kernel<uint16_t><<<grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), lengths, static_cast<uint16_t*>(y), B, T, per_row); break;
+    default: end_gather_kernel<uint8_t><<<grid, kThreads, 0, s>>>(static_cast<const uint8_t*>(x), lengths, static_cast<uint8_t*>(y), B, T, per_row); break;
+  }
+  return launch_status();
+}
+
+template <typename T>
+int launch_swiglu(const void* x, void* y, int64_t rows, int d, cudaStream_t s) {
+  const bool v4 = d % 4 == 0 && aligned(x, 4 * sizeof(T)) && aligned(y, 4 * sizeof(T));
+  const int64_t items = rows * (v4 ? d / 4 : d);
+  const int grid = grid_for(items, kThreads);
+  if (v4)
+    swiglu_kernel<T, true><<<grid, kThreads, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(y), rows, d);
+  else
+    swiglu_kernel<T, false><<<grid, kThreads, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(y), rows, d);
+  return launch_status();
+}
+
+template <typename T, typename TG>
+int launch_gated_concat(const void* x, const void* g, void* y, int64_t rows, int d, cudaStream_t s) {
+  const bool v4 = d % 4 == 0 && aligned(x, 4 * sizeof(T)) && aligned(y, 4 * sizeof(T));
+  const int64_t items = rows * 3 * (v4 ? d / 4 : d);
+  const int grid = grid_for(items, kThreads);
+  if (v4)
+    gated_concat_kernel<T, TG, true><<<grid, kThreads, 0, s>>>(static_cast<const T*>(x), static_cast<const TG*>(g), static_cast<T*>(y), rows, d);
+  else
+    gated_concat_kernel<T, TG, false><<<grid, kThreads, 0, s>>>(static_cast<const T*>(x), static_cast<const TG*>(g), static_cast<T*>(y), rows, d);
+  return launch_status();
+}
+
+}  // namespace tf
+
+// ===========================================================================
+// C ABI (declarations and reference citations in include/trifusion_b200.h)
+// ===========================================================================
+namespace {
+
+bool valid_dtype(int d) { return d == TF_F32 || d == TF_BF16; }
+
+}  // namespace
+
+extern "C" {
+
+int tf_rms_fwd(const void* x, int dtype, const float* w, void* y, int64_t rows, int width,
+               float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !w || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == TF_F32)
+    return tf::launch_row_norm<0, float, float, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+  return tf::launch_row_norm<0, tf::bf16, tf::bf16, tf::bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+}
+
+int tf_evidence_norm_fwd(const void* x, int x_dtype, const void* value, const void* gate,
+                         int vg_dtype, const float* w, const uint8_t* mask, float* y,
+                         int64_t rows, int width, float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(x_dtype) || !valid_dtype(vg_dtype)) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !value || !gate || !w || !mask || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  if (x_dtype == TF_F32 && vg_dtype == TF_F32)
+    return tf::launch_row_norm<1, float, float, float>(x, value, gate, w, mask, y, rows, width, eps, s);
+  if (x_dtype == TF_F32)
+    return tf::launch_row_norm<1, float, bf16, float>(x, value, gate, w, mask, y, rows, width, eps, s);
+  if (vg_dtype == TF_F32)
+    return tf::launch_row_norm<1, bf16, float, float>(x, value, gate, w, mask, y, rows, width, eps, s);
+  return tf::launch_row_norm<1, bf16, bf16, float>(x, value, gate, w, mask, y, rows, width, eps, s);
+}
+
+int tf_mean_norm_fwd(const void* a, const void* b, int dtype, const float* w, float* y,
+                     int64_t rows, int width, float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!a || !b || !w || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == TF_F32)
+    return tf::launch_row_norm<2, float, float, float>(a, b, nullptr, w, nullptr, y, rows, width, eps, s);
+  return tf::launch_row_norm<2, tf::bf16, tf::bf16, float>(a, b, nullptr, w, nullptr, y, rows, width, eps, s);
+}
+
+int tf_mamba_controls_fwd(const void* a, const void* ddt, int dtype, const int64_t* strides,
+                          const float* dt_bias, float a_floor, float* adt, float* dt, int batch,
+                          int seqlen, int heads, void* stream) {
+  if (batch < 0 || seqlen < 0 || heads < 0 || !valid_dtype(dtype) || !strides) return TF_ERR_ARG;
+  if (batch == 0 || seqlen == 0 || heads == 0) return TF_OK;
+  if (!a || !ddt || !dt_bias || !adt || !dt) return TF_ERR_ARG;
+  if (strides[2] != 1 || strides[5] != 1) return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = tf::grid_for(static_cast<int64_t>(batch) * seqlen * heads, tf::kThreads);
+  if (dtype == TF_F32)
+    tf::controls_kernel<float><<<grid, tf::kThreads, 0, s>>>(
+        static_cast<const float*>(a), static_cast<const float*>(ddt), strides[0], strides[1],
+        strides[3], strides[4], dt_bias, a_floor, adt, dt, batch, seqlen, heads);
+  else
+    tf::controls_kernel<tf::bf16><<<grid, tf::kThreads, 0, s>>>(
+        static_cast<const tf::bf16*>(a), static_cast<const tf::bf16*>(ddt), strides[0], strides[1],
+        strides[3], strides[4], dt_bias, a_floor, adt, dt, batch, seqlen, heads);
+  return tf::launch_status();
+}
+
+int tf_mask_rows_fwd(const void* x, const uint8_t* mask, void* y, int64_t rows,
+                     int64_t row_bytes, void* stream) {
+  if (rows < 0 || row_bytes < 0) return TF_ERR_ARG;
+  if (rows == 0 || row_bytes == 0) return TF_OK;
+  if (!x || !mask || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  return tf::launch_mask_rows(x, mask, y, rows, row_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int tf_reverse_valid_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
+                         int64_t row_bytes, void* stream) {
+  if (batch < 0 || seqlen < 0 || row_bytes < 0) return TF_ERR_ARG;
+  if (batch == 0 || seqlen == 0 || row_bytes == 0) return TF_OK;
+  if (!x || !lengths || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  return tf::launch_reverse_valid(x, lengths, y, batch, seqlen, row_bytes,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+int tf_swiglu_fwd(const void* x, int dtype, void* y, int64_t rows, int d, void* stream) {
+  if (rows < 0 || d < 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (rows == 0 || d == 0) return TF_OK;
+  if (!x || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == TF_F32) return tf::launch_swiglu<float>(x, y, rows, d, s);
+  return tf::launch_swiglu<tf::bf16>(x, y, rows, d, s);
+}
+
+int tf_gated_concat_fwd(const void* x, int dtype, const void* gate, int gate_dtype, void* y,
+                        int64_t rows, int d, void* stream) {
+  if (rows < 0 || d < 0 || !valid_dtype(dtype) || !valid_dtype(gate_dtype)) return TF_ERR_ARG;
+  if (rows == 0 || d == 0) return TF_OK;
+  if (!x || !gate || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  if (dtype == TF_F32 && gate_dtype == TF_F32) return tf::launch_gated_concat<float, float>(x, gate, y, rows, d, s);
+  if (dtype == TF_F32) return tf::launch_gated_concat<float, bf16>(x, gate, y, rows, d, s);
+  if (gate_dtype == TF_F32) return tf::launch_gated_concat<bf16, float>(x, gate, y, rows, d, s);
+  return tf::launch_gated_concat<bf16, bf16>(x, gate, y, rows, d, s);
+}
+
+int tf_pool4_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int batch, int seqlen,
+                 int width, void* stream) {
+  if (batch < 0 || seqlen < 0 || width < 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (batch == 0 || seqlen == 0 || width == 0) return TF_OK;
+  if (!x || !lengths || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int lt = (seqlen + 3) / 4;
+  const int grid = tf::grid_for(static_cast<int64_t>(batch) * lt * width, tf::kThreads);
+  if (dtype == TF_F32)
+    tf::pool4_kernel<float><<<grid, tf::kThreads, 0, s>>>(static_cast<const float*>(x), lengths,
+                                                          static_cast<float*>(y), batch, seqlen, lt, width);
+  else
+    tf::pool4_kernel<tf::bf16><<<grid, tf::kThreads, 0, s>>>(static_cast<const tf::bf16*>(x), lengths,
+                                                             static_cast<tf::bf16*>(y), batch, seqlen, lt, width);
+  return tf::launch_status();
+}
+
+int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* y, int batch,
+                       int seqlen, int width, void* stream) {
+  if (batch < 0 || seqlen < 0 || width < 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (batch == 0 || width == 0) return TF_OK;
+  if (!x || !lengths || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = tf::grid_for(static_cast<int64_t>(batch) * width, tf::kThreads);
+  if (dtype == TF_F32)
+    tf::masked_mean_kernel<float><<<grid, tf::kThreads, 0, s>>>(static_cast<const float*>(x), lengths, y,
+                                                                batch, seqlen, width);
+  else
+    tf::masked_mean_kernel<tf::bf16><<<grid, tf::kThreads, 0, s>>>(static_cast<const tf::bf16*>(x), lengths,
+                                                                   y, batch, seqlen, width);
+  return tf::launch_status();
+}
+
+int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
+                      int64_t row_bytes, void* stream) {
+  if (batch < 0 || seqlen <= 0 || row_bytes < 0) return batch == 0 ? TF_OK : TF_ERR_ARG;
+  if (batch == 0 || row_bytes == 0) return TF_OK;
+  if (!x || !lengths || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  return tf::launch_end_gather(x, lengths, y, batch, seqlen, row_bytes,
+                               static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

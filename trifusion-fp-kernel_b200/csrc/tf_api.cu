@@ -7,6 +7,7 @@
 
 #include "../../include/trifusion_b200.h"
 #include "recurrence.cuh"
+#include "tf_host.cuh"
 
 namespace tf {
 
@@ -32,6 +33,19 @@ int check_device() {
     g_arch_ok[dev] = (major == 10 && minor == 0) ? 1 : 2;
   }
   return g_arch_ok[dev] == 1 ? TF_OK : TF_ERR_DEVICE;
+}
+
+int g_sm_count[kMaxDevices] = {0};
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sm_count[dev] = n > 0 ? n : 148;
+  }
+  return g_sm_count[dev];
 }
 
 int launch_status() {

@@ -20,6 +20,7 @@ _p = ctypes.c_void_p
 _i = ctypes.c_int
 _f = ctypes.c_float
 _z = ctypes.c_size_t
+_q = ctypes.c_int64
 
 # name -> argtypes; every function returns int unless listed in _RESTYPES.
 SIGNATURES = {
@@ -34,6 +35,18 @@ SIGNATURES = {
                                 _i, _i, _i, _i, _p, _p, _f, _p, _p, _z, _p],
     "tf_mamba_recurrence_fwd_static": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
                                        _i, _i, _i, _i, _p, _p, _f, _p, _p],
+    # Satellite operators (argument order of include/trifusion_b200.h).
+    "tf_rms_fwd": [_p, _i, _p, _p, _q, _i, _f, _p],
+    "tf_evidence_norm_fwd": [_p, _i, _p, _p, _i, _p, _p, _p, _q, _i, _f, _p],
+    "tf_mean_norm_fwd": [_p, _p, _i, _p, _p, _q, _i, _f, _p],
+    "tf_mamba_controls_fwd": [_p, _p, _i, _p, _p, _f, _p, _p, _i, _i, _i, _p],
+    "tf_mask_rows_fwd": [_p, _p, _p, _q, _q, _p],
+    "tf_reverse_valid_fwd": [_p, _p, _p, _i, _i, _q, _p],
+    "tf_swiglu_fwd": [_p, _i, _p, _q, _i, _p],
+    "tf_gated_concat_fwd": [_p, _i, _p, _i, _p, _q, _i, _p],
+    "tf_pool4_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
+    "tf_masked_mean_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
+    "tf_end_gather_fwd": [_p, _p, _p, _i, _i, _q, _p],
 }
 _RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p,
              "tf_recurrence_workspace_size": ctypes.c_size_t}
@@ -74,6 +87,34 @@ def check(status):
 def int64_array(values):
     values = list(values)
     return (ctypes.c_int64 * len(values))(*values)
+
+
+def dtype_code(x, op):
+    """TF_F32 / TF_BF16 for a tensor's dtype; other dtypes are rejected."""
+    import torch
+
+    if x.dtype == torch.float32:
+        return TF_F32
+    if x.dtype == torch.bfloat16:
+        return TF_BF16
+    raise TypeError(f"{op}: expected float32 or bfloat16, got {x.dtype}")
+
+
+def require_cuda(op, *tensors):
+    """All tensors on one CUDA device (there is no CPU path)."""
+    dev = tensors[0].device
+    if dev.type != "cuda" or any(t.device != dev for t in tensors):
+        raise RuntimeError(f"{op}: all tensors must be CUDA tensors on one device")
+    return dev
+
+
+def launch(fn, device, *args):
+    """Call a C-ABI entry point on `device`'s current stream and check its status."""
+    import torch
+
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        check(getattr(lib(), fn)(*args, stream))
 
 
 _workspaces = {}

@@ -1,0 +1,64 @@
+"""Buffer operators on B200 — drop-in for ``trifusion_l4.kernels.buffers``
+(reference ``kernels/buffers.py``): length mask, Pool4 and the Mamba controls.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+
+def mask_buffer(x, mask):
+    """Rows of ``x`` where ``mask`` ([B, T] bool) is False become zero; the
+    others are copied bit for bit (reference ``buffers.py:6-10``)."""
+    x = x.contiguous()
+    dev = _lib.require_cuda("mask_buffer", x, mask)
+    rows = mask.numel()
+    if rows == 0 or x.numel() % rows:
+        if x.numel() == 0:
+            return torch.empty_like(x)
+        raise ValueError("mask_buffer: mask must have one entry per row of x")
+    m = mask.contiguous().to(torch.uint8)
+    y = torch.empty_like(x)
+    row_bytes = x.numel() // rows * x.element_size()
+    _lib.launch("tf_mask_rows_fwd", dev, x.data_ptr(), m.data_ptr(), y.data_ptr(), rows, row_bytes)
+    return y
+
+
+class Pool4:
+    """Mean over groups of 4 valid frames (reference ``buffers.py:35-43``)."""
+
+    @staticmethod
+    def apply(x, lengths):
+        x = x.contiguous()
+        dev = _lib.require_cuda("Pool4", x, lengths)
+        b, t, d = x.shape
+        lengths = lengths.to(torch.int64).contiguous()
+        y = x.new_empty((b, (t + 3) // 4, d))
+        _lib.launch("tf_pool4_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "Pool4"),
+                    lengths.data_ptr(), y.data_ptr(), b, t, d)
+        return y
+
+
+def mamba_controls(a, dt, bias, floor):
+    """``adt, dt`` as ``[B, H, T]`` FP32 from the ``[B, T, H]`` projection views
+    (reference ``buffers.py:82-101``)."""
+    dev = _lib.require_cuda("mamba_controls", a, dt, bias)
+    if dt.dtype != a.dtype:
+        dt = dt.to(a.dtype)
+    if a.stride(-1) != 1:
+        a = a.contiguous()
+    if dt.stride(-1) != 1:
+        dt = dt.contiguous()
+    b, t, h = a.shape
+    if tuple(dt.shape) != (b, t, h):
+        raise ValueError("mamba_controls: a and dt must have the same [B, T, H] shape")
+    bias = bias.detach().float().contiguous()
+    oa = torch.empty((b, h, t), device=dev, dtype=torch.float32)
+    od = torch.empty_like(oa)
+    strides = _lib.int64_array([*a.stride(), *dt.stride()])
+    _lib.launch("tf_mamba_controls_fwd", dev, a.data_ptr(), dt.data_ptr(),
+                _lib.dtype_code(a, "mamba_controls"), strides, bias.data_ptr(), float(floor),
+                oa.data_ptr(), od.data_ptr(), b, t, h)
+    return oa, od

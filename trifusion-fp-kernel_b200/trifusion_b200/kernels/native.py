@@ -1,0 +1,103 @@
+"""Row-norm and decoder-read operators on B200 — drop-in for
+``trifusion_l4.kernels.native`` (reference ``kernels/native.py``).
+
+Every function launches a kernel of ``libtrifusion_b200.so`` on the current
+stream (FP32 statistics, one rounding to the output type). Inputs are made
+contiguous first, as the reference wrappers do.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+
+def _rows(x):
+    d = x.shape[-1]
+    return (x.numel() // d if d else 0), d
+
+
+def _weight(weight, d, op):
+    w = weight.detach().float().contiguous()
+    if w.numel() != d:
+        raise ValueError(f"{op}: weight has {w.numel()} elements, rows have {d}")
+    return w
+
+
+def rms(x, weight, eps=1e-5):
+    """``x * rsqrt(mean(x^2) + eps) * weight``; output dtype = ``x.dtype``
+    (reference ``native.py:69-70``)."""
+    x = x.contiguous()
+    dev = _lib.require_cuda("rms", x, weight)
+    code = _lib.dtype_code(x, "rms")
+    rows, d = _rows(x)
+    w = _weight(weight, d, "rms")
+    y = torch.empty_like(x)
+    _lib.launch("tf_rms_fwd", dev, x.data_ptr(), code, w.data_ptr(), y.data_ptr(), rows, d,
+                float(eps))
+    return y
+
+
+def evidence_norm(x, value, gate, weight, mask, eps=1e-5):
+    """RMSNorm of ``x + value * 2 sigmoid(gate)`` on rows where ``mask`` is set
+    (zero rows elsewhere); FP32 output (reference ``native.py:73-74``)."""
+    x, value, gate = x.contiguous(), value.contiguous(), gate.contiguous()
+    if value.dtype != gate.dtype:
+        gate = gate.to(value.dtype)
+    dev = _lib.require_cuda("evidence_norm", x, value, gate, weight, mask)
+    rows, d = _rows(x)
+    if value.shape != x.shape or gate.shape != x.shape or mask.numel() != rows:
+        raise ValueError("evidence_norm: value/gate must match x and mask must have one entry per row")
+    w = _weight(weight, d, "evidence_norm")
+    m = mask.contiguous().to(torch.uint8)
+    y = torch.empty(x.shape, device=dev, dtype=torch.float32)
+    _lib.launch("tf_evidence_norm_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "evidence_norm"),
+                value.data_ptr(), gate.data_ptr(), _lib.dtype_code(value, "evidence_norm"),
+                w.data_ptr(), m.data_ptr(), y.data_ptr(), rows, d, float(eps))
+    return y
+
+
+def mean_norm(a, b, weight, eps=1e-5):
+    """RMSNorm of ``(a + b) / 2``; FP32 output (reference ``native.py:77-78``)."""
+    a, b = a.contiguous(), b.contiguous()
+    if b.dtype != a.dtype:
+        b = b.to(a.dtype)
+    dev = _lib.require_cuda("mean_norm", a, b, weight)
+    if a.shape != b.shape:
+        raise ValueError("mean_norm: a and b must have the same shape")
+    rows, d = _rows(a)
+    w = _weight(weight, d, "mean_norm")
+    y = torch.empty(a.shape, device=dev, dtype=torch.float32)
+    _lib.launch("tf_mean_norm_fwd", dev, a.data_ptr(), b.data_ptr(), _lib.dtype_code(a, "mean_norm"),
+                w.data_ptr(), y.data_ptr(), rows, d, float(eps))
+    return y
+
+
+def masked_mean(x, lengths):
+    """``(x.float() * mask).sum(1) / lengths`` over ``[B, T, D]`` → FP32 ``[B, D]``
+    (the decoder's global feature, reference ``decoder.py:60-62``)."""
+    x = x.contiguous()
+    dev = _lib.require_cuda("masked_mean", x, lengths)
+    b, t, d = x.shape
+    lengths = lengths.to(torch.int64).contiguous()
+    y = torch.empty((b, d), device=dev, dtype=torch.float32)
+    _lib.launch("tf_masked_mean_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "masked_mean"),
+                lengths.data_ptr(), y.data_ptr(), b, t, d)
+    return y
+
+
+def end_gather(x, lengths):
+    """``x[arange(B), lengths - 1]`` — the last valid row of each batch entry
+    (reference ``decoder.py:63``); bit-exact."""
+    x = x.contiguous()
+    dev = _lib.require_cuda("end_gather", x, lengths)
+    b, t = x.shape[:2]
+    lengths = lengths.to(torch.int64).contiguous()
+    y = torch.empty((b, *x.shape[2:]), device=dev, dtype=x.dtype)
+    row_bytes = x[0, 0].numel() * x.element_size() if t else 0
+    if b and t == 0:
+        raise IndexError("end_gather: time dimension is empty")
+    _lib.launch("tf_end_gather_fwd", dev, x.data_ptr(), lengths.data_ptr(), y.data_ptr(), b, t,
+                row_bytes)
+    return y

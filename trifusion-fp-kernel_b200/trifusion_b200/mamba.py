@@ -1,0 +1,90 @@
+"""Frozen Mamba-3 SISO layer with the reference's parameter layout (reference
+``mamba.py``), running the B200 recurrence.
+
+Optimized path (``fused_recurrence=True``, what ``load_student`` sets): one
+cuBLAS GEMM (``in_proj``), the controls kernel, ONE recurrence launch that
+also applies the C/B RMSNorm of the raw q/k rows and the length mask, and one
+cuBLAS GEMM (``out_proj``). With ``fused_recurrence=False`` the norms and the
+mask run as separate kernels around ``fused_mamba`` (the reference's
+unfused arrangement); ``backend="reference"`` evaluates the norms and controls
+with the reference's PyTorch formulas.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .kernels import RMSNorm
+
+
+class Mamba3Inference(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        self.d_inner = config.dim * 2
+        self.nheads = self.d_inner // 64
+        self.headdim = 64
+        self.d_state = config.state_dim
+        self.num_bc_heads = 1
+        self.num_rope_angles = self.d_state // 4
+        self.A_floor = 1e-4
+        self.chunk_size = 64
+        self.backend = config.backend
+        width = 2 * self.d_inner + 2 * self.d_state + 3 * self.nheads + self.num_rope_angles
+        self.in_proj = nn.Linear(config.dim, width, bias=False)
+        self.out_proj = nn.Linear(self.d_inner, config.dim, bias=False)
+        self.dt_bias = nn.Parameter(torch.full((self.nheads,), -4.0))
+        self.B_bias = nn.Parameter(torch.ones(self.nheads, 1, self.d_state))
+        self.C_bias = nn.Parameter(torch.ones_like(self.B_bias))
+        self.D = nn.Parameter(torch.ones(self.nheads))
+        self.B_norm = RMSNorm(self.d_state, backend=config.backend)
+        self.C_norm = RMSNorm(self.d_state, backend=config.backend)
+        self.fused_recurrence = False
+
+    def _split(self, p):
+        n, h, e = self.d_state, self.nheads, self.d_inner
+        return p.split([e, e, n, n, h, h, h, self.num_rope_angles], -1)
+
+    def _controls(self, a, ddt):
+        if self.backend == "reference":
+            af = a.float()
+            decay = -(af.clamp(min=0) + 1 / (1 - af.clamp(max=0))).clamp(min=self.A_floor)
+            dt = F.softplus(ddt.float() + self.dt_bias)
+            return (decay * dt).transpose(1, 2).contiguous(), dt.transpose(1, 2).contiguous()
+        from .kernels.buffers import mamba_controls
+
+        return mamba_controls(a, ddt, self.dt_bias, self.A_floor)
+
+    def forward(self, u, lengths=None):
+        """``u`` [B, T, dim] → [B, T, dim]. With ``lengths`` ([B] int64), rows at
+        or past each length come out zero (the block's length mask)."""
+        b, t, _ = u.shape
+        p = self.in_proj(u)
+        z, v, k, q, ddt, a, trap, angles = self._split(p)
+        adt, dt = self._controls(a, ddt)
+        angles = angles.unsqueeze(2).expand(b, t, self.nheads, self.num_rope_angles)
+        heads = (b, t, self.nheads, self.headdim)
+        q = q.reshape(b, t, 1, self.d_state)
+        k = k.reshape(b, t, 1, self.d_state)
+        if self.fused_recurrence and self.backend != "reference":
+            from .mamba_fused import fused_recurrence
+
+            y = fused_recurrence(q, k, v.reshape(heads), adt, dt, trap.transpose(1, 2),
+                                 self.C_bias[:, 0], self.B_bias[:, 0], angles, self.D,
+                                 z.reshape(heads), q_norm=self.C_norm.weight,
+                                 k_norm=self.B_norm.weight, lengths=lengths, eps=self.C_norm.eps)
+        else:
+            from .mamba_fused import fused_mamba
+
+            y = fused_mamba(self.C_norm(q), self.B_norm(k), v.reshape(heads), adt, dt,
+                            trap.transpose(1, 2), self.C_bias[:, 0], self.B_bias[:, 0], angles,
+                            self.D, z.reshape(heads))
+            if lengths is not None:
+                from .masking import masked, time_mask
+
+                y = masked(y.reshape(b, t, -1), time_mask(lengths, t))
+        y = y.reshape(b, t, self.d_inner)
+        if not torch.is_autocast_enabled(y.device.type):
+            y = y.to(self.out_proj.weight.dtype)
+        return self.out_proj(y)

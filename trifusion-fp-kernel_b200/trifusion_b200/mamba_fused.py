@@ -21,10 +21,13 @@ def _prep(q, k, v, adt, dt, trap, qb, kb, angles, d, z):
     r = angles.shape[-1]
     if n != 128 or p != 64 or r != 32:  # mamba_fused.py:159-160
         raise ValueError(_lib.SHAPE_MESSAGE)
-    named = dict(q=q, k=k, v=v, angles=angles, z=z)
-    for name, x in named.items():
-        if x.dtype != torch.bfloat16:
-            raise TypeError(f"fused_mamba: {name} must be bfloat16, got {x.dtype}")
+    # The kernel's operands are BF16 (docs/api.md:61-69); FP32/FP16 inputs are
+    # rounded to BF16 once, here.
+    for x in (q, k, v, angles, z):
+        if not x.is_floating_point():
+            raise TypeError(f"fused_mamba: expected bfloat16 tensors, got {x.dtype}")
+    q, k, v, angles, z = (x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+                          for x in (q, k, v, angles, z))
     if q.shape != k.shape or q.shape[:2] != (b, t) or q.dim() != 4:
         raise ValueError("fused_mamba: q and k must be [B,T,Hq,128] matching v")
     if z.shape != v.shape or angles.shape[:3] != (b, t, h):

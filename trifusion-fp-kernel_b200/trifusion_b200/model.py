@@ -1,0 +1,250 @@
+"""TriFusion-FP v3 student with the reference's parameter layout (reference
+``model.py``), running on the B200 kernels.
+
+Parameter names, shapes and the checkpoint format are the reference's, so its
+checkpoints load unchanged (``runtime.load_student``). The optimized backend
+(``"l4"``, the name the reference's checkpoints carry) runs these operators on
+``libtrifusion_b200.so``: the length mask, the row norms (pre/local/branch/FFN
+norms, evidence norm, bidirectional mean norm), Pool4, the fused Mamba-3
+recurrence (with its B/C norms, controls and length mask), the valid-prefix
+reversal, the branch gate and SwiGLU. GEMMs and convolutions run on
+cuBLAS/cuDNN; attention on PyTorch's SDPA in FP32; the depthwise merge
+convolutions, rotary table application and grid interpolation are PyTorch ops.
+``backend="reference"`` evaluates the reference's PyTorch formulas instead.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .attention import masked_attention
+from .front import Frontend
+from .kernels import RMSNorm, gated_concat, reverse_valid, swiglu
+from .masking import Grids, masked
+
+
+@dataclass
+class ModelConfig:
+    """The reference's configuration record (``model.py:14-34``); every field is
+    kept so that saved ``model_config`` dictionaries load unchanged."""
+
+    dim: int = 1024
+    depth: int = 16
+    ffn_dim: int = 2816
+    heads: int = 16
+    state_dim: int = 128
+    evidence_rank: int = 64
+    dropout: float = 0.1
+    backend: str = "l4"
+    checkpoint_blocks: bool = False
+    checkpoint_frontend: bool = False
+    channels_last: bool = False
+    buffer_fusion: bool = True
+    native_kernels: bool = True
+    mamba_packed: bool = True
+    paired_mamba: bool = False
+    mamba_parallel_bwd: bool = True
+    mamba_fast_launch: bool = True
+    paired_mamba_grid_limit: int = 64
+
+
+def mamba_factory(config):
+    from .mamba import Mamba3Inference
+
+    return Mamba3Inference(config)
+
+
+def rope(x, cos, sin):
+    """Rotate adjacent (even, odd) pairs of the last dim by the table angles."""
+    d = x.shape[-1]
+    even, odd = x.float().unflatten(-1, (d // 2, 2)).unbind(-1)
+    return torch.stack((even * cos - odd * sin, even * sin + odd * cos), -1).flatten(-2).to(x.dtype)
+
+
+def _mask_rows(x, mask, optimized):
+    if optimized:
+        from .kernels.buffers import mask_buffer
+
+        return mask_buffer(x, mask)
+    return masked(x, mask)
+
+
+def _depthwise(x, conv, mask):
+    """Depthwise Conv1d over time ([B, T, C] layout) with bias, zero past each
+    length (the reference's ``depthwise_masked``)."""
+    dtype = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
+    y = F.conv1d(x.to(dtype).transpose(1, 2), conv.weight.to(dtype), conv.bias.to(dtype),
+                 padding=conv.padding, groups=conv.groups)
+    return masked(y.transpose(1, 2), mask)
+
+
+class LocalCNN(nn.Module):
+    """GLU up-projection, depthwise conv (k=7), RMSNorm, SiLU, out-projection."""
+
+    def __init__(self, c):
+        super().__init__()
+        self.backend = c.backend
+        self.buffer_fusion = c.buffer_fusion
+        self.native_kernels = c.native_kernels
+        self.up = nn.Linear(c.dim, 2 * c.dim, bias=False)
+        self.dw = nn.Conv1d(c.dim, c.dim, 7, padding=3, groups=c.dim)
+        self.norm = RMSNorm(c.dim, backend=c.backend)
+        self.out = nn.Linear(c.dim, c.dim, bias=False)
+
+    def forward(self, x, mask, lengths):
+        h = F.glu(self.up(x), dim=-1)
+        if self.backend == "reference":
+            h = masked(h, mask)
+        h = _depthwise(h, self.dw, mask)
+        y = self.out(F.silu(self.norm(h)))
+        return masked(y, mask) if self.backend == "reference" else y
+
+
+class GlobalAttention(nn.Module):
+    """Attention over the 4x-pooled sequence with rotary q/k, interpolated back."""
+
+    def __init__(self, c):
+        super().__init__()
+        self.heads, self.head_dim = c.heads, c.dim // c.heads
+        self.backend, self.buffer_fusion = c.backend, c.buffer_fusion
+        self.native_kernels = c.native_kernels
+        self.qkv = nn.Linear(c.dim, 3 * c.dim, bias=False)
+        self.out = nn.Linear(c.dim, c.dim, bias=False)
+
+    def forward(self, x, grids):
+        p = grids.pool(x)
+        b, t = p.shape[:2]
+        q, k, v = self.qkv(p).view(b, t, 3, self.heads, self.head_dim).permute(2, 0, 3, 1, 4).unbind(0)
+        q, k = rope(q, grids.rope_cos, grids.rope_sin), rope(k, grids.rope_cos, grids.rope_sin)
+        y = masked_attention(q, k, v, grids.low_mask[:, None, None, :])
+        y = self.out(y.transpose(1, 2).reshape(b, t, -1))
+        return grids.interpolate(y)
+
+
+class TriFusionBlock(nn.Module):
+    def __init__(self, c):
+        super().__init__()
+        d, r = c.dim, c.evidence_rank
+        self.backend = c.backend
+        self.buffer_fusion = c.buffer_fusion
+        self.native_kernels = c.native_kernels
+        self.paired_mamba = c.paired_mamba
+        self.paired_mamba_grid_limit = c.paired_mamba_grid_limit
+        self.pre = RMSNorm(d, backend=c.backend)
+        self.local, self.attention = LocalCNN(c), GlobalAttention(c)
+        self.cn, self.an, self.mn = [RMSNorm(d, backend=c.backend) for _ in range(3)]
+        self.e_down = nn.Linear(2 * d, r)
+        self.e_value, self.e_gate = nn.Linear(r, d), nn.Linear(r, d)
+        self.u_norm = RMSNorm(d, backend=c.backend)
+        self.forward_mamba, self.backward_mamba = mamba_factory(c), mamba_factory(c)
+        self.gate = nn.Linear(3 * d, 3)
+        self.merge_dw = nn.Conv1d(3 * d, 3 * d, 3, padding=1, groups=3 * d)
+        self.merge = nn.Linear(3 * d, d, bias=False)
+        self.ff_norm = RMSNorm(d, backend=c.backend)
+        self.gate_up = nn.Linear(d, 2 * c.ffn_dim, bias=False)
+        self.down = nn.Linear(c.ffn_dim, d, bias=False)
+        self.dropout = nn.Dropout(c.dropout)
+        # Initialisation of a fresh block (model.py:135-144).
+        for layer in (self.e_gate, self.gate):
+            nn.init.zeros_(layer.weight)
+            nn.init.zeros_(layer.bias)
+        nn.init.normal_(self.e_value.weight, std=1e-3)
+        nn.init.zeros_(self.e_value.bias)
+        with torch.no_grad():
+            for layer in (self.merge, self.down):
+                layer.weight.mul_(1 / math.sqrt(2 * c.depth))
+
+    def forward(self, x, grids):
+        mask, lengths = grids.mask, grids.lengths
+        opt = self.backend != "reference"
+
+        def keep_zero(value):  # the optimized path's operators already keep padded rows at zero
+            return value if opt else masked(value, mask)
+
+        if opt:
+            x = _mask_rows(x, mask, True)
+        h = keep_zero(self.pre(x))
+        cn = keep_zero(self.cn(self.local(h, mask, lengths)))
+        an = keep_zero(self.an(self.attention(h, grids)))
+        z = F.silu(self.e_down(torch.cat((cn, an), -1)))
+        if opt and x.is_cuda:
+            from .kernels import native
+
+            u = native.evidence_norm(x, self.e_value(z), self.e_gate(z), self.u_norm.weight, mask,
+                                     self.u_norm.eps)
+            # The recurrence zeroes rows past each length itself (out_proj has no bias).
+            mf = self.forward_mamba(u, lengths)
+            mb = reverse_valid(self.backward_mamba(reverse_valid(u, lengths), lengths), lengths)
+            mn = native.mean_norm(mf, mb, self.mn.weight, self.mn.eps)
+        else:
+            evidence = self.e_value(z).float() * (2 * torch.sigmoid(self.e_gate(z).float()))
+            u = _mask_rows(self.u_norm(x + evidence), mask, opt)
+            mf = _mask_rows(self.forward_mamba(u), mask, opt)
+            mb = reverse_valid(self.backward_mamba(reverse_valid(u, lengths, self.backend)),
+                               lengths, self.backend)
+            mn = keep_zero(self.mn((mf.float() + mb.float()) * 0.5))
+        s = torch.cat((cn, mn, an), -1)
+        v = keep_zero(gated_concat(s, self.gate(s), self.backend))
+        conv = _depthwise(v, self.merge_dw, mask)
+        r = keep_zero(x + self.dropout(self.merge(v + conv)))
+        f = swiglu(self.gate_up(self.ff_norm(r)), self.backend)
+        out = _mask_rows(r + self.dropout(self.down(f)), mask, opt)
+        return out, mf, mb
+
+
+class TriFusion(nn.Module):
+    def __init__(self, config=None):
+        super().__init__()
+        self.config = config or ModelConfig()
+        c = self.config
+        if c.dim % c.heads or c.dim % 32:
+            raise ValueError("dim must divide attention heads and Mamba headdim")
+        self.front = Frontend(c.backend, c.channels_last, c.checkpoint_frontend)
+        self.front_projection = nn.Identity() if c.dim == 1024 else nn.Linear(1024, c.dim, bias=False)
+        self.blocks = nn.ModuleList([TriFusionBlock(c) for _ in range(c.depth)])
+        from .decoder import Decoder
+
+        self.decoder = Decoder(c.dim)
+        self.memory_head = nn.Linear(c.dim, 2)
+        self.set_buffer_fusion(c.buffer_fusion)
+        self.set_native_kernels(c.native_kernels)
+
+    def _set(self, name, value):
+        for module in self.modules():
+            if hasattr(module, name):
+                setattr(module, name, value)
+
+    def set_backend(self, backend):
+        """Switch between ``"l4"`` (B200 kernels) and ``"reference"`` formulas."""
+        if backend not in ("reference", "l4"):
+            raise ValueError(backend)
+        self._set("backend", backend)
+        self.config.backend = backend
+
+    def set_buffer_fusion(self, enabled):
+        self._set("buffer_fusion", bool(enabled))
+        self.config.buffer_fusion = bool(enabled)
+
+    def set_native_kernels(self, enabled):
+        self._set("native_kernels", bool(enabled))
+        self.config.native_kernels = bool(enabled)
+
+    def encode(self, audio, lengths, channels):
+        x, fine, main_lengths, fine_lengths = self.front(audio, lengths, channels)
+        x = self.front_projection(x).float()
+        optimized = self.config.backend == "l4"
+        grids = Grids.make(main_lengths, x.shape[1], self.config.dim // self.config.heads,
+                           self.config.buffer_fusion and optimized,
+                           self.config.native_kernels and optimized)
+        mf = mb = None
+        for block in self.blocks:
+            x, mf, mb = block(x, grids)
+        return x, fine, grids, fine_lengths, mf, mb
+
+    def forward(self, audio, lengths, channels):
+        return self.decoder(*self.encode(audio, lengths, channels))

@@ -116,3 +116,92 @@ def norm_weight(width, seed=0):
     """RMSNorm weights ~ 1 + N(0, 0.02) (benchmark configuration 1)."""
     g = torch.Generator().manual_seed(seed + 11)
     return 1 + 0.02 * torch.randn(width, generator=g)
+
+
+# ---------------------------------------------------------------------------
+# Synthetic student checkpoints and audio (the model-level configurations).
+# Weights are a function of (parameter name, shape, seed) alone, so any model
+# with the reference's parameter layout — this package's or the reference's —
+# receives identical values.
+# ---------------------------------------------------------------------------
+
+def _name_seed(name, seed):
+    import zlib
+
+    return (zlib.crc32(name.encode()) + 7919 * seed) % (2 ** 31)
+
+
+def parameter_value(name, shape, seed=0, depth=1):
+    """Deterministic FP32 value of one student parameter.
+
+    Matrices and convolution kernels ~ N(0, 1/fan_in) (the three logit heads
+    0.1x that, so that the logits stay in sigmoid's unsaturated range; the
+    residual ``merge``/``down`` projections 1/sqrt(2 depth) that, as the
+    reference initialises them); norm
+    weights 1 + N(0, 0.02);
+    biases N(0, 0.02); Mamba ``dt_bias`` -4 + N(0, 0.3), ``B_bias``/``C_bias``
+    1 + N(0, 0.1), ``D`` ~ N(0, 1); decoder queries/bands N(0, 0.02).
+    """
+    g = torch.Generator().manual_seed(_name_seed(name, seed))
+    x = torch.randn(*shape, generator=g)
+    leaf = name.rsplit(".", 1)[-1]
+    if leaf == "dt_bias":
+        return -4.0 + 0.3 * x
+    if leaf in ("B_bias", "C_bias"):
+        return 1.0 + 0.1 * x
+    if leaf == "D":
+        return x
+    if leaf in ("query", "band"):
+        return 0.02 * x
+    if leaf == "bias":
+        return 0.02 * x
+    if len(shape) == 1:  # RMSNorm weights
+        return 1.0 + 0.02 * x
+    fan_in = math.prod(shape[1:])
+    if name.startswith(_HEADS):  # keep the logits in sigmoid's unsaturated range
+        return 0.1 * x / math.sqrt(fan_in)
+    if name.endswith((".merge.weight", ".down.weight")):  # residual branches (model.py:142-144)
+        return x / math.sqrt(fan_in * 2 * depth)
+    return x / math.sqrt(fan_in)
+
+
+_HEADS = ("decoder.file_head.2.", "decoder.voice_head.", "decoder.music_head.")
+
+
+def student_state(shapes, seed=0):
+    """State dict for ``{name: shape}`` (a model's parameter/buffer layout)."""
+    blocks = {int(k.split(".")[1]) for k in shapes if k.startswith("blocks.")}
+    depth = max(blocks) + 1 if blocks else 1
+    return {name: parameter_value(name, tuple(shape), seed, depth)
+            for name, shape in sorted(shapes.items())}
+
+
+def student_checkpoint(path, config, seed=0):
+    """Write a reference-format checkpoint (``{"model_config", "model"}``) with
+    synthetic weights for ``config`` (a dict of ``ModelConfig`` fields)."""
+    from .model import ModelConfig, TriFusion
+
+    with torch.device("meta"):
+        model = TriFusion(ModelConfig(**config))
+    shapes = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    torch.save({"model_config": dict(config), "model": student_state(shapes, seed)}, path)
+    return path
+
+
+def synthetic_audio(batch, samples, *, channels=None, lengths=None, seed=0):
+    """PCM16-quantised Gaussian noise (sigma 0.1) ``[B, C, samples]`` FP32,
+    zero past each length and in absent channels; returns (audio, lengths,
+    channels) as CPU tensors."""
+    g = torch.Generator().manual_seed(seed)
+    if channels is None:
+        channels = torch.ones(batch, dtype=torch.int64)
+    channels = torch.as_tensor(channels, dtype=torch.int64)
+    if lengths is None:
+        lengths = torch.full((batch,), samples, dtype=torch.int64)
+    lengths = torch.as_tensor(lengths, dtype=torch.int64)
+    c = int(channels.max())
+    wave = torch.randn(batch, c, samples, generator=g) * 0.1
+    wave = torch.clamp(torch.round(wave * 32768), -32768, 32767) / 32768
+    keep = torch.arange(samples)[None, None, :] < lengths[:, None, None]
+    keep = keep & (torch.arange(c)[None, :, None] < channels[:, None, None])
+    return wave * keep, lengths, channels

@@ -40,11 +40,17 @@ METRIC = "fused_mamba tokens/s + HBM GB/s vs peak; audio-sec/s at 1/2/4/8 B200"
 L2_BYTES = 126 * 2 ** 20
 FALLBACK_HBM_GBS = 6650.0
 
+STUDENT = dict(dim=384, depth=8, heads=6, ffn_dim=1536, state_dim=128)
 WORKLOADS = {
-    # name: (B, T, H, lengths spec)
-    "cfg1": dict(batch=16, time=200, heads=12, lengths=("uniform", 120, 200)),
-    "cfg2": dict(batch=2, time=3600, heads=12, lengths=("fixed", [3600, 2871])),
+    # recurrence steps: (B, T, H, lengths spec)
+    "cfg1": dict(kind="recurrence", batch=16, time=200, heads=12, lengths=("uniform", 120, 200)),
+    "cfg2": dict(kind="recurrence", batch=2, time=3600, heads=12, lengths=("fixed", [3600, 2871])),
+    # whole student forward through InferenceEngine(graphs=True)
+    "cfg3": dict(kind="model", batch=16, samples=64000, lengths=("uniform", 32000, 64000)),
+    # box-level sweep: 1024 clips, length buckets, LPT partition over the GPUs
+    "cfg4": dict(kind="box", clips=1024, max_batch=32, padded_seconds=120),
 }
+AUDIO_METRIC_UNIT = "audio-sec/s"
 
 
 def parse():
@@ -229,16 +235,10 @@ def run_reference(args, wl):
     print(json.dumps(line), flush=True)
 
 
-def main():
-    args = parse()
-    wl = WORKLOADS[args.workload]
-    if args.impl == "reference":
-        run_reference(args, wl)
-        return
+def setup_dist():
+    """(world, rank, local rank, device); NCCL process group when world > 1."""
     import torch
     import torch.distributed as dist
-    from trifusion_b200 import fused_recurrence
-    from trifusion_b200.synthetic import recurrence_inputs, norm_weight
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -248,6 +248,37 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return world, rank, local, dev
+
+
+def max_over_ranks(value, world, dev):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    args = parse()
+    wl = WORKLOADS[args.workload]
+    kind = wl["kind"]
+    if args.impl == "reference":
+        (run_reference if kind == "recurrence" else run_reference_model)(args, wl)
+        return
+    {"recurrence": run_recurrence, "model": run_model, "box": run_box}[kind](args, wl)
+
+
+def run_recurrence(args, wl):
+    import torch
+    import torch.distributed as dist
+    from trifusion_b200 import fused_recurrence
+    from trifusion_b200.synthetic import recurrence_inputs, norm_weight
+
+    world, rank, local, dev = setup_dist()
 
     b, t, h = wl["batch"], wl["time"], wl["heads"]
     lengths_cpu = make_lengths(wl["lengths"], b, seed=rank)
@@ -386,6 +417,272 @@ def main():
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def _student(dev, tmpdir, optimized=True):
+    from trifusion_b200 import load_student
+    from trifusion_b200.synthetic import student_checkpoint
+
+    path = student_checkpoint(Path(tmpdir) / "student.pt", STUDENT, seed=0)
+    return load_student(path, optimized=optimized, device=dev)
+
+
+def _l2_flush_buffer(dev):
+    import torch
+
+    return torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+
+
+def run_model(args, wl):
+    """cfg3: one step = one ``InferenceEngine(graphs=True)`` call on a [16, 1, 64000]
+    batch (graph replay: input copies into the graph's buffers, the forward,
+    the owned logits copy). Each timed step is bracketed by its own CUDA events
+    with an L2 flush (a 252 MiB write) before it, outside the events."""
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+    from trifusion_b200 import InferenceEngine, configure_runtime
+    from trifusion_b200.synthetic import synthetic_audio
+
+    world, rank, local, dev = setup_dist()
+    configure_runtime()
+    b, n = wl["batch"], wl["samples"]
+    lengths = make_lengths(wl["lengths"], b, seed=rank)
+    audio, lengths, channels = synthetic_audio(b, n, lengths=lengths, seed=rank)
+    with tempfile.TemporaryDirectory() as tmp:
+        model = _student(dev, tmp)
+    engine = InferenceEngine(model, graphs=True, max_graphs=1)
+    inputs = tuple(x.to(dev) for x in (audio, lengths, channels))
+    flush = _l2_flush_buffer(dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 1)):
+        engine(*inputs)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    tl0 = time.time()
+    while time.time() - tl0 < 0.6:
+        engine(*inputs)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    for e0, e1 in events:
+        flush.fill_(1)
+        e0.record(stream)
+        engine(*inputs)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    tw1 = time.time()
+    sampler.stop()
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in events)
+    ms = max_over_ranks(ms, world, dev)
+    ms_per_step = ms / max(args.steps, 1)
+    audio_s = float(lengths.sum()) / 16000
+    value = world * audio_s / (ms_per_step / 1e3)
+
+    # End to end: pinned host audio in, logits back to pinned host memory.
+    host = tuple(x.pin_memory() for x in (audio, lengths, channels))
+    dev_in = tuple(torch.empty_like(x, device=dev) for x in host)
+    host_out = torch.empty(b, 5).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in host)
+
+    def e2e_step():
+        for src, dst in zip(host, dev_in):
+            dst.copy_(src, non_blocking=True)
+        host_out.copy_(engine(*dev_in), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    e_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(min(args.steps, args.e2e_steps))]
+    for e0, e1 in e_events:
+        flush.fill_(1)
+        e0.record(stream)
+        e2e_step()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = sum(a.elapsed_time(c) for a, c in e_events) / max(len(e_events), 1)
+    e_ms = max_over_ranks(e_ms, world, dev)
+    if world > 1:
+        dist.barrier()
+        engine.clear()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": AUDIO_METRIC_UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init student, PCM16-quantised noise)",
+        "config": {"workload": args.workload, "student": STUDENT, "batch": b, "samples": n,
+                   "channels": 1, "audio_seconds_per_step": audio_s,
+                   "step": "InferenceEngine(graphs=True) replay incl. input/output copies",
+                   "l2": "252 MiB write before every timed step (outside the events)",
+                   "parallelism": f"replicas x{world} (one batch per GPU)"},
+        "roofline": None,
+        "e2e": {"value": world * audio_s / (e_ms / 1e3), "unit": AUDIO_METRIC_UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": b * 5 * 4},
+        "clocks": sampler.summary(tl0, tw1),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_box(args, wl):
+    """cfg4: 1024 clips bucketed by (channels, length) into batches of up to 32,
+    partitioned over the ranks longest-processing-time first; one step = every
+    rank runs all of its batches through its ``InferenceEngine(graphs=True)``
+    (one graph per batch shape, captured during warm-up) and the logits are
+    all-gathered once. ``value`` = total audio-seconds / step time (max over
+    ranks); inputs are device-resident for ``value`` and copied from pinned
+    host memory batch by batch for ``e2e``."""
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+    from trifusion_b200 import InferenceEngine, configure_runtime
+    from trifusion_b200.audio import plan_batches
+    from trifusion_b200.sharding import batch_cost, gather_logits, lpt_partition
+    from trifusion_b200.synthetic import batch_audio, clip_set
+
+    world, rank, local, dev = setup_dist()
+    configure_runtime()
+    records = clip_set(wl["clips"], seed=0)
+    plan = plan_batches(records, padded_seconds=wl["padded_seconds"], max_batch=wl["max_batch"])
+    mine = lpt_partition([batch_cost(lim, rows) for lim, rows in plan], world)[rank]
+    host = [tuple(x.pin_memory() for x in batch_audio(plan[i][0], plan[i][1], seed=0)) for i in mine]
+    indices = torch.tensor([r.index for i in mine for r in plan[i][1]], dtype=torch.int64, device=dev)
+    dev_in = [tuple(x.to(dev) for x in h) for h in host]
+    shapes = {tuple(h[0].shape) for h in host}
+    with tempfile.TemporaryDirectory() as tmp:
+        model = _student(dev, tmp)
+    engine = InferenceEngine(model, graphs=True, max_graphs=max(len(shapes), 1))
+    total_audio_s = sum(r.samples for r in records) / 16000
+    stream = torch.cuda.current_stream(dev)
+
+    def sweep(inputs):
+        outs = [engine(*x) for x in inputs]
+        local_logits = torch.cat(outs) if outs else torch.zeros(0, 5, device=dev)
+        if world > 1:
+            return gather_logits(indices, local_logits)
+        return indices, local_logits
+
+    for _ in range(max(args.warmup, 1)):
+        sweep(dev_in)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    tl0 = time.time()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    for e0, e1 in events:
+        e0.record(stream)
+        idx, logits = sweep(dev_in)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    tw1 = time.time()
+    sampler.stop()
+    ms = max_over_ranks(sum(a.elapsed_time(c) for a, c in events), world, dev)
+    ms_per_step = ms / max(args.steps, 1)
+    assert idx.numel() == len(records) and bool(torch.isfinite(logits).all())
+
+    h2d = sum(x.numel() * x.element_size() for h in host for x in h)
+
+    def e2e_sweep():
+        staged = []
+        for h, d in zip(host, dev_in):
+            for src, dst in zip(h, d):
+                dst.copy_(src, non_blocking=True)
+            staged.append(d)
+        idx_, logits_ = sweep(staged)
+        return logits_.to("cpu", non_blocking=True)
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    e2e_sweep()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    if world > 1:
+        dist.barrier()
+        engine.clear()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": total_audio_s / (ms_per_step / 1e3), "unit": AUDIO_METRIC_UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 1),
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init student, 1024 PCM16-quantised noise clips)",
+        "config": {"workload": args.workload, "student": STUDENT, "clips": len(records),
+                   "audio_seconds": total_audio_s, "batches": len(plan),
+                   "batches_on_rank0": len(mine), "graph_shapes_on_rank0": len(shapes),
+                   "max_batch": wl["max_batch"],
+                   "step": "all batches through InferenceEngine(graphs=True) + one logits all-gather",
+                   "l2": "inputs larger than L2 (the sweep streams all batches)",
+                   "parallelism": f"data-parallel x{world}, LPT partition by padded audio-seconds"},
+        "roofline": None,
+        "e2e": {"value": total_audio_s / (e_ms / 1e3), "unit": AUDIO_METRIC_UNIT,
+                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": len(records) * 5 * 4},
+        "clocks": sampler.summary(tl0, tw1),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_model(args, wl):
+    """`--impl reference` for cfg3/cfg4: the reference model's arithmetic on the
+    host CPU (FP32, this package's host model with the reference formulas and
+    the oracle recurrence), on a bounded sample of clips."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import tempfile
+
+    import numpy as np
+    import torch
+    from oracle import mamba_oracle as O
+    import trifusion_b200.mamba_fused as mf
+    from trifusion_b200.synthetic import synthetic_audio
+
+    cores = host_threads()
+    torch.set_num_threads(cores)
+
+    def oracle_recurrence(q, k, v, adt, dt, trap, qb, kb, angles, d, z, warps=8):
+        a = [t.detach().float().numpy() for t in (q, k, v, adt, dt, trap, qb, kb, angles, d, z)]
+        return torch.from_numpy(np.asarray(O.fused_mamba(*a, dtype=np.float32), np.float32))
+
+    mf.fused_mamba = oracle_recurrence
+    with tempfile.TemporaryDirectory() as tmp:
+        model = _student("cpu", tmp, optimized=False)
+    b, n = 2, 64000
+    audio, lengths, channels = synthetic_audio(b, n, lengths=[64000, 48000], seed=0)
+    with torch.inference_mode():
+        model(audio, lengths, channels)
+        steps = max(1, min(args.steps, 3))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            model(audio, lengths, channels)
+        el = time.perf_counter() - t0
+    audio_s = float(lengths.sum()) / 16000
+    value = audio_s * steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": AUDIO_METRIC_UNIT,
+        "n_gpus": args.gpus, "steps": steps, "warmup": 1, "ms_per_step": el / steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": args.workload, "student": STUDENT},
+        "cpu_baseline": {"value": value, "unit": AUDIO_METRIC_UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{steps} forwards of 2 clips (4 s, 3 s) on the host, FP32"},
+        "e2e": {"value": value, "unit": AUDIO_METRIC_UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
     print(json.dumps(line), flush=True)
 
 

@@ -205,3 +205,30 @@ def synthetic_audio(batch, samples, *, channels=None, lengths=None, seed=0):
     keep = torch.arange(samples)[None, None, :] < lengths[:, None, None]
     keep = keep & (torch.arange(c)[None, :, None] < channels[:, None, None])
     return wave * keep, lengths, channels
+
+
+def clip_set(count=1024, *, seed=0, min_seconds=1.0, max_seconds=72.0, stereo_fraction=0.3):
+    """Synthetic clip records for the box-level sweep: durations log-uniform in
+    [min_seconds, max_seconds], ``stereo_fraction`` of them two-channel."""
+    from .audio import SAMPLE_RATE, AudioFile
+
+    g = torch.Generator().manual_seed(seed)
+    u = torch.rand(count, generator=g, dtype=torch.float64)
+    seconds = torch.exp(math.log(min_seconds) + u * (math.log(max_seconds) - math.log(min_seconds)))
+    stereo = torch.rand(count, generator=g, dtype=torch.float64) < stereo_fraction
+    return [AudioFile(i, None, max(1, min(int(round(float(s) * SAMPLE_RATE)), 72 * SAMPLE_RATE)),
+                      2 if bool(st) else 1)
+            for i, (s, st) in enumerate(zip(seconds, stereo))]
+
+
+def batch_audio(limit, rows, *, seed=0):
+    """Padded ``[len(rows), channels, limit]`` audio for one planned batch, each
+    clip PCM16-quantised noise from its own seed; returns (audio, lengths, channels)."""
+    c = max(r.channels for r in rows)
+    audio = torch.zeros(len(rows), c, limit)
+    for i, r in enumerate(rows):
+        clip, _, _ = synthetic_audio(1, r.samples, channels=[r.channels], seed=seed * 1_000_003 + r.index)
+        audio[i, :r.channels, :r.samples] = clip[0, :r.channels]
+    lengths = torch.tensor([r.samples for r in rows], dtype=torch.int64)
+    channels = torch.tensor([r.channels for r in rows], dtype=torch.int64)
+    return audio, lengths, channels

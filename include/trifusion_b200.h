@@ -199,6 +199,30 @@ int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* 
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
                       int64_t row_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Spectrogram front end, on channels-last activations: a [B, C, T, F] tensor
+ * stored as [B, T, F, C] (every (b, t, f) position one contiguous row of C).
+ * ------------------------------------------------------------------------ */
+
+/* Channel RMSNorm of every (b, t, f) row, zero where t >= lengths[b], then SiLU
+ * when `silu` != 0 (the normalised value is rounded to `dtype` first); C <= 256.
+ * Replaces kernels/buffers.py:58-79 `front_norm` (`_front_norm`,
+ * kernels/primitives.py:153-187), used by front.py:19-43. */
+int tf_front_norm_fwd(const void* x, int dtype, const float* w, const int64_t* lengths, void* y,
+                      int batch, int time, int freq, int channels, float eps, int silu, void* stream);
+
+/* Residual tail of a CNN stage: y = t < lengths[b] ? silu(h + skip) : 0, the sum
+ * rounded to `dtype` before SiLU. Replaces front.py:43
+ * (`clean(F.silu(h + clean(self.skip(x))))`). */
+int tf_front_residual_fwd(const void* h, const void* skip, int dtype, const int64_t* lengths, void* y,
+                          int batch, int time, int freq, int channels, void* stream);
+
+/* Frequency bands: x [B, T, F, C] -> y [B, T, 8, C], band i the mean over
+ * f in [floor(i F / 8), ceil((i + 1) F / 8)). Replaces kernels/native.py:141-163
+ * `bands` and front.py:80-87 (adaptive_avg_pool2d + permute). */
+int tf_bands_fwd(const void* x, int dtype, void* y, int batch, int time, int freq, int channels,
+                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

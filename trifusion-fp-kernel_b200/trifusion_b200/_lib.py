@@ -47,6 +47,9 @@ SIGNATURES = {
     "tf_pool4_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
     "tf_masked_mean_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
     "tf_end_gather_fwd": [_p, _p, _p, _i, _i, _q, _p],
+    "tf_front_norm_fwd": [_p, _i, _p, _p, _p, _i, _i, _i, _i, _f, _i, _p],
+    "tf_front_residual_fwd": [_p, _p, _i, _p, _p, _i, _i, _i, _i, _p],
+    "tf_bands_fwd": [_p, _i, _p, _i, _i, _i, _i, _p],
 }
 _RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p,
              "tf_recurrence_workspace_size": ctypes.c_size_t}

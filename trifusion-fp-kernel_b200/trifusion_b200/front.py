@@ -1,9 +1,10 @@
 """Spectrogram front end (reference ``front.py``): STFT power on cuFFT, three
-residual Conv2d stages on cuDNN with channel RMSNorm (the CUDA row-norm
-kernel), and frequency band pooling.
+residual Conv2d stages on cuDNN, and frequency band pooling.
 
 Parameter names match the reference's checkpoints. The convolutions and the
-STFT are library calls; the channel norms run on ``libtrifusion_b200.so``.
+STFT are library calls; on the optimized backend the activations stay
+channels-last and the masked channel norms (+SiLU), the residual tails and the
+band pooling run as single-pass kernels of ``libtrifusion_b200.so``.
 """
 
 from __future__ import annotations
@@ -39,6 +40,15 @@ class CNNStage(nn.Module):
 
     def forward(self, x, lengths):
         lengths = (lengths + self.stride - 1) // self.stride
+        if self.backend != "reference" and x.is_cuda:
+            # Channels-last activations: each channel norm reads contiguous rows,
+            # and mask + norm + SiLU (and the residual tail) are one pass each.
+            from .kernels.buffers import front_norm, front_residual
+
+            x = x.contiguous(memory_format=torch.channels_last)
+            h = front_norm(self.conv1(x), lengths, self.norm1, silu=True)
+            h = front_norm(self.conv2(h), lengths, self.norm2)
+            return front_residual(h, self.skip(x), lengths)
         h = self.conv1(x)
         valid = time_mask(lengths, h.shape[2])[:, None, :, None]
         # A zero row stays zero through the bias-free norm and SiLU, so masking
@@ -49,9 +59,13 @@ class CNNStage(nn.Module):
         return F.silu(h + skip).masked_fill(~valid, 0)
 
 
-def band_pool(x):
+def band_pool(x, native=False):
     """Average the frequency axis of [B, C, T, F] into 8 bands → [B, T, 8, C]
     (band i covers [floor(iF/8), ceil((i+1)F/8)); reference ``front.py:80-87``)."""
+    if native and x.is_cuda:
+        from .kernels.native import bands
+
+        return bands(x)
     return F.adaptive_avg_pool2d(x, (x.shape[2], 8)).permute(0, 2, 3, 1).contiguous()
 
 
@@ -104,5 +118,5 @@ class Frontend(nn.Module):
             x = stage(x, lengths)
             lengths = (lengths + stage.stride - 1) // stage.stride
             if i == 1:
-                fine, fine_lengths = band_pool(x), lengths
-        return band_pool(x).flatten(2), fine, lengths, fine_lengths
+                fine, fine_lengths = band_pool(x, self.native_kernels), lengths
+        return band_pool(x, self.native_kernels).flatten(2), fine, lengths, fine_lengths

@@ -62,3 +62,38 @@ def mamba_controls(a, dt, bias, floor):
                 _lib.dtype_code(a, "mamba_controls"), strides, bias.data_ptr(), float(floor),
                 oa.data_ptr(), od.data_ptr(), b, t, h)
     return oa, od
+
+
+def _nhwc(x):
+    """A [B, C, T, F] tensor in channels-last memory (rows of C contiguous)."""
+    return x.contiguous(memory_format=torch.channels_last)
+
+
+def front_norm(x, lengths, norm, silu=False):
+    """Channel RMSNorm of a [B, C, T, F] activation at every (t, f), zero where
+    t >= lengths, then SiLU if asked (reference ``buffers.py:58-79``). Returns a
+    [B, C, T, F] view of channels-last memory, like the reference."""
+    x = _nhwc(x)
+    dev = _lib.require_cuda("front_norm", x, lengths, norm.weight)
+    b, c, t, f = x.shape
+    w = norm.weight.detach().float().contiguous()
+    lengths = lengths.to(torch.int64).contiguous()
+    y = torch.empty_like(x)  # channels-last too
+    _lib.launch("tf_front_norm_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "front_norm"), w.data_ptr(),
+                lengths.data_ptr(), y.data_ptr(), b, t, f, c, float(norm.eps), int(bool(silu)))
+    return y
+
+
+def front_residual(h, skip, lengths):
+    """Residual tail of a front-end stage: ``silu(h + skip)`` zero past the
+    lengths (reference ``front.py:43``), channels-last in and out."""
+    h, skip = _nhwc(h), _nhwc(skip.to(h.dtype))
+    dev = _lib.require_cuda("front_residual", h, skip, lengths)
+    if h.shape != skip.shape:
+        raise ValueError("front_residual: h and skip must have the same shape")
+    b, c, t, f = h.shape
+    lengths = lengths.to(torch.int64).contiguous()
+    y = torch.empty_like(h)
+    _lib.launch("tf_front_residual_fwd", dev, h.data_ptr(), skip.data_ptr(),
+                _lib.dtype_code(h, "front_residual"), lengths.data_ptr(), y.data_ptr(), b, t, f, c)
+    return y

@@ -101,3 +101,14 @@ def end_gather(x, lengths):
     _lib.launch("tf_end_gather_fwd", dev, x.data_ptr(), lengths.data_ptr(), y.data_ptr(), b, t,
                 row_bytes)
     return y
+
+
+def bands(x):
+    """Average the frequency axis of [B, C, T, F] into 8 bands -> [B, T, 8, C]
+    (reference ``native.py:157-163``)."""
+    x = x.contiguous(memory_format=torch.channels_last)
+    dev = _lib.require_cuda("bands", x)
+    b, c, t, f = x.shape
+    y = torch.empty((b, t, 8, c), device=dev, dtype=x.dtype)
+    _lib.launch("tf_bands_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "bands"), y.data_ptr(), b, t, f, c)
+    return y

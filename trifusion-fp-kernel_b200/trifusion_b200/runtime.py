@@ -66,6 +66,8 @@ def prepare_static_weights(model):
     for module in model.modules():
         if isinstance(module, (torch.nn.Linear, torch.nn.Conv1d, torch.nn.Conv2d)):
             module.to(dtype=torch.bfloat16)
+        if isinstance(module, torch.nn.Conv2d):  # the front end runs channels-last
+            module.to(memory_format=torch.channels_last)
 
 
 def configure_runtime(threads=2, enforce_l4=True):

@@ -199,6 +199,15 @@ int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* 
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
                       int64_t row_bytes, void* stream);
 
+/* Depthwise Conv1d over time on [B, T, C] rows with zero padding outside [0, T):
+ * y[b,t,c] = t < lengths[b] ? sum_k x[b, t+k-K/2, c] w[c,k] + bias[c] : 0, inputs
+ * rounded to BF16, BF16 out; w [C, K] and bias [C] (may be NULL) BF16; K in
+ * {3, 5, 7}; C % 4 == 0. Replaces kernels/buffers.py:13-32 `depthwise_masked`
+ * (`_dw_forward`, kernels/primitives.py:73-87), used by model.py:70-72,186-190. */
+int tf_depthwise_masked_fwd(const void* x, int dtype, const void* w, const void* bias,
+                            const int64_t* lengths, void* y, int batch, int seqlen, int channels,
+                            int taps, void* stream);
+
 /* ------------------------------------------------------------------------
  * Spectrogram front end, on channels-last activations: a [B, C, T, F] tensor
  * stored as [B, T, F, C] (every (b, t, f) position one contiguous row of C).

@@ -255,3 +255,25 @@ def test_capture_in_cuda_graph_matches_eager():
     torch.cuda.synchronize()
     for a, c in zip(eager, captured):
         assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("dtype", [BF, torch.float32])
+@pytest.mark.parametrize("taps,width", [(7, 384), (3, 1152)])
+def test_depthwise_masked_matches_conv1d(dtype, taps, width):
+    from trifusion_b200.kernels.buffers import depthwise_masked
+
+    b, t = 4, 101
+    x = seeded((b, t, width), 21, dtype=dtype).to(DEV)
+    torch.manual_seed(22)
+    conv = torch.nn.Conv1d(width, width, taps, padding=taps // 2, groups=width).to(DEV).to(BF)
+    lengths = torch.tensor([101, 50, 1, 0], device=DEV)
+    y = depthwise_masked(x, conv, lengths)
+    assert y.dtype == BF and y.shape == (b, t, width)
+    # The reference rounds the input to BF16 (the autocast type) and sums in FP32.
+    ref = torch.nn.functional.conv1d(x.to(BF).float().transpose(1, 2), conv.weight.float(), conv.bias.float(),
+                                     padding=taps // 2, groups=width).transpose(1, 2)
+    valid = (torch.arange(t, device=DEV)[None, :] < lengths[:, None])[..., None]
+    ref = torch.where(valid, ref, torch.zeros((), device=DEV)).to(BF)
+    y32, r32 = y.float(), ref.float()
+    assert torch.all((y32 - r32).abs() <= BF16_ULP * r32.abs() + 1e-5), (y32 - r32).abs().max()
+    assert (y.masked_select(~valid.expand_as(y)) == 0).all()

@@ -41,13 +41,82 @@ __device__ __forceinline__ int valid_len(const int64_t* lengths, int b, int T) {
   return static_cast<int>(len < 0 ? 0 : (len > T ? T : len));
 }
 
+// Streaming kernels: enough resident threads for many 16-byte requests in flight.
+int grid_vec(int64_t threads) {
+  const int64_t blocks = (threads + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  return static_cast<int>(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
+}
+
 int grid_for(int64_t items, int per_block) {
   const int64_t blocks = (items + per_block - 1) / per_block;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   return static_cast<int>(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
 }
 
-// One warp per (b, t, f) row of C channels; C <= 32 * kMaxPerLane.
+// A group of G = C / 8 threads per (b, t, f) row; each thread moves one 16-byte
+// vector of 8 BF16 channels and the group reduces with shuffles. Used for BF16
+// rows with C in {8, 16, 32, 64, 128, 256}.
+template <int G>
+__global__ void __launch_bounds__(kThreads) front_norm_vec_kernel(const bf16* __restrict__ x,
+                                                                  const float* __restrict__ w,
+                                                                  const int64_t* __restrict__ lengths,
+                                                                  bf16* __restrict__ y, int B, int Tn, int F,
+                                                                  float eps, int silu) {
+  constexpr int C = 8 * G;
+  const int64_t rows = static_cast<int64_t>(B) * Tn * F;
+  const int sub = threadIdx.x % G;
+  const float4 w0 = *reinterpret_cast<const float4*>(w + 8 * sub);
+  const float4 w1 = *reinterpret_cast<const float4*>(w + 8 * sub + 4);
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * (kThreads / G);
+  // The loop bound is uniform across the block, so whole warps take part in the
+  // group shuffles; rows past the end only skip their loads and stores.
+  for (int64_t first = blockIdx.x * static_cast<int64_t>(kThreads / G); first < rows; first += stride) {
+    const int64_t row = first + threadIdx.x / G;
+    const bool in = row < rows;
+    bool live = false;
+    if (in) {
+      const int t = static_cast<int>((row / F) % Tn);
+      const int b = static_cast<int>(row / (static_cast<int64_t>(F) * Tn));
+      live = t < valid_len(lengths, b, Tn);
+    }
+    float v[8];
+    if (live) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + row * C + 8 * sub);
+      const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f2 = unpack_bf16x2(ww[i]);
+        v[2 * i] = f2.x;
+        v[2 * i + 1] = f2.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / static_cast<float>(C) + eps);
+    uint32_t out[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a = round_to<bf16>(v[2 * i] * r * wv[2 * i]);
+      float c = round_to<bf16>(v[2 * i + 1] * r * wv[2 * i + 1]);
+      if (silu) {
+        a = a * sigmoid_ieee(a);
+        c = c * sigmoid_ieee(c);
+      }
+      out[i] = pack_bf16x2(a, c);
+    }
+    if (in) *reinterpret_cast<uint4*>(y + row * C + 8 * sub) = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+// General form: one warp per row; C <= 32 * kMaxPerLane.
 template <typename T, int kMaxPerLane>
 __global__ void __launch_bounds__(kThreads) front_norm_kernel(const T* __restrict__ x,
                                                               const float* __restrict__ w,
@@ -107,6 +176,36 @@ __global__ void __launch_bounds__(kThreads) residual_silu_kernel(const T* __rest
   }
 }
 
+// BF16, C % 8 == 0: each thread handles one 16-byte vector of a row.
+__global__ void __launch_bounds__(kThreads) residual_silu_vec_kernel(const bf16* __restrict__ h,
+                                                                     const bf16* __restrict__ skip,
+                                                                     const int64_t* __restrict__ lengths,
+                                                                     bf16* __restrict__ y, int B, int Tn,
+                                                                     int F, int C) {
+  const int64_t vecs = static_cast<int64_t>(B) * Tn * F * (C / 8);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < vecs;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t row = i / (C / 8);
+    const int t = static_cast<int>((row / F) % Tn);
+    const int b = static_cast<int>(row / (static_cast<int64_t>(F) * Tn));
+    uint4 out = make_uint4(0, 0, 0, 0);
+    if (t < valid_len(lengths, b, Tn)) {
+      const uint4 a = reinterpret_cast<const uint4*>(h)[i];
+      const uint4 c = reinterpret_cast<const uint4*>(skip)[i];
+      const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, cc[4] = {c.x, c.y, c.z, c.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 p = unpack_bf16x2(aa[k]), q = unpack_bf16x2(cc[k]);
+        const float s0 = round_to<bf16>(p.x + q.x), s1 = round_to<bf16>(p.y + q.y);
+        o[k] = pack_bf16x2(s0 * sigmoid_ieee(s0), s1 * sigmoid_ieee(s1));
+      }
+      out = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    reinterpret_cast<uint4*>(y)[i] = out;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) bands_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                          int B, int Tn, int F, int C) {
@@ -128,9 +227,27 @@ template <typename T>
 int launch_front_norm(const void* x, const float* w, const int64_t* lengths, void* y, int B, int Tn,
                       int F, int C, float eps, int silu, cudaStream_t s) {
   const int64_t rows = static_cast<int64_t>(B) * Tn * F;
-  const int grid = grid_for(rows, kThreads / 32);
   auto X = static_cast<const T*>(x);
   auto Y = static_cast<T*>(y);
+  if constexpr (sizeof(T) == 2) {
+    const bool vec = (C == 8 || C == 16 || C == 32 || C == 64 || C == 128 || C == 256) &&
+                     reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(w) % 16 == 0;
+    if (vec) {
+      const int g = C / 8;
+      const int grid = grid_vec(rows * g);
+      switch (g) {
+        case 1: front_norm_vec_kernel<1><<<grid, kThreads, 0, s>>>(X, w, lengths, Y, B, Tn, F, eps, silu); break;
+        case 2: front_norm_vec_kernel<2><<<grid, kThreads, 0, s>>>(X, w, lengths, Y, B, Tn, F, eps, silu); break;
+        case 4: front_norm_vec_kernel<4><<<grid, kThreads, 0, s>>>(X, w, lengths, Y, B, Tn, F, eps, silu); break;
+        case 8: front_norm_vec_kernel<8><<<grid, kThreads, 0, s>>>(X, w, lengths, Y, B, Tn, F, eps, silu); break;
+        case 16: front_norm_vec_kernel<16><<<grid, kThreads, 0, s>>>(X, w, lengths, Y, B, Tn, F, eps, silu); break;
+        default: front_norm_vec_kernel<32><<<grid, kThreads, 0, s>>>(X, w, lengths, Y, B, Tn, F, eps, silu); break;
+      }
+      return launch_status();
+    }
+  }
+  const int grid = grid_for(rows, kThreads / 32);
   if (C <= 32)
     front_norm_kernel<T, 1><<<grid, kThreads, 0, s>>>(X, w, lengths, Y, B, Tn, F, C, eps, silu);
   else if (C <= 64)
@@ -171,6 +288,14 @@ int tf_front_residual_fwd(const void* h, const void* skip, int dtype, const int6
   const int st = tf::check_device();
   if (st != TF_OK) return st;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == TF_BF16 && channels % 8 == 0 && reinterpret_cast<uintptr_t>(h) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(skip) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0) {
+    const int64_t vecs = static_cast<int64_t>(batch) * time * freq * (channels / 8);
+    tf::residual_silu_vec_kernel<<<tf::grid_vec(vecs), tf::kThreads, 0, s>>>(
+        static_cast<const tf::bf16*>(h), static_cast<const tf::bf16*>(skip), lengths, static_cast<tf::bf16*>(y),
+        batch, time, freq, channels);
+    return tf::launch_status();
+  }
   const int grid = tf::grid_for(static_cast<int64_t>(batch) * time * freq * channels, tf::kThreads);
   if (dtype == TF_F32)
     tf::residual_silu_kernel<float><<<grid, tf::kThreads, 0, s>>>(

@@ -367,7 +367,62 @@ __global__ void __launch_bounds__(kThreads) masked_mean_kernel(const T* __restri
   }
 }
 
+// Depthwise Conv1d over time on [B, T, C] rows (kernels/primitives.py:73-87
+// `_dw_forward`, kernels/buffers.py:13-32 `depthwise_masked`):
+//   y[b, t, c] = t < len ? sum_k x[b, t + k - K/2, c] w[c, k] + bias[c] : 0,
+// zero padding outside [0, T). Inputs are rounded to BF16 first (the autocast
+// type the reference converts to), each product and sum is rounded separately
+// as in the reference kernel, and the result is BF16. Four channels per thread.
+template <typename TI, int K>
+__global__ void __launch_bounds__(kThreads) depthwise_kernel(const TI* __restrict__ x,
+                                                             const bf16* __restrict__ w,
+                                                             const bf16* __restrict__ bias,
+                                                             const int64_t* __restrict__ lengths,
+                                                             bf16* __restrict__ y, int B, int T, int C) {
+  const int quads = C / 4;
+  const int64_t total = static_cast<int64_t>(B) * T * quads;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int c = 4 * static_cast<int>(i % quads);
+    const int64_t bt = i / quads;
+    const int t = static_cast<int>(bt % T);
+    const int b = static_cast<int>(bt / T);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool live = t < clamp_len(lengths[b], T);
+    if (live) {
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int src = t + k - K / 2;
+        if (src < 0 || src >= T) continue;
+        const float4 xv = load4(x + (static_cast<int64_t>(b) * T + src) * C + c);
+        const float xs[4] = {bf16_round(xv.x), bf16_round(xv.y), bf16_round(xv.z), bf16_round(xv.w)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(xs[j], __bfloat162float(w[(c + j) * K + k])));
+      }
+      if (bias) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], __bfloat162float(bias[c + j]));
+      }
+    }
+    store4(y + bt * C + c, make_float4(acc[0], acc[1], acc[2], acc[3]));
+  }
+}
+
 }  // namespace
+
+template <typename TI>
+int launch_depthwise(const void* x, const bf16* w, const bf16* bias, const int64_t* lengths, bf16* y,
+                     int B, int T, int C, int K, cudaStream_t s) {
+  const int grid = grid_for(static_cast<int64_t>(B) * T * (C / 4), kThreads);
+  auto X = static_cast<const TI*>(x);
+  switch (K) {
+    case 3: depthwise_kernel<TI, 3><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 5: depthwise_kernel<TI, 5><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 7: depthwise_kernel<TI, 7><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    default: return TF_ERR_ARG;
+  }
+  return launch_status();
+}
 
 int launch_mask_rows(const void* x, const uint8_t* mask, void* y, int64_t rows, int64_t row_bytes,
                      cudaStream_t s) {
@@ -600,6 +655,26 @@ int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* 
     tf::masked_mean_kernel<tf::bf16><<<grid, tf::kThreads, 0, s>>>(static_cast<const tf::bf16*>(x), lengths,
                                                                    y, batch, seqlen, width);
   return tf::launch_status();
+}
+
+int tf_depthwise_masked_fwd(const void* x, int dtype, const void* w, const void* bias,
+                            const int64_t* lengths, void* y, int batch, int seqlen, int channels,
+                            int taps, void* stream) {
+  if (batch < 0 || seqlen < 0 || channels < 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (taps != 3 && taps != 5 && taps != 7) return TF_ERR_ARG;
+  if (channels % 4) return TF_ERR_LAYOUT;
+  if (batch == 0 || seqlen == 0 || channels == 0) return TF_OK;
+  if (!x || !w || !lengths || !y) return TF_ERR_ARG;
+  const uintptr_t align = dtype == TF_F32 ? 16 : 8;
+  if (reinterpret_cast<uintptr_t>(x) % align || reinterpret_cast<uintptr_t>(y) % 8) return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto W = static_cast<const tf::bf16*>(w);
+  auto Bs = static_cast<const tf::bf16*>(bias);
+  auto Y = static_cast<tf::bf16*>(y);
+  if (dtype == TF_F32) return tf::launch_depthwise<float>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
+  return tf::launch_depthwise<tf::bf16>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
 }
 
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,

@@ -97,3 +97,23 @@ def front_residual(h, skip, lengths):
     _lib.launch("tf_front_residual_fwd", dev, h.data_ptr(), skip.data_ptr(),
                 _lib.dtype_code(h, "front_residual"), lengths.data_ptr(), y.data_ptr(), b, t, f, c)
     return y
+
+
+def depthwise_masked(x, layer, lengths):
+    """Depthwise Conv1d (``layer``: groups = channels, odd kernel, 'same'
+    padding) over the time axis of [B, T, C] rows, with bias, zero past the
+    lengths; BF16 result (reference ``buffers.py:13-32``)."""
+    x = x.contiguous()
+    dev = _lib.require_cuda("depthwise_masked", x, lengths, layer.weight)
+    b, t, c = x.shape
+    k = layer.weight.shape[-1]
+    if layer.groups != c or layer.weight.shape[0] != c or 2 * layer.padding[0] + 1 != k:
+        raise ValueError("depthwise_masked: expected a depthwise Conv1d with 'same' padding")
+    w = layer.weight.detach().to(torch.bfloat16).reshape(c, k).contiguous()
+    bias = None if layer.bias is None else layer.bias.detach().to(torch.bfloat16).contiguous()
+    lengths = lengths.to(torch.int64).contiguous()
+    y = torch.empty((b, t, c), device=dev, dtype=torch.bfloat16)
+    _lib.launch("tf_depthwise_masked_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "depthwise_masked"),
+                w.data_ptr(), None if bias is None else bias.data_ptr(), lengths.data_ptr(), y.data_ptr(),
+                b, t, c, k)
+    return y

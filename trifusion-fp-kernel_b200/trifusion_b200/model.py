@@ -8,8 +8,9 @@ checkpoints load unchanged (``runtime.load_student``). The optimized backend
 norms, evidence norm, bidirectional mean norm), Pool4, the fused Mamba-3
 recurrence (with its B/C norms, controls and length mask), the valid-prefix
 reversal, the branch gate and SwiGLU. GEMMs and convolutions run on
-cuBLAS/cuDNN; attention on PyTorch's SDPA in FP32; the depthwise merge
-convolutions, rotary table application and grid interpolation are PyTorch ops.
+cuBLAS/cuDNN; attention on PyTorch's SDPA in FP32; the depthwise time
+convolutions run channels-last on the library too; the rotary table
+application and grid interpolation are PyTorch ops.
 ``backend="reference"`` evaluates the reference's PyTorch formulas instead.
 """
 
@@ -74,9 +75,15 @@ def _mask_rows(x, mask, optimized):
     return masked(x, mask)
 
 
-def _depthwise(x, conv, mask):
+def _depthwise(x, conv, mask, lengths, optimized):
     """Depthwise Conv1d over time ([B, T, C] layout) with bias, zero past each
-    length (the reference's ``depthwise_masked``)."""
+    length (the reference's ``depthwise_masked``). The optimized path is one
+    channels-last kernel; otherwise cuDNN on the transposed rows."""
+    bf16_out = torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+    if optimized and x.is_cuda and bf16_out and x.shape[-1] % 4 == 0:
+        from .kernels.buffers import depthwise_masked
+
+        return depthwise_masked(x, conv, lengths)
     dtype = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
     y = F.conv1d(x.to(dtype).transpose(1, 2), conv.weight.to(dtype), conv.bias.to(dtype),
                  padding=conv.padding, groups=conv.groups)
@@ -100,7 +107,7 @@ class LocalCNN(nn.Module):
         h = F.glu(self.up(x), dim=-1)
         if self.backend == "reference":
             h = masked(h, mask)
-        h = _depthwise(h, self.dw, mask)
+        h = _depthwise(h, self.dw, mask, lengths, self.backend != "reference")
         y = self.out(F.silu(self.norm(h)))
         return masked(y, mask) if self.backend == "reference" else y
 
@@ -190,7 +197,7 @@ class TriFusionBlock(nn.Module):
             mn = keep_zero(self.mn((mf.float() + mb.float()) * 0.5))
         s = torch.cat((cn, mn, an), -1)
         v = keep_zero(gated_concat(s, self.gate(s), self.backend))
-        conv = _depthwise(v, self.merge_dw, mask)
+        conv = _depthwise(v, self.merge_dw, mask, lengths, opt)
         r = keep_zero(x + self.dropout(self.merge(v + conv)))
         f = swiglu(self.gate_up(self.ff_norm(r)), self.backend)
         out = _mask_rows(r + self.dropout(self.down(f)), mask, opt)

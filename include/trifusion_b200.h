@@ -208,6 +208,23 @@ int tf_depthwise_masked_fwd(const void* x, int dtype, const void* w, const void*
                             const int64_t* lengths, void* y, int batch, int seqlen, int channels,
                             int taps, void* stream);
 
+/* Rotary q/k of the attention branch: x [B, T, 3, H, D] BF16 (the qkv projection)
+ * -> y [3, B, H, T, D] FP32 holding BF16-rounded values; q and k pairs rotated by
+ * the table angle (cosv/sinv [T, D/2] FP32), v copied. Replaces
+ * kernels/buffers.py:46-55 `RotaryQKV.apply` (`_rotary_qkv`,
+ * kernels/primitives.py:116-150) and the FP32 widening of attention.py:14-16. */
+int tf_rotary_qkv_fwd(const void* x, const float* cosv, const float* sinv, float* y, int batch,
+                      int time, int heads, int head_dim, void* stream);
+
+/* Interpolation from the pooled grid: y[b, t] = t < lengths[b] ?
+ * a + (z - a) alpha[b, t] : 0 with a = low[b, left[b, t]], z = low[b, right[b, t]];
+ * low [B, LT, D] BF16, y [B, T, D] BF16, D % 4 == 0. Replaces
+ * kernels/native.py:119-138 `interpolate` (`_interpolate`, native.py:103-117) and
+ * masking.py:71-80 `Grids.interpolate`. */
+int tf_interpolate_fwd(const void* low, const int64_t* left, const int64_t* right, const float* alpha,
+                       const int64_t* lengths, void* y, int batch, int time, int low_time, int width,
+                       void* stream);
+
 /* ------------------------------------------------------------------------
  * Spectrogram front end, on channels-last activations: a [B, C, T, F] tensor
  * stored as [B, T, F, C] (every (b, t, f) position one contiguous row of C).

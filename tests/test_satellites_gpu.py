@@ -277,3 +277,31 @@ def test_depthwise_masked_matches_conv1d(dtype, taps, width):
     y32, r32 = y.float(), ref.float()
     assert torch.all((y32 - r32).abs() <= BF16_ULP * r32.abs() + 1e-5), (y32 - r32).abs().max()
     assert (y.masked_select(~valid.expand_as(y)) == 0).all()
+
+
+def test_rotary_qkv_bit_exact_with_formula():
+    from trifusion_b200.kernels.buffers import RotaryQKV
+    from trifusion_b200.masking import rotary_table
+    from trifusion_b200.model import rope
+
+    b, t, heads, d = 4, 26, 6, 64
+    x = seeded((b, t, 3 * heads * d), 23, scale=2.0).to(DEV)
+    cos, sin = rotary_table(t, d, DEV)
+    y = RotaryQKV.apply(x, cos, sin, heads, torch.float32)
+    q, k, v = x.view(b, t, 3, heads, d).permute(2, 0, 3, 1, 4).unbind(0)
+    assert torch.equal(y[0], rope(q, cos, sin).float())
+    assert torch.equal(y[1], rope(k, cos, sin).float())
+    assert torch.equal(y[2], v.float())
+    assert torch.equal(RotaryQKV.apply(x, cos, sin, heads), y.to(BF))
+
+
+def test_interpolate_bit_exact_with_formula():
+    from trifusion_b200.kernels.native import interpolate
+    from trifusion_b200.masking import Grids
+
+    lengths = torch.tensor([101, 57, 1, 9], device=DEV)
+    grids = Grids.make(lengths, 101, 64)
+    low = seeded((4, 26, 384), 24).to(DEV)
+    y = interpolate(low, grids)
+    ref = Grids.make(lengths, 101, 64, native_kernels=False).interpolate(low)
+    assert torch.equal(y, ref)

@@ -48,6 +48,8 @@ SIGNATURES = {
     "tf_masked_mean_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
     "tf_end_gather_fwd": [_p, _p, _p, _i, _i, _q, _p],
     "tf_depthwise_masked_fwd": [_p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _p],
+    "tf_rotary_qkv_fwd": [_p, _p, _p, _p, _i, _i, _i, _i, _p],
+    "tf_interpolate_fwd": [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p],
     "tf_front_norm_fwd": [_p, _i, _p, _p, _p, _i, _i, _i, _i, _f, _i, _p],
     "tf_front_residual_fwd": [_p, _p, _i, _p, _p, _i, _i, _i, _i, _p],
     "tf_bands_fwd": [_p, _i, _p, _i, _i, _i, _i, _p],

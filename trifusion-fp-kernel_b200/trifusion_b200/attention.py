@@ -12,8 +12,10 @@ import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
 
-def masked_attention(q, k, v, mask):
-    out_dtype = q.dtype
+def masked_attention(q, k, v, mask, out_dtype=None):
+    """``out_dtype`` defaults to q's dtype; FP32 operands may be given directly
+    (the B200 rotary kernel writes them) with a BF16 result requested."""
+    out_dtype = q.dtype if out_dtype is None else out_dtype
     with torch.autocast(q.device.type, enabled=False), sdpa_kernel(
             [SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]):
         if out_dtype in (torch.float16, torch.bfloat16):

@@ -117,3 +117,25 @@ def depthwise_masked(x, layer, lengths):
                 w.data_ptr(), None if bias is None else bias.data_ptr(), lengths.data_ptr(), y.data_ptr(),
                 b, t, c, k)
     return y
+
+
+class RotaryQKV:
+    """Rotary q/k of the attention branch (reference ``buffers.py:46-55``):
+    x [B, T, 3*H*D] (the qkv projection) -> [3, B, H, T, D], q and k rotated by
+    the (cos, sin) table of the pooled grid, v unchanged. The kernel writes FP32
+    holding BF16-rounded values — the attention's own operand type; ``out_dtype``
+    BF16 gives the reference's return type."""
+
+    @staticmethod
+    def apply(x, cos, sin, heads, out_dtype=torch.bfloat16):
+        x = x.to(torch.bfloat16).contiguous()
+        dev = _lib.require_cuda("RotaryQKV", x, cos, sin)
+        b, t, width = x.shape
+        d = width // (3 * heads)
+        if 3 * heads * d != width or cos.shape[0] < t or cos.shape[-1] != d // 2:
+            raise ValueError("RotaryQKV: x must be [B, T, 3*heads*D] and the table [>=T, D/2]")
+        cos, sin = cos.float().contiguous(), sin.float().contiguous()
+        y = torch.empty((3, b, heads, t, d), device=dev, dtype=torch.float32)
+        _lib.launch("tf_rotary_qkv_fwd", dev, x.data_ptr(), cos.data_ptr(), sin.data_ptr(), y.data_ptr(),
+                    b, t, heads, d)
+        return y if out_dtype == torch.float32 else y.to(out_dtype)

@@ -112,3 +112,21 @@ def bands(x):
     y = torch.empty((b, t, 8, c), device=dev, dtype=x.dtype)
     _lib.launch("tf_bands_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "bands"), y.data_ptr(), b, t, f, c)
     return y
+
+
+def interpolate(low, grids):
+    """Pooled rows back to the main grid: ``a + (z - a) * alpha`` of the left and
+    right pooled rows, zero past each length (reference ``native.py:119-138``)."""
+    low = low.contiguous()
+    dev = _lib.require_cuda("interpolate", low, grids.left)
+    b, t = grids.left.shape
+    d = low.shape[-1]
+    if low.dtype != torch.bfloat16 or d % 4:
+        raise ValueError("interpolate: expects BF16 rows whose width is a multiple of 4")
+    y = low.new_empty((b, t, d))
+    left, right = grids.left.contiguous(), grids.right.contiguous()
+    alpha = grids.alpha.float().contiguous()
+    lengths = grids.lengths.to(torch.int64).contiguous()
+    _lib.launch("tf_interpolate_fwd", dev, low.data_ptr(), left.data_ptr(), right.data_ptr(), alpha.data_ptr(),
+                lengths.data_ptr(), y.data_ptr(), b, t, low.shape[1], d)
+    return y

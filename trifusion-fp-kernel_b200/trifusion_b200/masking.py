@@ -75,6 +75,10 @@ class Grids:
     def interpolate(self, low):
         """Back to the main grid: ``a + (b - a) * alpha`` of the two nearest pooled
         rows, zero past each length."""
+        if self.native_kernels and low.is_cuda and low.dtype == torch.bfloat16 and low.shape[-1] % 4 == 0:
+            from .kernels.native import interpolate
+
+            return interpolate(low, self)
         idx_shape = (*self.left.shape, low.shape[-1])
         a = low.gather(1, self.left.unsqueeze(-1).expand(idx_shape)).float()
         b = low.gather(1, self.right.unsqueeze(-1).expand(idx_shape)).float()

@@ -9,8 +9,8 @@ norms, evidence norm, bidirectional mean norm), Pool4, the fused Mamba-3
 recurrence (with its B/C norms, controls and length mask), the valid-prefix
 reversal, the branch gate and SwiGLU. GEMMs and convolutions run on
 cuBLAS/cuDNN; attention on PyTorch's SDPA in FP32; the depthwise time
-convolutions run channels-last on the library too; the rotary table
-application and grid interpolation are PyTorch ops.
+convolutions, the rotary q/k (writing the FP32 attention operands) and the
+grid interpolation run on the library too.
 ``backend="reference"`` evaluates the reference's PyTorch formulas instead.
 """
 
@@ -126,9 +126,19 @@ class GlobalAttention(nn.Module):
     def forward(self, x, grids):
         p = grids.pool(x)
         b, t = p.shape[:2]
-        q, k, v = self.qkv(p).view(b, t, 3, self.heads, self.head_dim).permute(2, 0, 3, 1, 4).unbind(0)
+        qkv = self.qkv(p)
+        mask = grids.low_mask[:, None, None, :]
+        if self.backend != "reference" and self.buffer_fusion and qkv.is_cuda and qkv.dtype == torch.bfloat16:
+            # One kernel: rotary q/k and the FP32 attention operands.
+            from .kernels.buffers import RotaryQKV
+
+            q, k, v = RotaryQKV.apply(qkv, grids.rope_cos, grids.rope_sin, self.heads, torch.float32).unbind(0)
+            y = masked_attention(q, k, v, mask, out_dtype=torch.bfloat16)
+            y = self.out(y.transpose(1, 2).reshape(b, t, -1))
+            return grids.interpolate(y)
+        q, k, v = qkv.view(b, t, 3, self.heads, self.head_dim).permute(2, 0, 3, 1, 4).unbind(0)
         q, k = rope(q, grids.rope_cos, grids.rope_sin), rope(k, grids.rope_cos, grids.rope_sin)
-        y = masked_attention(q, k, v, grids.low_mask[:, None, None, :])
+        y = masked_attention(q, k, v, mask)
         y = self.out(y.transpose(1, 2).reshape(b, t, -1))
         return grids.interpolate(y)
 

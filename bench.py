@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-eager", type=int, default=0, metavar="K",
+                    help="model workloads: run K untimed eager forwards and exit (for ncu launch lists)")
     return ap.parse_args()
 
 
@@ -453,8 +455,14 @@ def run_model(args, wl):
     audio, lengths, channels = synthetic_audio(b, n, lengths=lengths, seed=rank)
     with tempfile.TemporaryDirectory() as tmp:
         model = _student(dev, tmp)
-    engine = InferenceEngine(model, graphs=True, max_graphs=1)
     inputs = tuple(x.to(dev) for x in (audio, lengths, channels))
+    if args.profile_eager:
+        eager = InferenceEngine(model, graphs=False)
+        for _ in range(args.profile_eager):
+            eager(*inputs)
+        torch.cuda.synchronize(dev)
+        return
+    engine = InferenceEngine(model, graphs=True, max_graphs=1)
     flush = _l2_flush_buffer(dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 1)):

@@ -128,6 +128,56 @@ int tf_mamba_recurrence_fwd_static(const void* q, const void* k, const void* v,
                                    const float* k_norm_w, float eps, const int64_t* lengths,
                                    void* stream);
 
+/* ------------------------------------------------------------------------
+ * One launch for one or two recurrences over the same [B, T, H] shape (the
+ * forward and backward directions of a block's bidirectional pair,
+ * model.py:173-179), each optionally
+ *   - computing its controls from the projection views (prologue fusion of
+ *     mamba.py:58-63 / kernels/buffers.py:82-101): a_raw, ddt_raw [B,T,H] BF16
+ *     with dt = softplus(ddt + dt_bias[h]) and adt = min(-(relu(a) +
+ *     1/(1 - min(a, 0))), -a_floor) * dt, instead of adt/dt;
+ *   - reading and writing the valid prefix of every row in reverse time order
+ *     (`reverse`): local step t uses time len-1-t, so the backward direction
+ *     needs no reverse_valid copies (kernels/__init__.py:43-54) around it;
+ *     rows at or past the length come out zero in place.
+ * q_norm_w/k_norm_w and `lengths` act as in tf_mamba_recurrence_fwd. Strides are
+ * the 33 of tf_fused_mamba_fwd followed by a_raw (b, t, h) and ddt_raw (b, t, h).
+ * ------------------------------------------------------------------------ */
+typedef struct tf_recurrence_io {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* z;
+  const void* angles;
+  const float* qb;
+  const float* kb;
+  const float* d;
+  const float* adt;       /* [B,H,T] FP32, or NULL when a_raw/ddt_raw are given */
+  const float* dt;
+  const void* trap;
+  int trap_dtype;
+  const void* a_raw;      /* [B,T,H] BF16 views, or NULL */
+  const void* ddt_raw;
+  const float* dt_bias;   /* [H] */
+  float a_floor;
+  const float* q_norm_w;  /* [128] or NULL */
+  const float* k_norm_w;
+  void* out;
+  int64_t strides[39];
+  int reverse;
+} tf_recurrence_io;
+
+/* Workspace bytes for `count` (1 or 2) directions of [B, T, H]. */
+size_t tf_recurrence_workspace_size_multi(int count, int batch, int seqlen, int heads);
+
+/* Runs io[0..count-1] in one launch; the workspace rules of the header apply.
+ * No counterpart function in the reference: it replaces the pair of
+ * Mamba3Inference calls with their reverse_valid copies and the controls
+ * launches of model.py:175-179 / mamba.py:58-66. */
+int tf_mamba_recurrence_multi_fwd(const tf_recurrence_io* io, int count, int batch, int seqlen,
+                                  int heads, int groups, float eps, const int64_t* lengths,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* ========================================================================
  * Satellite operators on the recurrence path. Contiguous row-major tensors
  * (the reference wrappers call .contiguous() first); `dtype` is TF_F32 or

@@ -1,0 +1,138 @@
+"""GPU checks of the multi-direction recurrence launch (tf_mamba_recurrence_multi_fwd):
+
+* controls computed inside the launch from the projection views (prologue
+  fusion) equal the controls kernel followed by the recurrence, bit for bit;
+* a reversed direction equals reversing the valid prefix of the projection
+  rows, running forward, and reversing the output back, bit for bit (short rows
+  that fold every predecessor and long rows that use the look-back);
+* both directions in one launch equal two separate launches, bit for bit;
+* the reversed direction against the CPU oracle, at the recurrence tolerance.
+"""
+
+import pytest
+import torch
+
+from parity import assert_recurrence_close, oracle_out
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from trifusion_b200 import fused_recurrence  # noqa: E402
+from trifusion_b200.kernels.buffers import mamba_controls  # noqa: E402
+from trifusion_b200.mamba_fused import fused_recurrence_multi  # noqa: E402
+from trifusion_b200.synthetic import norm_weight  # noqa: E402
+
+DEV = "cuda"
+H, N, R = 12, 128, 32
+WIDTH = 2 * 768 + 2 * N + 3 * H + R  # the in_proj row of a dim-384 block: 1860
+
+
+def projection(b, t, seed):
+    """A [B, T, 1860] BF16 projection with the model's value scales per field."""
+    g = torch.Generator().manual_seed(seed)
+    p = torch.randn(b, t, WIDTH, generator=g)
+    p[..., 1536:1792] *= 1.0                     # k, q (normalised in the launch)
+    p[..., 1792:1804] = p[..., 1792:1804] * 0.5  # ddt (dt = softplus(ddt - 4 + ...))
+    p[..., 1804:1816] *= 2.0                     # a
+    return p.to(torch.bfloat16).to(DEV)
+
+
+def split(p, b, t):
+    z, v, k, q, ddt, a, trap, angles = p.split([768, 768, N, N, H, H, H, R], -1)
+    heads = (b, t, H, 64)
+    return dict(q=q.reshape(b, t, 1, N), k=k.reshape(b, t, 1, N), v=v.reshape(heads), z=z.reshape(heads),
+                trap=trap.transpose(1, 2), angles=angles.unsqueeze(2).expand(b, t, H, R), a=a, ddt=ddt)
+
+
+def params(seed):
+    g = torch.Generator().manual_seed(seed)
+    return dict(qb=(1 + 0.1 * torch.randn(H, N, generator=g)).to(DEV),
+                kb=(1 + 0.1 * torch.randn(H, N, generator=g)).to(DEV),
+                d=torch.randn(H, generator=g).to(DEV),
+                dt_bias=(-4 + 0.3 * torch.randn(H, generator=g)).to(DEV),
+                q_norm=norm_weight(N, seed + 1).to(DEV), k_norm=norm_weight(N, seed + 2).to(DEV))
+
+
+def direction(p, b, t, prm, reverse=False):
+    s = split(p, b, t)
+    return dict(q=s["q"], k=s["k"], v=s["v"], z=s["z"], trap=s["trap"], angles=s["angles"], qb=prm["qb"],
+                kb=prm["kb"], d=prm["d"], a_raw=s["a"], ddt_raw=s["ddt"], dt_bias=prm["dt_bias"],
+                a_floor=1e-4, q_norm=prm["q_norm"], k_norm=prm["k_norm"], reverse=reverse)
+
+
+def reverse_rows(x, lengths):
+    """Reverse every row's valid prefix along dim 1; rows past the length stay."""
+    b, t = x.shape[:2]
+    pos = torch.arange(t, device=x.device)[None, :]
+    idx = torch.where(pos < lengths[:, None], lengths[:, None] - 1 - pos, pos)
+    return torch.take_along_dim(x, idx.view(b, t, *([1] * (x.dim() - 2))), dim=1)
+
+
+CASES = [(16, 200, [200, 137, 1, 0, 64, 199, 3, 128, 65, 200, 150, 77, 190, 13, 100, 180]),
+         (3, 700, [700, 513, 64])]
+
+
+@pytest.mark.parametrize("b,t,lens", CASES)
+def test_controls_inside_the_launch_equal_the_controls_kernel(b, t, lens):
+    p = projection(b, t, 1)
+    prm = params(2)
+    lengths = torch.tensor(lens, device=DEV)
+    fused = fused_recurrence_multi([direction(p, b, t, prm)], lengths=lengths)[0]
+    s = split(p, b, t)
+    adt, dt = mamba_controls(s["a"], s["ddt"], prm["dt_bias"], 1e-4)
+    ref = fused_recurrence(s["q"], s["k"], s["v"], adt, dt, s["trap"], prm["qb"], prm["kb"], s["angles"],
+                           prm["d"], s["z"], q_norm=prm["q_norm"], k_norm=prm["k_norm"], lengths=lengths)
+    assert torch.equal(fused, ref)
+
+
+@pytest.mark.parametrize("b,t,lens", CASES)
+def test_reversed_direction_equals_reversed_rows(b, t, lens):
+    p = projection(b, t, 3)
+    prm = params(4)
+    lengths = torch.tensor(lens, device=DEV)
+    rev = fused_recurrence_multi([direction(p, b, t, prm, reverse=True)], lengths=lengths)[0]
+    fwd_of_reversed = fused_recurrence_multi([direction(reverse_rows(p, lengths), b, t, prm)], lengths=lengths)[0]
+    assert torch.equal(rev, reverse_rows(fwd_of_reversed, lengths))
+    # rows at or past each length are zero
+    pad = torch.arange(t, device=DEV)[None, :] >= lengths[:, None]
+    assert (rev[pad] == 0).all()
+
+
+@pytest.mark.parametrize("b,t,lens", CASES)
+def test_pair_launch_equals_two_launches(b, t, lens):
+    pf, pb = projection(b, t, 5), projection(b, t, 6)
+    prf, prb = params(7), params(8)
+    lengths = torch.tensor(lens, device=DEV)
+    yf, yb = fused_recurrence_multi([direction(pf, b, t, prf), direction(pb, b, t, prb, reverse=True)],
+                                    lengths=lengths)
+    sf = fused_recurrence_multi([direction(pf, b, t, prf)], lengths=lengths)[0]
+    sb = fused_recurrence_multi([direction(pb, b, t, prb, reverse=True)], lengths=lengths)[0]
+    assert torch.equal(yf, sf) and torch.equal(yb, sb)
+
+
+def test_reversed_direction_against_oracle():
+    b, t = 2, 150
+    lengths = torch.tensor([150, 97], device=DEV)
+    p = projection(b, t, 9)
+    prm = params(10)
+    rev = fused_recurrence_multi([direction(p, b, t, prm, reverse=True)], lengths=lengths)[0]
+    # Oracle: the reversed rows, controls and norms in PyTorch FP32, the FP64 recurrence.
+    pr = reverse_rows(p, lengths)
+    s = split(pr, b, t)
+    a, ddt = s["a"].float(), s["ddt"].float()
+    control = -(a.clamp(min=0) + 1 / (1 - a.clamp(max=0))).clamp(min=1e-4)
+    dt = torch.nn.functional.softplus(ddt + prm["dt_bias"])
+    adt, dt = (control * dt).transpose(1, 2), dt.transpose(1, 2)
+
+    def rms(x, w):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w).to(torch.bfloat16)
+
+    args = (rms(s["q"], prm["q_norm"]), rms(s["k"], prm["k_norm"]), s["v"], adt, dt, s["trap"], prm["qb"],
+            prm["kb"], s["angles"], prm["d"], s["z"])
+    ref = torch.as_tensor(oracle_out(args))
+    pad = torch.arange(t)[None, :] >= lengths.cpu()[:, None]
+    ref[pad] = 0
+    assert_recurrence_close(reverse_rows(rev, lengths).float().cpu(), ref, "reversed direction")

@@ -27,13 +27,31 @@ struct RecurrenceParams {
   float eps;
   int trap_bf16;
   int B, T, H, Hq;
+  // Raw controls (mamba.py:58-63 computed in the producer instead of adt/dt):
+  // a, ddt [B,T,H] BF16 views of the projection, dt_bias [H], A floor.
+  const bf16* a_raw;
+  const bf16* ddt_raw;
+  int64_t sar[3], sdr[3];
+  const float* dt_bias;
+  float a_floor;
+  int raw_controls;
+  // Reverse: local step t of a row reads and writes time len-1-t (the backward
+  // direction of the bidirectional pair, model.py:175-179, without the copies).
+  int reverse;
+};
+
+// One launch may run up to two directions over the same (B, T, H) shape; their
+// units share the ticket space (chunk-major, then direction).
+struct RecurrenceLaunch {
+  RecurrenceParams dir[2];
+  int ndir;
 };
 
 // Persistent chunk-parallel tensor-core kernel (any T). `workspace` must hold
 // recurrence_workspace_bytes(B, T, H) bytes, zero-filled before its first use
 // and then reused unchanged. Returns 0 on success.
-size_t recurrence_workspace_bytes(int B, int T, int H);
-int launch_recurrence_persistent(const RecurrenceParams& p, void* workspace, size_t workspace_bytes,
+size_t recurrence_workspace_bytes(int B, int T, int H, int ndir = 1);
+int launch_recurrence_persistent(const RecurrenceLaunch& launch, void* workspace, size_t workspace_bytes,
                                  cudaStream_t stream);
 // Device error word set when a kernel's bounded wait gave up (synchronous read).
 int read_device_error(int reset);

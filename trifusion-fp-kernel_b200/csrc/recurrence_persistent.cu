@@ -77,6 +77,7 @@ constexpr uint32_t kOffMisc = kOffPhase + 64 * 33 * 4;
 struct SlotHeader {
   int unit;  // -1: no more work
   int b, h, c, nv;
+  int dir, teff;        // direction of the unit, valid length of its row
   float cs[kChunk];     // decay cumsum (log2 units)
   float gamma[kChunk];
   float qe[kChunk];     // q16 row exponents
@@ -223,13 +224,25 @@ __device__ __forceinline__ float silu_tanh(float z) {
 __device__ int g_device_error = 0;  // set when a bounded wait gives up
 
 struct Shape {
-  int B, H, nck, units;
+  int B, H, nck, units, ndir;
 };
-__device__ __forceinline__ void decode_unit(int u, const Shape& s, int& b, int& h, int& c) {
+// Units are numbered chunk-major, then direction: u = ((c*ndir + dir)*B + b)*H + h.
+__device__ __forceinline__ void decode_unit(int u, const Shape& s, int& b, int& h, int& c, int& dir) {
   h = u % s.H;
-  const int rest = u / s.H;
+  int rest = u / s.H;
   b = rest % s.B;
-  c = rest / s.B;
+  rest /= s.B;
+  dir = rest % s.ndir;
+  c = rest / s.ndir;
+}
+__device__ __forceinline__ int unit_index(const Shape& s, int c, int dir, int b, int h) {
+  return ((c * s.ndir + dir) * s.B + b) * s.H + h;
+}
+// The controls of mamba.py:58-63 / kernels/primitives.py:190-216, in the same
+// FP32 operations as the standalone controls kernel.
+__device__ __forceinline__ float softplus_dt(float v) { return v > 20.f ? v : log1pf(expf(v)); }
+__device__ __forceinline__ float a_control(float a, float floor_) {
+  return fminf(-(fmaxf(a, 0.f) + 1.f / (1.f - fminf(a, 0.f))), -floor_);
 }
 __device__ __forceinline__ unsigned char* unit_ws(unsigned char* ws, int u) {
   return ws + kWsHeader + static_cast<size_t>(u) * kUnitBytes;
@@ -248,9 +261,12 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, 
 }
 
 // =====================================================================================
-template <int kVec>
-__global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(RecurrenceParams p,
-                                                                              unsigned char* ws) {
+// kDirs: directions in the launch (1 or 2), a compile-time constant so that a
+// one-direction launch reads its parameters at fixed offsets. kExt: reversed
+// rows and in-launch controls are possible (otherwise compiled out).
+template <int kVec, int kDirs, bool kExt>
+__device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, const RecurrenceParams& pd1,
+                                                unsigned char* ws) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -260,7 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
   uint32_t* ws_epoch = reinterpret_cast<uint32_t*>(ws);
   int* ws_ticket = reinterpret_cast<int*>(ws + 128);
   int* ws_done = reinterpret_cast<int*>(ws + 256);
-  const Shape shp{p.B, p.H, (p.T + kChunk - 1) / kChunk, ((p.T + kChunk - 1) / kChunk) * p.B * p.H};
+  const RecurrenceParams& p0 = pd0;
+  const int nck = (p0.T + kChunk - 1) / kChunk;
+  const Shape shp{p0.B, p0.H, nck, nck * kDirs * p0.B * p0.H, kDirs};
   const bool lookback = shp.nck > kLookbackChunks;
 
   if (warp == 0) {
@@ -309,8 +327,10 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
         }
         break;
       }
-      int b, h, c;
-      decode_unit(u, shp, b, h, c);
+      int b, h, c, dir;
+      decode_unit(u, shp, b, h, c, dir);
+      if (kDirs == 1) dir = 0;
+      const RecurrenceParams& p = (kDirs == 1 || dir == 0) ? pd0 : pd1;
       int T_eff = p.T;
       if (p.lengths) {
         const int64_t len = p.lengths[b];
@@ -330,10 +350,13 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
         continue;
       }
       const bool row_ok = t < nv;
+      // Time of local step x of this row: x itself, or len-1-x for a reversed row.
+      const bool rev = kExt && p.reverse != 0;
+      auto src_row = [&](int64_t x) -> int64_t { return rev ? (T_eff - 1 - x) : x; };
       // ---- loads ------------------------------------------------------------------
       uint4 qraw[4], kraw[4], vraw[2], zraw[2];
       {
-        const int64_t pos = c0 + t;
+        const int64_t pos = row_ok ? src_row(c0 + t) : 0;
         const bf16* qrow = p.q + b * p.sq[0] + pos * p.sq[1] + (h / (p.H / p.Hq)) * p.sq[2];
         const bf16* krow = p.k + b * p.sk[0] + pos * p.sk[1] + (h / (p.H / p.Hq)) * p.sk[2];
         const bf16* vrow = p.v + b * p.sv[0] + pos * p.sv[1] + h * p.sv[2];
@@ -358,14 +381,34 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
         const char* trbase =
             static_cast<const char*>(p.trap) + (b * p.str[0] + h * p.str[1]) * (p.trap_bf16 ? 2 : 4);
         const int64_t tt = c0 + tid;
-        if (tid < nv) {
-          c_dt = dtbase[tt * p.sdt[2]];
-          c_tr = load_trap(p, trbase, tt * p.str[2]);
-          c_adt = adtbase[tt * p.sadt[2]];
-        }
-        if (tt + 1 < T_eff) {
-          c_dn = dtbase[(tt + 1) * p.sdt[2]];
-          c_tn = load_trap(p, trbase, (tt + 1) * p.str[2]);
+        if (kExt && p.raw_controls) {
+          // dt = softplus(ddt + dt_bias), adt = A dt from the projection views.
+          const bf16* abase = p.a_raw + b * p.sar[0] + h * p.sar[2];
+          const bf16* dbase = p.ddt_raw + b * p.sdr[0] + h * p.sdr[2];
+          const float bias = p.dt_bias[h];
+          if (tid < nv) {
+            const int64_t sr = src_row(tt);
+            c_dt = softplus_dt(bf2f(dbase[sr * p.sdr[1]]) + bias);
+            c_adt = a_control(bf2f(abase[sr * p.sar[1]]), p.a_floor) * c_dt;
+            c_tr = load_trap(p, trbase, sr * p.str[2]);
+          }
+          if (tt + 1 < T_eff) {
+            const int64_t sn = src_row(tt + 1);
+            c_dn = softplus_dt(bf2f(dbase[sn * p.sdr[1]]) + bias);
+            c_tn = load_trap(p, trbase, sn * p.str[2]);
+          }
+        } else {
+          if (tid < nv) {
+            const int64_t sr = src_row(tt);
+            c_dt = dtbase[sr * p.sdt[2]];
+            c_tr = load_trap(p, trbase, sr * p.str[2]);
+            c_adt = adtbase[sr * p.sadt[2]];
+          }
+          if (tt + 1 < T_eff) {
+            const int64_t sn = src_row(tt + 1);
+            c_dn = dtbase[sn * p.sdt[2]];
+            c_tn = load_trap(p, trbase, sn * p.str[2]);
+          }
         }
       }
       float araw[8];
@@ -374,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int tt = warp * 8 + i;
-          araw[i] = tt < nv ? bf2f(abase[static_cast<int64_t>(c0 + tt) * p.sa[1] + lane * p.sa[3]]) : 0.f;
+          araw[i] = tt < nv ? bf2f(abase[src_row(c0 + tt) * p.sa[1] + lane * p.sa[3]]) : 0.f;
         }
       }
       // The slot's previous unit must be fully retired before it is rewritten.
@@ -592,6 +635,8 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
         hd.h = h;
         hd.c = c;
         hd.nv = nv;
+        hd.dir = dir;
+        hd.teff = T_eff;
         hd.gtot = ex2_approx(total);
       }
       fence_async_smem();
@@ -635,7 +680,8 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
       ok &= mbar_wait(&mi.ready[slot], ph);
       const int u = hd.unit;
       if (u < 0) break;
-      const int b = hd.b, h = hd.h, c = hd.c;
+      const int b = hd.b, h = hd.h, c = hd.c, dir = kDirs == 1 ? 0 : hd.dir;
+      const RecurrenceParams& p = (kDirs == 1 || dir == 0) ? pd0 : pd1;
       const uint32_t sb = base + slot * kSlotBytes;
       const uint32_t tm = tmem0 + slot * kSlotCols;
       unsigned char* uws = unit_ws(ws, u);
@@ -761,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
         }
       };
       auto fetch = [&](int x, uint4 (&w)[4], float& f, float& gx, float& th) {
-        const unsigned char* xws = unit_ws(ws, (x * shp.B + b) * shp.H + h);
+        const unsigned char* xws = unit_ws(ws, unit_index(shp, x, dir, b, h));
         uint32_t seen = 0;
         ok &= wait_flag(reinterpret_cast<const uint32_t*>(xws + kUnitFlag), epoch, kFlagAgg, seen);
         const __half* agg = reinterpret_cast<const __half*>(xws + kUnitAgg) + n * 64 + 32 * chalf;
@@ -782,7 +828,7 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
             int y = c - 1;
             for (; y >= 0; --y) {
               uint32_t seen = 0;
-              const int ub = (y * shp.B + b) * shp.H + h;
+              const int ub = unit_index(shp, y, dir, b, h);
               ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, ub) + kUnitFlag), epoch, kFlagAgg, seen);
               if (static_cast<int>(seen - epoch) >= static_cast<int>(kFlagIncl)) break;
             }
@@ -791,7 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
           bar_sync_n(kBarEpilogue, kEpilogueThreads);
           const int y = mi.lookback_start;
           if (y >= 0) {
-            const unsigned char* yws = unit_ws(ws, (y * shp.B + b) * shp.H + h);
+            const unsigned char* yws = unit_ws(ws, unit_index(shp, y, dir, b, h));
             (void)ld_acquire_u32(reinterpret_cast<const uint32_t*>(yws + kUnitFlag));
             const float* incl = reinterpret_cast<const float*>(yws + kUnitIncl) + n * 64 + 32 * chalf;
 #pragma unroll
@@ -921,7 +967,9 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
         // 64 rows x 8 16-byte chunks over 256 threads: row et/4, chunks 2*(et&3), +1.
         const int r = et >> 2;
         if (c0 + r < p.T) {
-          bf16* orow = p.out + b * p.so[0] + static_cast<int64_t>(c0 + r) * p.so[1] + h * p.so[2];
+          // Valid rows of a reversed row go back to time len-1-x; padding stays put.
+          const int64_t row = (kExt && p.reverse && r < nv) ? static_cast<int64_t>(hd.teff - 1 - (c0 + r)) : c0 + r;
+          bf16* orow = p.out + b * p.so[0] + row * p.so[1] + h * p.so[2];
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             const int e = 8 * (2 * (et & 3) + q);
@@ -954,7 +1002,21 @@ __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(Recu
   }
 }
 
-int alignment_class(const RecurrenceParams& p) {
+// One direction: a single parameter block (the launch copies less).
+template <int kVec, bool kExt>
+__global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(const __grid_constant__ RecurrenceParams p,
+                                                                              unsigned char* ws) {
+  recurrence_body<kVec, 1, kExt>(p, p, ws);
+}
+// Both directions of a bidirectional pair in one launch.
+template <int kVec>
+__global__ void __launch_bounds__(kThreads, 1) recurrence_pair_kernel(const __grid_constant__ RecurrenceParams p0,
+                                                                        const __grid_constant__ RecurrenceParams p1,
+                                                                        unsigned char* ws) {
+  recurrence_body<kVec, 2, true>(p0, p1, ws);
+}
+
+int alignment_class_one(const RecurrenceParams& p) {
   auto rows_aligned = [](const void* ptr, const int64_t* st, int nd, int bytes) {
     if (reinterpret_cast<uintptr_t>(ptr) % bytes) return false;
     for (int i = 0; i < nd; ++i)
@@ -984,32 +1046,53 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
-template <int kVec>
-int launch(const RecurrenceParams& p, unsigned char* ws, cudaStream_t stream) {
-  auto kernel = recurrence_persistent_kernel<kVec>;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
-  const int units = ((p.T + kChunk - 1) / kChunk) * p.B * p.H;
+int alignment_class(const RecurrenceLaunch& L) {
+  int a = alignment_class_one(L.dir[0]);
+  if (L.ndir > 1) a = a < alignment_class_one(L.dir[1]) ? a : alignment_class_one(L.dir[1]);
+  return a;
+}
+
+template <int kVec, int kDirs, bool kExt>
+int launch(const RecurrenceLaunch& L, unsigned char* ws, cudaStream_t stream) {
+  const RecurrenceParams& p = L.dir[0];
+  const int units = ((p.T + kChunk - 1) / kChunk) * p.B * p.H * L.ndir;
   const int grid = units < sm_count() ? units : sm_count();
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, ws);
+  if constexpr (kDirs == 2) {
+    auto kernel = recurrence_pair_kernel<kVec>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(L.dir[0], L.dir[1], ws);
+  } else {
+    auto kernel = recurrence_persistent_kernel<kVec, kExt>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(L.dir[0], ws);
+  }
   return 0;
 }
 
 }  // namespace
 
-size_t recurrence_workspace_bytes(int B, int T, int H) {
-  const size_t units = static_cast<size_t>((T + kChunk - 1) / kChunk) * B * H;
+size_t recurrence_workspace_bytes(int B, int T, int H, int ndir) {
+  const size_t units = static_cast<size_t>((T + kChunk - 1) / kChunk) * B * H * ndir;
   return kWsHeader + units * kUnitBytes;
 }
 
-int launch_recurrence_persistent(const RecurrenceParams& p, void* workspace, size_t workspace_bytes,
+int launch_recurrence_persistent(const RecurrenceLaunch& L, void* workspace, size_t workspace_bytes,
                                  cudaStream_t stream) {
-  if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H)) return 1;
+  const RecurrenceParams& p = L.dir[0];
+  if (L.ndir < 1 || L.ndir > 2) return 1;
+  if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H, L.ndir)) return 1;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
-  switch (alignment_class(p)) {
-    case 16: return launch<16>(p, ws, stream);
-    case 8: return launch<8>(p, ws, stream);
-    default: return launch<2>(p, ws, stream);
-  }
+  const int a = alignment_class(L);
+  bool ext = false;
+  for (int i = 0; i < L.ndir; ++i) ext = ext || L.dir[i].reverse || L.dir[i].raw_controls;
+  if (L.ndir == 2)
+    return a == 16 ? launch<16, 2, true>(L, ws, stream)
+                   : a == 8 ? launch<8, 2, true>(L, ws, stream) : launch<2, 2, true>(L, ws, stream);
+  if (ext)
+    return a == 16 ? launch<16, 1, true>(L, ws, stream)
+                   : a == 8 ? launch<8, 1, true>(L, ws, stream) : launch<2, 1, true>(L, ws, stream);
+  return a == 16 ? launch<16, 1, false>(L, ws, stream)
+                 : a == 8 ? launch<8, 1, false>(L, ws, stream) : launch<2, 1, false>(L, ws, stream);
 }
 
 int read_device_error(int reset) {

@@ -107,7 +107,11 @@ int recurrence_entry(const void* q, const void* k, const void* v, const float* a
   if (!workspace) return TF_ERR_ARG;
   if (workspace_bytes < recurrence_workspace_bytes(batch, seqlen, heads)) return TF_ERR_SIZE;
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  st = launch_recurrence_persistent(p, workspace, workspace_bytes, cs);
+  RecurrenceLaunch launch{};
+  launch.dir[0] = p;
+  launch.dir[1] = p;
+  launch.ndir = 1;
+  st = launch_recurrence_persistent(launch, workspace, workspace_bytes, cs);
   if (st != 0) {
     const int ls = launch_status();
     return ls != TF_OK ? ls : TF_ERR_LAUNCH;
@@ -115,9 +119,93 @@ int recurrence_entry(const void* q, const void* k, const void* v, const float* a
   return launch_status();
 }
 
+// One direction's parameters from the public argument record; validation as in
+// recurrence_entry. Returns TF_OK or an error status.
+int params_from_io(const tf_recurrence_io& io, int batch, int seqlen, int heads, int groups, float eps,
+                   const int64_t* lengths, RecurrenceParams& p) {
+  if (io.trap_dtype != TF_F32 && io.trap_dtype != TF_BF16) return TF_ERR_ARG;
+  const bool raw = io.a_raw != nullptr || io.ddt_raw != nullptr;
+  if (raw && (!io.a_raw || !io.ddt_raw || !io.dt_bias)) return TF_ERR_ARG;
+  if (!raw && (!io.adt || !io.dt)) return TF_ERR_ARG;
+  if (!io.q || !io.k || !io.v || !io.z || !io.angles || !io.trap || !io.qb || !io.kb || !io.d || !io.out)
+    return TF_ERR_ARG;
+  p = RecurrenceParams{};
+  p.q = static_cast<const bf16*>(io.q);
+  p.k = static_cast<const bf16*>(io.k);
+  p.v = static_cast<const bf16*>(io.v);
+  p.z = static_cast<const bf16*>(io.z);
+  p.ang = static_cast<const bf16*>(io.angles);
+  p.adt = io.adt;
+  p.dt = io.dt;
+  p.trap = io.trap;
+  p.trap_bf16 = io.trap_dtype == TF_BF16;
+  p.qb = io.qb;
+  p.kb = io.kb;
+  p.d = io.d;
+  p.qw = io.q_norm_w;
+  p.kw = io.k_norm_w;
+  p.eps = eps;
+  p.lengths = lengths;
+  p.out = static_cast<bf16*>(io.out);
+  const int64_t* s = io.strides;
+  for (int i = 0; i < 4; ++i) p.sq[i] = s[i];
+  for (int i = 0; i < 4; ++i) p.sk[i] = s[4 + i];
+  for (int i = 0; i < 4; ++i) p.sv[i] = s[8 + i];
+  for (int i = 0; i < 3; ++i) p.sadt[i] = s[12 + i];
+  for (int i = 0; i < 3; ++i) p.sdt[i] = s[15 + i];
+  for (int i = 0; i < 3; ++i) p.str[i] = s[18 + i];
+  for (int i = 0; i < 4; ++i) p.sa[i] = s[21 + i];
+  for (int i = 0; i < 4; ++i) p.sz[i] = s[25 + i];
+  for (int i = 0; i < 4; ++i) p.so[i] = s[29 + i];
+  for (int i = 0; i < 3; ++i) p.sar[i] = s[33 + i];
+  for (int i = 0; i < 3; ++i) p.sdr[i] = s[36 + i];
+  if (p.sq[3] != 1 || p.sk[3] != 1 || p.sv[3] != 1 || p.sz[3] != 1 || p.so[3] != 1) return TF_ERR_LAYOUT;
+  p.raw_controls = raw ? 1 : 0;
+  p.a_raw = static_cast<const bf16*>(io.a_raw);
+  p.ddt_raw = static_cast<const bf16*>(io.ddt_raw);
+  p.dt_bias = io.dt_bias;
+  p.a_floor = io.a_floor;
+  p.reverse = io.reverse ? 1 : 0;
+  p.B = batch;
+  p.T = seqlen;
+  p.H = heads;
+  p.Hq = groups;
+  return TF_OK;
+}
+
 }  // namespace tf
 
 extern "C" {
+
+size_t tf_recurrence_workspace_size_multi(int count, int batch, int seqlen, int heads) {
+  if (count < 1 || count > 2 || batch <= 0 || seqlen <= 0 || heads <= 0) return 0;
+  return tf::recurrence_workspace_bytes(batch, seqlen, heads, count);
+}
+
+int tf_mamba_recurrence_multi_fwd(const tf_recurrence_io* io, int count, int batch, int seqlen,
+                                  int heads, int groups, float eps, const int64_t* lengths,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (!io || count < 1 || count > 2) return TF_ERR_ARG;
+  if (batch < 0 || seqlen < 0 || heads < 0 || groups <= 0 || heads % groups) return TF_ERR_ARG;
+  if (batch == 0 || seqlen == 0 || heads == 0) return TF_OK;
+  tf::RecurrenceLaunch launch{};
+  for (int i = 0; i < count; ++i) {
+    const int st = tf::params_from_io(io[i], batch, seqlen, heads, groups, eps, lengths, launch.dir[i]);
+    if (st != TF_OK) return st;
+  }
+  if (count == 1) launch.dir[1] = launch.dir[0];
+  launch.ndir = count;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  if (!workspace) return TF_ERR_ARG;
+  if (workspace_bytes < tf::recurrence_workspace_bytes(batch, seqlen, heads, count)) return TF_ERR_SIZE;
+  if (tf::launch_recurrence_persistent(launch, workspace, workspace_bytes, static_cast<cudaStream_t>(stream)) != 0) {
+    const int ls = tf::launch_status();
+    return ls != TF_OK ? ls : TF_ERR_LAUNCH;
+  }
+  return tf::launch_status();
+}
+
 
 const char* tf_status_string(int status) {
   switch (status) {

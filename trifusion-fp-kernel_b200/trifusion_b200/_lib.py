@@ -35,6 +35,8 @@ SIGNATURES = {
                                 _i, _i, _i, _i, _p, _p, _f, _p, _p, _z, _p],
     "tf_mamba_recurrence_fwd_static": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
                                        _i, _i, _i, _i, _p, _p, _f, _p, _p],
+    "tf_recurrence_workspace_size_multi": [_i, _i, _i, _i],
+    "tf_mamba_recurrence_multi_fwd": [_p, _i, _i, _i, _i, _i, _f, _p, _p, _z, _p],
     # Satellite operators (argument order of include/trifusion_b200.h).
     "tf_rms_fwd": [_p, _i, _p, _p, _q, _i, _f, _p],
     "tf_evidence_norm_fwd": [_p, _i, _p, _p, _i, _p, _p, _p, _q, _i, _f, _p],
@@ -55,7 +57,20 @@ SIGNATURES = {
     "tf_bands_fwd": [_p, _i, _p, _i, _i, _i, _i, _p],
 }
 _RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p,
-             "tf_recurrence_workspace_size": ctypes.c_size_t}
+             "tf_recurrence_workspace_size": ctypes.c_size_t,
+             "tf_recurrence_workspace_size_multi": ctypes.c_size_t}
+
+
+class RecurrenceIO(ctypes.Structure):
+    """``tf_recurrence_io`` of include/trifusion_b200.h (one direction of a launch)."""
+
+    _fields_ = [
+        ("q", _p), ("k", _p), ("v", _p), ("z", _p), ("angles", _p),
+        ("qb", _p), ("kb", _p), ("d", _p), ("adt", _p), ("dt", _p),
+        ("trap", _p), ("trap_dtype", _i), ("a_raw", _p), ("ddt_raw", _p),
+        ("dt_bias", _p), ("a_floor", _f), ("q_norm_w", _p), ("k_norm_w", _p),
+        ("out", _p), ("strides", ctypes.c_int64 * 39), ("reverse", _i),
+    ]
 
 _lib = None
 

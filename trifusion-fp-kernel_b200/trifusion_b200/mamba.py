@@ -2,12 +2,13 @@
 ``mamba.py``), running the B200 recurrence.
 
 Optimized path (``fused_recurrence=True``, what ``load_student`` sets): one
-cuBLAS GEMM (``in_proj``), the controls kernel, ONE recurrence launch that
-also applies the C/B RMSNorm of the raw q/k rows and the length mask, and one
-cuBLAS GEMM (``out_proj``). With ``fused_recurrence=False`` the norms and the
-mask run as separate kernels around ``fused_mamba`` (the reference's
-unfused arrangement); ``backend="reference"`` evaluates the norms and controls
-with the reference's PyTorch formulas.
+cuBLAS GEMM (``in_proj``), ONE recurrence launch that also computes the A/dt
+controls from the projection, applies the C/B RMSNorm of the raw q/k rows and
+the length mask, and one cuBLAS GEMM (``out_proj``); ``bidirectional_pair``
+runs a block's two directions in one launch. With ``fused_recurrence=False``
+the controls, norms and mask run as separate kernels around ``fused_mamba``
+(the reference's unfused arrangement); ``backend="reference"`` evaluates the
+norms and controls with the reference's PyTorch formulas.
 """
 
 from __future__ import annotations
@@ -56,35 +57,64 @@ class Mamba3Inference(nn.Module):
 
         return mamba_controls(a, ddt, self.dt_bias, self.A_floor)
 
+    def _direction(self, p, b, t, reverse=False):
+        """Arguments of one fused launch from the projection ``p``: the C/B norms,
+        the controls (from the a/ddt views) and the length mask run inside it."""
+        z, v, k, q, ddt, a, trap, angles = self._split(p)
+        heads = (b, t, self.nheads, self.headdim)
+        return dict(q=q.reshape(b, t, 1, self.d_state), k=k.reshape(b, t, 1, self.d_state),
+                    v=v.reshape(heads), z=z.reshape(heads), trap=trap.transpose(1, 2),
+                    angles=angles.unsqueeze(2).expand(b, t, self.nheads, self.num_rope_angles),
+                    qb=self.C_bias[:, 0], kb=self.B_bias[:, 0], d=self.D, a_raw=a, ddt_raw=ddt,
+                    dt_bias=self.dt_bias, a_floor=self.A_floor, q_norm=self.C_norm.weight,
+                    k_norm=self.B_norm.weight, reverse=reverse)
+
     def forward(self, u, lengths=None):
         """``u`` [B, T, dim] → [B, T, dim]. With ``lengths`` ([B] int64), rows at
         or past each length come out zero (the block's length mask)."""
         b, t, _ = u.shape
         p = self.in_proj(u)
+        if self.fused_recurrence and self.backend != "reference":
+            from .mamba_fused import fused_recurrence_multi
+
+            y = fused_recurrence_multi([self._direction(p, b, t)], lengths=lengths, eps=self.C_norm.eps)[0]
+            return self._out(y, b, t)
         z, v, k, q, ddt, a, trap, angles = self._split(p)
         adt, dt = self._controls(a, ddt)
         angles = angles.unsqueeze(2).expand(b, t, self.nheads, self.num_rope_angles)
         heads = (b, t, self.nheads, self.headdim)
         q = q.reshape(b, t, 1, self.d_state)
         k = k.reshape(b, t, 1, self.d_state)
-        if self.fused_recurrence and self.backend != "reference":
-            from .mamba_fused import fused_recurrence
+        from .mamba_fused import fused_mamba
 
-            y = fused_recurrence(q, k, v.reshape(heads), adt, dt, trap.transpose(1, 2),
-                                 self.C_bias[:, 0], self.B_bias[:, 0], angles, self.D,
-                                 z.reshape(heads), q_norm=self.C_norm.weight,
-                                 k_norm=self.B_norm.weight, lengths=lengths, eps=self.C_norm.eps)
-        else:
-            from .mamba_fused import fused_mamba
+        y = fused_mamba(self.C_norm(q), self.B_norm(k), v.reshape(heads), adt, dt, trap.transpose(1, 2),
+                        self.C_bias[:, 0], self.B_bias[:, 0], angles, self.D, z.reshape(heads))
+        if lengths is not None:
+            from .masking import masked, time_mask
 
-            y = fused_mamba(self.C_norm(q), self.B_norm(k), v.reshape(heads), adt, dt,
-                            trap.transpose(1, 2), self.C_bias[:, 0], self.B_bias[:, 0], angles,
-                            self.D, z.reshape(heads))
-            if lengths is not None:
-                from .masking import masked, time_mask
+            y = masked(y.reshape(b, t, -1), time_mask(lengths, t))
+        return self._out(y, b, t)
 
-                y = masked(y.reshape(b, t, -1), time_mask(lengths, t))
+    def _out(self, y, b, t):
         y = y.reshape(b, t, self.d_inner)
         if not torch.is_autocast_enabled(y.device.type):
             y = y.to(self.out_proj.weight.dtype)
         return self.out_proj(y)
+
+
+def bidirectional_pair(fwd, bwd, u, lengths):
+    """Both directions of a block (model.py:175-179) in one recurrence launch.
+
+    The backward direction reads and writes every row's valid prefix in reverse
+    time order inside the launch. ``in_proj`` and ``out_proj`` act row by row and
+    rows past the length are zero, so this equals
+    ``reverse_valid(bwd(reverse_valid(u)))`` without the two copies. Returns the
+    two directions' outputs, both in forward time order, zero past the lengths.
+    """
+    from .mamba_fused import fused_recurrence_multi
+
+    b, t, _ = u.shape
+    pf, pb = fwd.in_proj(u), bwd.in_proj(u)
+    yf, yb = fused_recurrence_multi([fwd._direction(pf, b, t), bwd._direction(pb, b, t, reverse=True)],
+                                    lengths=lengths, eps=fwd.C_norm.eps)
+    return fwd._out(yf, b, t), bwd._out(yb, b, t)

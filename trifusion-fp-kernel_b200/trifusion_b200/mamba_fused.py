@@ -121,3 +121,92 @@ def fused_recurrence(q, k, v, adt, dt, trap, qb, kb, angles, d, z, *, q_norm=Non
             None if kw is None else kw.data_ptr(), float(eps),
             None if lengths is None else lengths.data_ptr(), ws.data_ptr(), ws.numel(), stream))
     return out
+
+
+def fused_recurrence_multi(directions, *, lengths=None, eps=1e-5):
+    """One launch for one or two recurrences over the same ``[B, T, H]`` shape —
+    the two directions of a bidirectional block — returning their outputs.
+
+    Each direction is a dict with the ``fused_mamba`` tensors (``q k v adt dt
+    trap qb kb angles d z``) and optionally:
+
+    * ``a_raw``, ``ddt_raw`` ([B,T,H] projection views), ``dt_bias`` ([H]) and
+      ``a_floor`` instead of ``adt``/``dt``: the controls of ``mamba.py:58-63``
+      computed inside the launch;
+    * ``q_norm``/``k_norm`` (the C/B RMSNorm weights);
+    * ``reverse=True``: every row's valid prefix is read and written in reverse
+      time order (the backward direction of ``model.py:175-179`` without the
+      ``reverse_valid`` copies); rows at or past ``lengths`` come out zero;
+    * ``out``: a preallocated contiguous output.
+    """
+    if not 1 <= len(directions) <= 2:
+        raise ValueError("fused_recurrence_multi: one or two directions")
+    ios = (_lib.RecurrenceIO * len(directions))()
+    keep, outs, shape = [], [], None
+    for i, d_ in enumerate(directions):
+        raw = d_.get("a_raw") is not None
+        adt = d_.get("adt")
+        dt = d_.get("dt")
+        if raw:  # adt/dt are computed in the launch: pass a one-element stand-in
+            b_, t_, h_ = d_["a_raw"].shape
+            adt = dt = torch.zeros(1, device=d_["v"].device).expand(b_, h_, t_)
+        (q, k, v, adt_, dt_, trap, qb, kb, angles, d, z), dims = _prep(
+            d_["q"], d_["k"], d_["v"], adt, dt, d_["trap"], d_["qb"], d_["kb"], d_["angles"], d_["d"],
+            d_["z"])
+        if shape is None:
+            shape = dims
+        elif dims != shape:
+            raise ValueError("fused_recurrence_multi: both directions need the same [B,T,H] and groups")
+        b, t, h, hq = dims
+        out = d_.get("out")
+        if out is None:
+            out = torch.empty_like(v, memory_format=torch.contiguous_format)
+        io = ios[i]
+        io.q, io.k, io.v, io.z, io.angles = (x.data_ptr() for x in (q, k, v, z, angles))
+        io.qb, io.kb, io.d = qb.data_ptr(), kb.data_ptr(), d.data_ptr()
+        io.trap = trap.data_ptr()
+        io.trap_dtype = _lib.TF_BF16 if trap.dtype == torch.bfloat16 else _lib.TF_F32
+        st = list(_strides(q, k, v, adt_, dt_, trap, angles, z, out))
+        if raw:
+            a_raw, ddt_raw = d_["a_raw"], d_["ddt_raw"]
+            if a_raw.dtype != torch.bfloat16 or ddt_raw.dtype != torch.bfloat16:
+                a_raw, ddt_raw = a_raw.to(torch.bfloat16), ddt_raw.to(torch.bfloat16)
+            if tuple(a_raw.shape) != (b, t, h) or tuple(ddt_raw.shape) != (b, t, h):
+                raise ValueError("fused_recurrence_multi: a_raw/ddt_raw must be [B,T,H]")
+            bias = d_["dt_bias"].detach().float().contiguous()
+            io.a_raw, io.ddt_raw, io.dt_bias = a_raw.data_ptr(), ddt_raw.data_ptr(), bias.data_ptr()
+            io.a_floor = float(d_.get("a_floor", 1e-4))
+            st += [*a_raw.stride(), *ddt_raw.stride()]
+            keep += [a_raw, ddt_raw, bias]
+        else:
+            io.adt, io.dt = adt_.data_ptr(), dt_.data_ptr()
+            st += [0] * 6
+        for j, val in enumerate(st):
+            io.strides[j] = val
+        for name, field in (("q_norm", "q_norm_w"), ("k_norm", "k_norm_w")):
+            w = d_.get(name)
+            if w is not None:
+                w = w.detach().float().contiguous()
+                if w.numel() != 128:
+                    raise ValueError("fused_recurrence_multi: norm weights must be [128]")
+                setattr(io, field, w.data_ptr())
+                keep.append(w)
+        io.out = out.data_ptr()
+        io.reverse = 1 if d_.get("reverse") else 0
+        keep += [q, k, v, adt_, dt_, trap, qb, kb, angles, d, z]
+        outs.append(out)
+    b, t, h, hq = shape
+    dev = outs[0].device
+    if lengths is not None:
+        if lengths.dtype != torch.int64 or lengths.numel() != b or lengths.device != dev:
+            raise ValueError("fused_recurrence_multi: lengths must be int64 [B] on the same device")
+        lengths = lengths.contiguous()
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        n = len(directions)
+        ws = _lib.workspace(dev, lib.tf_recurrence_workspace_size_multi(n, b, t, h))
+        _lib.check(lib.tf_mamba_recurrence_multi_fwd(
+            ios, n, b, t, h, hq, float(eps), None if lengths is None else lengths.data_ptr(),
+            ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream))
+    del keep
+    return outs

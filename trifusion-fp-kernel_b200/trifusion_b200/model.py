@@ -194,9 +194,16 @@ class TriFusionBlock(nn.Module):
 
             u = native.evidence_norm(x, self.e_value(z), self.e_gate(z), self.u_norm.weight, mask,
                                      self.u_norm.eps)
-            # The recurrence zeroes rows past each length itself (out_proj has no bias).
-            mf = self.forward_mamba(u, lengths)
-            mb = reverse_valid(self.backward_mamba(reverse_valid(u, lengths), lengths), lengths)
+            # Both directions in one launch; the recurrence zeroes rows past each length
+            # itself (out_proj has no bias) and runs the backward direction reversed.
+            fwd, bwd = self.forward_mamba, self.backward_mamba
+            if fwd.fused_recurrence and bwd.fused_recurrence:
+                from .mamba import bidirectional_pair
+
+                mf, mb = bidirectional_pair(fwd, bwd, u, lengths)
+            else:
+                mf = fwd(u, lengths)
+                mb = reverse_valid(bwd(reverse_valid(u, lengths), lengths), lengths)
             mn = native.mean_norm(mf, mb, self.mn.weight, self.mn.eps)
         else:
             evidence = self.e_value(z).float() * (2 * torch.sigmoid(self.e_gate(z).float()))

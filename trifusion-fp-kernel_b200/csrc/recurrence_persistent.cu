@@ -223,6 +223,74 @@ __device__ __forceinline__ float silu_tanh(float z) {
 
 __device__ int g_device_error = 0;  // set when a bounded wait gives up
 
+__device__ __forceinline__ float2 pair(const float* x) { return make_float2(x[0], x[1]); }
+__device__ __forceinline__ void set_pair(float* x, float2 v) {
+  x[0] = v.x;
+  x[1] = v.y;
+}
+// One producer thread's 32 elements of a q or k row (8-element vectors i = 0..3
+// at columns 32 i + 8 s4): optional RMSNorm with FP32 statistics (weights w),
+// (output rounded to BF16, the reference's tensor type), bias, and the rotation
+// of the two vectors that hold rotating pairs. Returns
+// the row's max |x| over its four threads. Paired FP32 arithmetic (exact per
+// lane) halves the instruction count. Rows past the valid length are left as
+// computed: their outputs are never stored and their decay-weighted values are
+// zero, so they contribute nothing.
+__device__ __forceinline__ float prep_qk_row(float (&x)[32], const uint4 (&raw)[4], const float* __restrict__ w,
+                                             float eps, const float* __restrict__ bias, int s4,
+                                             const float (&cn)[8], const float (&sn)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) unpack8(raw[i], &x[8 * i]);
+  if (w) {  // RMSNorm (native.py:8-39)
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int m = 0; m < 16; ++m) acc = __ffma2_rn(pair(&x[2 * m]), pair(&x[2 * m]), acc);
+    float ss = acc.x + acc.y;
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    const float rr = rsqrtf(ss * (1.f / kState) + eps);
+    const float2 r2 = make_float2(rr, rr);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 32 * i + 8 * s4));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + 32 * i + 8 * s4 + 4));
+      const float2 wp[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                            make_float2(w1.z, w1.w)};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        // The norm's output is a BF16 tensor in the reference (native.py:37-38): round it.
+        const float2 y = __fmul2_rn(__fmul2_rn(pair(&x[8 * i + 2 * m]), r2), wp[m]);
+        set_pair(&x[8 * i + 2 * m], __bfloat1622float2(__float22bfloat162_rn(y)));
+      }
+    }
+  }
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + 32 * i + 8 * s4));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + 32 * i + 8 * s4 + 4));
+    const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                          make_float2(b1.z, b1.w)};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) set_pair(&x[8 * i + 2 * m], __fadd2_rn(pair(&x[8 * i + 2 * m]), bp[m]));
+    if (i < 2) {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        // (a0 c - a1 s, a0 s + a1 c) = (a0, a0) * (c, s) + (a1, a1) * (-s, c)
+        const float a0 = x[8 * i + 2 * m], a1 = x[8 * i + 2 * m + 1];
+        const float c = cn[4 * i + m], sv = sn[4 * i + m];
+        const float2 tt = __fmul2_rn(make_float2(a1, a1), make_float2(-sv, c));
+        set_pair(&x[8 * i + 2 * m], __ffma2_rn(make_float2(a0, a0), make_float2(c, sv), tt));
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(x[8 * i + e]));
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  return mx;
+}
+
 struct Shape {
   int B, H, nck, units, ndir;
 };
@@ -480,44 +548,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           __sincosf(phase[t * 33 + (m < 4 ? 4 * s4 + m : 12 + 4 * s4 + m)], &sn[m], &cn[m]);
         float x[32];
         // q: optional C_norm, bias, rotation, row exponent.
-#pragma unroll
-        for (int i = 0; i < 4; ++i) unpack8(qraw[i], &x[8 * i]);
-        if (p.qw) {  // RMSNorm, FP32 statistics, BF16 result (native.py:8-39)
-          float ss = 0.f;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ss = fmaf(x[e], x[e], ss);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-          const float rr = rsqrtf(ss * (1.f / kState) + p.eps);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[8 * i + e] = bf16_round((x[8 * i + e] * rr) * p.qw[32 * i + 8 * s4 + e]);
-        }
-        float qmax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          {
-            const float4 b0 = __ldg(reinterpret_cast<const float4*>(qbh + 32 * i + 8 * s4));
-            const float4 b1 = __ldg(reinterpret_cast<const float4*>(qbh + 32 * i + 8 * s4 + 4));
-            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[8 * i + e] = row_ok ? x[8 * i + e] + bb[e] : 0.f;
-          }
-          if (i < 2) {
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              const float a0 = x[8 * i + 2 * m], a1 = x[8 * i + 2 * m + 1];
-              const float cc = cn[4 * i + m], ssn = sn[4 * i + m];
-              x[8 * i + 2 * m] = a0 * cc - a1 * ssn;
-              x[8 * i + 2 * m + 1] = a0 * ssn + a1 * cc;
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) qmax = fmaxf(qmax, fabsf(x[8 * i + e]));
-        }
-        qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
-        qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));
+        const float qmax = prep_qk_row(x, qraw, p.qw, p.eps, qbh, s4, cn, sn);
         const int qe = pow2_scale_exponent(qmax);
         {
           const float qs = exp2i(qe);
@@ -531,44 +562,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           }
         }
         // k: optional B_norm, bias, rotation.
-#pragma unroll
-        for (int i = 0; i < 4; ++i) unpack8(kraw[i], &x[8 * i]);
-        if (p.kw) {
-          float ss = 0.f;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ss = fmaf(x[e], x[e], ss);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-          const float rr = rsqrtf(ss * (1.f / kState) + p.eps);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[8 * i + e] = bf16_round((x[8 * i + e] * rr) * p.kw[32 * i + 8 * s4 + e]);
-        }
-        float kmax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          {
-            const float4 b0 = __ldg(reinterpret_cast<const float4*>(kbh + 32 * i + 8 * s4));
-            const float4 b1 = __ldg(reinterpret_cast<const float4*>(kbh + 32 * i + 8 * s4 + 4));
-            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[8 * i + e] = row_ok ? x[8 * i + e] + bb[e] : 0.f;
-          }
-          if (i < 2) {
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              const float a0 = x[8 * i + 2 * m], a1 = x[8 * i + 2 * m + 1];
-              const float cc = cn[4 * i + m], ssn = sn[4 * i + m];
-              x[8 * i + 2 * m] = a0 * cc - a1 * ssn;
-              x[8 * i + 2 * m + 1] = a0 * ssn + a1 * cc;
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) kmax = fmaxf(kmax, fabsf(x[8 * i + e]));
-        }
-        kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, 1));
-        kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, 2));
+        const float kmax = prep_qk_row(x, kraw, p.kw, p.eps, kbh, s4, cn, sn);
         float vf[16];
         unpack8(vraw[0], &vf[0]);
         unpack8(vraw[1], &vf[8]);

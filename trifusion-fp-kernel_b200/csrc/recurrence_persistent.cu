@@ -681,8 +681,11 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       unsigned char* uws = unit_ws(ws, u);
       ok &= mbar_wait(&mi.mma1[slot], ph);
       tc_fence_after();
+      // The row's last chunk has no successor: nothing reads its dS, flag or state.
+      // (Read from the slot header at each use rather than held in a register.)
+      auto last = [&]() { return (c + 1) * kChunk >= hd.teff; };
       // ---- export dS^T (row n, this thread's 32-column half) -----------------------
-      {
+      if (!last()) {
         float r[32];
         tmem_ld16(tmem_addr(tm, 32 * q4, kColD + 32 * chalf), *reinterpret_cast<float(*)[16]>(&r[0]));
         tmem_ld16(tmem_addr(tm, 32 * q4, kColD + 32 * chalf + 16), *reinterpret_cast<float(*)[16]>(&r[16]));
@@ -761,10 +764,10 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       }
       fence_async_smem();
       tc_fence_before();
-      __threadfence();  // the dS export has drained meanwhile; make it visible
+      if (!last()) __threadfence();  // the dS export has drained meanwhile; make it visible
       bar_sync_n(kBarEpilogue, kEpilogueThreads);
       if (et == 0) {
-        st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
+        if (!last()) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
@@ -800,10 +803,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           }
         }
       };
+      // Loads of a predecessor whose dS is known to be published.
       auto fetch = [&](int x, uint4 (&w)[4], float& f, float& gx, float& th) {
         const unsigned char* xws = unit_ws(ws, unit_index(shp, x, dir, b, h));
-        uint32_t seen = 0;
-        ok &= wait_flag(reinterpret_cast<const uint32_t*>(xws + kUnitFlag), epoch, kFlagAgg, seen);
         const __half* agg = reinterpret_cast<const __half*>(xws + kUnitAgg) + n * 64 + 32 * chalf;
 #pragma unroll
         for (int q = 0; q < 4; ++q) w[q] = ld_cg_v4(agg + 8 * q);
@@ -844,6 +846,15 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
             }
             start = y + 1;
           }
+        }
+        if (!lookback) {
+          // Short rows: lane l of every warp waits for predecessor l's dS flag.
+          for (int x = lane; x < c; x += 32) {
+            uint32_t seen = 0;
+            ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, unit_index(shp, x, dir, b, h)) + kUnitFlag),
+                            epoch, kFlagAgg, seen);
+          }
+          __syncwarp();
         }
         if (start < c) {
           uint4 wa[4];
@@ -892,7 +903,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           umma_commit(&mi.mma3[slot]);
         }
         // Outgoing state S(c+1) = R(-theta_c) (2^total_c S(c) + dS_c) for look-back.
-        if (lookback && c + 1 < shp.nck) {
+        if (lookback && !last()) {
           uint4 w[4];
           const __half* agg = reinterpret_cast<const __half*>(uws + kUnitAgg) + n * 64 + 32 * chalf;
 #pragma unroll
@@ -909,7 +920,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         }
       } else {
         if (et == 0) mbar_arrive(&mi.mma3[slot]);  // no inter-chunk MMA; keep the phase in step
-        if (lookback && shp.nck > 1) {
+        if (lookback && !last()) {
           // Chunk 0: its outgoing state is R(-theta_0) dS_0.
           float st[32];
 #pragma unroll

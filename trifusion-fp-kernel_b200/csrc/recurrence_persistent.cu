@@ -764,10 +764,8 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       }
       fence_async_smem();
       tc_fence_before();
-      if (!last()) __threadfence();  // the dS export has drained meanwhile; make it visible
       bar_sync_n(kBarEpilogue, kEpilogueThreads);
       if (et == 0) {
-        if (!last()) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
@@ -778,6 +776,10 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           umma_f16(tm + kColPV, desc_sw128(sb + kSlotPL + kk * 32u, 0, 1024),
                    desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, 1);
         umma_commit(&mi.mma2[slot]);
+        // Publish dS. Every epilogue thread's export stores precede the barrier
+        // above, and a release after a CTA barrier is cumulative over them, so
+        // one thread's gpu-scope release orders the whole export before the flag.
+        if (!last()) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
       }
       // ---- fold the predecessors' state contributions (row n, 32-column half) ---
       // One step: st = R(-theta) (g st + dS), dS from a published unit.
@@ -914,8 +916,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(st[4 * q], st[4 * q + 1], st[4 * q + 2], st[4 * q + 3]);
-          __threadfence();
-          bar_sync_n(kBarEpilogue, kEpilogueThreads);
+          bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the release below is cumulative over these stores
           if (et == 0) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
         }
       } else {
@@ -935,8 +936,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(st[4 * q], st[4 * q + 1], st[4 * q + 2], st[4 * q + 3]);
-          __threadfence();
-          bar_sync_n(kBarEpilogue, kEpilogueThreads);
+          bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the release below is cumulative over these stores
           if (et == 0) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
         }
       }

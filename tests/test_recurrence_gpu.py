@@ -167,6 +167,22 @@ def test_length_edge_cases():
     assert_recurrence_close(out, ref, "length edges")
 
 
+def test_padding_rows_zeroed_into_a_dirty_buffer():
+    """Chunks wholly past a row's length are zeroed apart from the ticketed
+    units; the caller's output buffer starts full of NaN, and most chunks of the
+    shorter rows are empty (look-back rows: T = 1000 is 16 chunks)."""
+    b, t, h = 8, 1000, 4
+    args = list(recurrence_inputs(b, t, h, kind="reftest", device=DEV))
+    lengths = torch.tensor([0, 1, 5, 64, 65, 300, 999, 1000])
+    out = torch.full((b, t, h, 64), float("nan"), dtype=torch.bfloat16, device=DEV)
+    for _ in range(2):
+        fused_recurrence(*args, lengths=lengths.to(DEV), out=out)
+    ref = O.mask_rows(oracle_out(args), lengths.numpy())
+    assert_recurrence_close(out, ref, "dirty buffer")
+    mask = torch.arange(t)[None, :] >= lengths[:, None]
+    assert (out.cpu()[mask] == 0).all()
+
+
 @pytest.mark.parametrize("batch,time,heads", [(2, 65, 4), (1, 255, 32), (1, 1501, 32)])
 def test_agrees_with_reference_bf16_arithmetic(batch, time, heads):
     """Against the reference fused kernel's own BF16 rounding points, with the

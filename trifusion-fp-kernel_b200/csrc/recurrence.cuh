@@ -38,6 +38,9 @@ struct RecurrenceParams {
   // Reverse: local step t of a row reads and writes time len-1-t (the backward
   // direction of the bidirectional pair, model.py:175-179, without the copies).
   int reverse;
+  // Set by the launcher: angle rows are 8-byte aligned with contiguous pairs
+  // (staged by cp.async with the other rows).
+  int ang_vec;
 };
 
 // One launch may run up to two directions over the same (B, T, H) shape; their

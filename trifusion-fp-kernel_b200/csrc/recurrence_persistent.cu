@@ -59,20 +59,30 @@ constexpr int kBarProducer = 1, kBarEpilogue = 2, kBarPair = 3;  // kBarPair + q
 constexpr int kLookbackChunks = 8;     // rows with more chunks publish outgoing states
 
 // ---- shared memory --------------------------------------------------------------
-// Per slot (bytes from the slot base, 1024-aligned).
+// Per slot (bytes from the slot base, 1024-aligned). The k tile and the vs hi/lo
+// tiles are read only by MMA 1; the epilogue starts after MMA 1 has completed, so
+// its P hi/lo tiles reuse the k tile and its S^T tile reuses the vs tiles.
 constexpr uint32_t kSlotQ = 0;        // q16  K-major  [2 K-blocks][64 rows][128 B]
 constexpr uint32_t kSlotK = 16384;    // k16  K-major  [2 K-blocks][64 rows][128 B]
-constexpr uint32_t kSlotV = 32768;    // v16  MN-major [64 rows][128 B]
-constexpr uint32_t kSlotVH = 40960;   // vs hi MN-major
-constexpr uint32_t kSlotVL = 49152;   // vs lo MN-major
-constexpr uint32_t kSlotPH = 57344;   // P hi K-major [64 rows][128 B]
-constexpr uint32_t kSlotPL = 65536;   // P lo
-constexpr uint32_t kSlotS = 73728;    // S^T MN-major [128 rows][128 B]
-constexpr uint32_t kSlotZ = 90112;    // z in / out staging, BF16 [64 rows][128 B]
-constexpr uint32_t kSlotBytes = 98304;
-// Producer scratch and barriers after the two slots.
-constexpr uint32_t kOffPhase = 2 * kSlotBytes;        // FP32 [64][33]
-constexpr uint32_t kOffMisc = kOffPhase + 64 * 33 * 4;
+constexpr uint32_t kSlotPH = 16384;   // P hi K-major [64 rows][128 B]   (over k16, after MMA 1)
+constexpr uint32_t kSlotPL = 24576;   // P lo                            (over k16, after MMA 1)
+constexpr uint32_t kSlotVH = 32768;   // vs hi MN-major
+constexpr uint32_t kSlotVL = 40960;   // vs lo MN-major
+constexpr uint32_t kSlotS = 32768;    // S^T MN-major [128 rows][128 B]  (over vs hi/lo, after MMA 1)
+constexpr uint32_t kSlotV = 49152;    // v16  MN-major [64 rows][128 B]
+constexpr uint32_t kSlotZ = 57344;    // z in / out staging, BF16 [64 rows][128 B]
+constexpr uint32_t kSlotBytes = 65536;
+// Staging of the next unit's raw rows, filled by cp.async while the current unit
+// is prepared. Each producer thread copies and later reads back only its own
+// 16-byte chunks ([chunk][thread] order: a warp's accesses are contiguous); the
+// angle rows ([64][32] BF16) are read across threads after a barrier.
+constexpr uint32_t kOffStage = 2 * kSlotBytes;
+constexpr uint32_t kStQ = 0, kStK = 16384, kStV = 32768, kStZ = 40960, kStA = 49152, kStageBytes = 53248;
+// Producer scratch and barriers after the staging area.
+constexpr uint32_t kOffPhase = kOffStage + kStageBytes;  // FP32 [64][33]
+constexpr uint32_t kOffTeff = kOffPhase + 64 * 33 * 4;   // int [2][kTeffTable]: valid length of every row
+constexpr int kTeffTable = 1024;                          // batches beyond this read lengths[] directly
+constexpr uint32_t kOffMisc = kOffTeff + 2 * kTeffTable * 4;
 
 struct SlotHeader {
   int unit;  // -1: no more work
@@ -99,11 +109,13 @@ struct Misc {
   int ticket;
   int next_ticket;
   int lookback_start;
+  int quota;            // non-empty units one CTA takes at most
   uint32_t epoch;
   uint32_t tmem_base;
   uint64_t ready[2], freed[2], mma1[2], mma2[2], mma3[2];
 };
 constexpr uint32_t kSmemBytes = kOffMisc + sizeof(Misc) + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory beyond the 227 KB a B200 CTA may use");
 
 constexpr uint32_t kColS = 0, kColD = 64, kColPV = 128, kColI = 192, kSlotCols = 256, kTmemCols = 512;
 
@@ -174,6 +186,31 @@ __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+// Asynchronous global -> shared copies (zero-filled beyond `src_bytes`; a
+// zero-byte copy reads nothing and writes zeros).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// 16 bytes of a row (16- or 8-byte aligned) into shared memory, or zeros.
+template <int kVec>
+__device__ __forceinline__ void stage16(uint32_t dst, const bf16* src, bool valid) {
+  if constexpr (kVec == 16) {
+    cp_async16(dst, src, valid ? 16u : 0u);
+  } else {
+    cp_async8(dst, src, valid ? 8u : 0u);
+    cp_async8(dst + 8, src + 4, valid ? 8u : 0u);
+  }
 }
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
@@ -348,6 +385,22 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
   const int nck = (p0.T + kChunk - 1) / kChunk;
   const Shape shp{p0.B, p0.H, nck, nck * kDirs * p0.B * p0.H, kDirs};
   const bool lookback = shp.nck > kLookbackChunks;
+  // Valid length of every row (per direction), read once per CTA.
+  int* teff_tab = reinterpret_cast<int*>(smem + kOffTeff);
+  auto row_length = [&](const RecurrenceParams& pr, int bb) -> int {
+    if (!pr.lengths) return pr.T;
+    const int64_t len = pr.lengths[bb];
+    return static_cast<int>(len < 0 ? 0 : (len > pr.T ? pr.T : len));
+  };
+  if (p0.B <= kTeffTable) {
+    for (int i = tid; i < kDirs * p0.B; i += kThreads) {
+      const int dd = i / p0.B;
+      teff_tab[dd * kTeffTable + (i - dd * p0.B)] = row_length(dd == 0 ? pd0 : pd1, i - dd * p0.B);
+    }
+  }
+  auto teff_of = [&](int dd, int bb, const RecurrenceParams& pr) -> int {
+    return p0.B <= kTeffTable ? teff_tab[dd * kTeffTable + bb] : row_length(pr, bb);
+  };
 
   if (warp == 0) {
     tmem_alloc(&mi.tmem_base, kTmemCols);
@@ -375,15 +428,78 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
     // =========================== producer ===========================
     const int t = tid >> 2, s4 = tid & 3;  // row, sub-slot (4 threads per row)
     int k = 0;                             // slot uses so far
-    if (tid == 0) mi.next_ticket = atomicAdd(ws_ticket, 1);
+    constexpr bool kStage = kVec >= 8;     // rows aligned for 8/16-byte cp.async
+    const uint32_t stage = base + kOffStage;
+    // Stage unit un's q/k/v/z rows (this thread's chunks) and angle rows.
+    auto stage_unit = [&](int un) {
+      if constexpr (kStage) {
+        if (un >= shp.units) return;
+        int nb, nh, nc, nd;
+        decode_unit(un, shp, nb, nh, nc, nd);
+        if (kDirs == 1) nd = 0;
+        const RecurrenceParams& pn = (kDirs == 1 || nd == 0) ? pd0 : pd1;
+        const int te = teff_of(nd, nb, pn);
+        const int nvn = max(0, min(kChunk, te - nc * kChunk));
+        if (nvn == 0) return;
+        const bool rv = kExt && pn.reverse != 0;
+        const bool valid = t < nvn;
+        const int64_t x = static_cast<int64_t>(nc) * kChunk + t;
+        const int64_t pos = valid ? (rv ? te - 1 - x : x) : 0;
+        const int hq = nh / (pn.H / pn.Hq);
+        const bf16* qrow = pn.q + nb * pn.sq[0] + pos * pn.sq[1] + hq * pn.sq[2];
+        const bf16* krow = pn.k + nb * pn.sk[0] + pos * pn.sk[1] + hq * pn.sk[2];
+        const bf16* vrow = pn.v + nb * pn.sv[0] + pos * pn.sv[1] + nh * pn.sv[2];
+        const bf16* zrow = pn.z + nb * pn.sz[0] + pos * pn.sz[1] + nh * pn.sz[2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          stage16<kVec>(stage + kStQ + i * 4096u + tid * 16u, qrow + 32 * i + 8 * s4, valid);
+          stage16<kVec>(stage + kStK + i * 4096u + tid * 16u, krow + 32 * i + 8 * s4, valid);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          stage16<kVec>(stage + kStV + i * 4096u + tid * 16u, vrow + 32 * i + 8 * s4, valid);
+          stage16<kVec>(stage + kStZ + i * 4096u + tid * 16u, zrow + 32 * i + 8 * s4, valid);
+        }
+        if (pn.ang_vec) {  // row tid/4, pairs 8*(tid%4) .. +7
+          const int ra = tid >> 2;
+          const bool av = ra < nvn;
+          const int64_t xa = static_cast<int64_t>(nc) * kChunk + ra;
+          const int64_t apos = av ? (rv ? te - 1 - xa : xa) : 0;
+          const bf16* arow = pn.ang + nb * pn.sa[0] + apos * pn.sa[1] + nh * pn.sa[2] + 8 * s4;
+          cp_async8(stage + kStA + ra * 64u + s4 * 16u, arow, av ? 8u : 0u);
+          cp_async8(stage + kStA + ra * 64u + s4 * 16u + 8u, arow + 4, av ? 8u : 0u);
+        }
+        cp_async_commit();
+      }
+    };
+    // Quota: ceil(non-empty units / CTAs). Tickets are claimed one unit ahead, so
+    // without it a CTA whose first units were cheap runs one unit more than the
+    // rest and sets the launch's end. A CTA at its quota stops claiming; the
+    // others, below it, claim what is left (CTAs x quota >= non-empty units).
+    if (warp == 0) {
+      long long nonempty = 0;
+      if (p0.B <= kTeffTable) {
+        for (int i = lane; i < kDirs * p0.B; i += 32) nonempty += (teff_tab[(i / p0.B) * kTeffTable + i % p0.B] + kChunk - 1) / kChunk;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) nonempty += __shfl_xor_sync(0xffffffffu, nonempty, o);
+        nonempty *= p0.H;
+      }
+      if (lane == 0) {
+        const long long g = gridDim.x;
+        mi.quota = p0.B <= kTeffTable ? static_cast<int>((nonempty + g - 1) / g) : 0x7fffffff;
+        mi.next_ticket = atomicAdd(ws_ticket, 1);
+      }
+    }
+    bar_sync_n(kBarProducer, kProducerThreads);
+    const int quota = mi.quota;
+    int held = 0;  // non-empty units this CTA has taken
+    stage_unit(mi.next_ticket);
     for (;;) {
-      bar_sync_n(kBarProducer, kProducerThreads);
+      if constexpr (kStage) cp_async_wait_all();
+      bar_sync_n(kBarProducer, kProducerThreads);  // staged rows and the ticket are visible
       const int u = mi.next_ticket;
       bar_sync_n(kBarProducer, kProducerThreads);  // everyone has read the ticket
-      // Request the following unit now; the atomic stays in flight while this
-      // unit is prepared and its result is stored only at the end.
-      int my_next = 0;
-      if (tid == 0 && u < shp.units) my_next = atomicAdd(ws_ticket, 1);
+      int my_next = shp.units;  // no further unit unless claimed below
       const int slot = k & 1;
       SlotHeader& hd = mi.hdr[slot];
       if (u >= shp.units) {
@@ -399,22 +515,21 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       decode_unit(u, shp, b, h, c, dir);
       if (kDirs == 1) dir = 0;
       const RecurrenceParams& p = (kDirs == 1 || dir == 0) ? pd0 : pd1;
-      int T_eff = p.T;
-      if (p.lengths) {
-        const int64_t len = p.lengths[b];
-        T_eff = static_cast<int>(len < 0 ? 0 : (len > p.T ? p.T : len));
-      }
+      const int T_eff = teff_of(dir, b, p);
       const int c0 = c * kChunk;
       const int nv = max(0, min(kChunk, T_eff - c0));
+      // Request the following unit now (below the quota); the atomic stays in
+      // flight while this unit's loads complete, and its rows are staged once
+      // the controls are done.
+      held += nv > 0;
+      if (tid == 0 && held < quota) my_next = atomicAdd(ws_ticket, 1);
       if (nv == 0) {
-        // Whole chunk past the length: zero rows, no tensor work, no slot.
-        // (Every later chunk of this row is empty too, so nobody reads its state.)
-        if (c0 + t < p.T) {
-          bf16* orow = p.out + b * p.so[0] + static_cast<int64_t>(c0 + t) * p.so[1] + h * p.so[2];
-#pragma unroll
-          for (int i = 0; i < 2; ++i) store16<kVec>(orow + 32 * i + 8 * s4, make_uint4(0, 0, 0, 0));
-        }
+        // Whole chunk past the length: no tensor work, no slot; its rows are
+        // zeroed after the loop. (Every later chunk of this row is empty too,
+        // so nobody reads its state.)
         if (tid == 0) mi.next_ticket = my_next;
+        bar_sync_n(kBarProducer, kProducerThreads);
+        stage_unit(mi.next_ticket);
         continue;
       }
       const bool row_ok = t < nv;
@@ -423,7 +538,18 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       auto src_row = [&](int64_t x) -> int64_t { return rev ? (T_eff - 1 - x) : x; };
       // ---- loads ------------------------------------------------------------------
       uint4 qraw[4], kraw[4], vraw[2], zraw[2];
-      {
+      if constexpr (kStage) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          qraw[i] = ld_shared_v4(stage + kStQ + i * 4096u + tid * 16u);
+          kraw[i] = ld_shared_v4(stage + kStK + i * 4096u + tid * 16u);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          vraw[i] = ld_shared_v4(stage + kStV + i * 4096u + tid * 16u);
+          zraw[i] = ld_shared_v4(stage + kStZ + i * 4096u + tid * 16u);
+        }
+      } else {
         const int64_t pos = row_ok ? src_row(c0 + t) : 0;
         const bf16* qrow = p.q + b * p.sq[0] + pos * p.sq[1] + (h / (p.H / p.Hq)) * p.sq[2];
         const bf16* krow = p.k + b * p.sk[0] + pos * p.sk[1] + (h / (p.H / p.Hq)) * p.sk[2];
@@ -480,7 +606,11 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         }
       }
       float araw[8];
-      {
+      if (kStage && p.ang_vec) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          araw[i] = __uint_as_float(ld_shared_u16(stage + kStA + (warp * 8 + i) * 64u + lane * 2u) << 16);
+      } else {
         const bf16* abase = p.ang + b * p.sa[0] + h * p.sa[2];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -506,7 +636,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         mi.scale[tid] = c_dn * (1.f - sigmoidf_fast(c_tn)) + gm;
         hd.cs[tid] = x;
       }
-      bar_sync_n(kBarProducer, kProducerThreads);
+      if (tid == 0) mi.next_ticket = my_next;
+      bar_sync_n(kBarProducer, kProducerThreads);  // also: every thread has read its staged rows
+      stage_unit(mi.next_ticket);
       if (tid >= 32 && tid < kChunk) hd.cs[tid] += mi.wsum[0];
       // ---- local angle phases: lane = pair r, warp = 8-step segment ------------
       float* phase = reinterpret_cast<float*>(smem + kOffPhase);
@@ -655,9 +787,21 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
                    desc_sw128(sb + kSlotVL + kk * 2048u, 8192, 1024), kIdState, 1);
         umma_commit(&mi.mma1[slot]);
         mbar_arrive(&mi.ready[slot]);
-        mi.next_ticket = my_next;
       }
       ++k;
+    }
+    // Units wholly past their row's length: zero their output rows. A static
+    // share per CTA (no waits involved), so no ticket has to reach them.
+    for (int zu = blockIdx.x; zu < shp.units; zu += gridDim.x) {
+      int zb, zh, zc, zd;
+      decode_unit(zu, shp, zb, zh, zc, zd);
+      if (kDirs == 1) zd = 0;
+      const RecurrenceParams& pz = (kDirs == 1 || zd == 0) ? pd0 : pd1;
+      const int z0 = zc * kChunk;
+      if (z0 < teff_of(zd, zb, pz) || z0 + t >= pz.T) continue;
+      bf16* orow = pz.out + zb * pz.so[0] + static_cast<int64_t>(z0 + t) * pz.so[1] + zh * pz.so[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) store16<kVec>(orow + 32 * i + 8 * s4, make_uint4(0, 0, 0, 0));
     }
   } else {
     // =========================== epilogue ===========================
@@ -1051,6 +1195,14 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
+// Angle rows can be staged with 8-byte cp.async: aligned rows of contiguous pairs.
+int angles_vectorizable(const RecurrenceParams& p) {
+  if (reinterpret_cast<uintptr_t>(p.ang) % 8 || p.sa[3] != 1) return 0;
+  for (int i = 0; i < 3; ++i)
+    if ((p.sa[i] * 2) % 8) return 0;
+  return 1;
+}
+
 int alignment_class(const RecurrenceLaunch& L) {
   int a = alignment_class_one(L.dir[0]);
   if (L.ndir > 1) a = a < alignment_class_one(L.dir[1]) ? a : alignment_class_one(L.dir[1]);
@@ -1081,10 +1233,12 @@ size_t recurrence_workspace_bytes(int B, int T, int H, int ndir) {
   return kWsHeader + units * kUnitBytes;
 }
 
-int launch_recurrence_persistent(const RecurrenceLaunch& L, void* workspace, size_t workspace_bytes,
+int launch_recurrence_persistent(const RecurrenceLaunch& launch_in, void* workspace, size_t workspace_bytes,
                                  cudaStream_t stream) {
+  if (launch_in.ndir < 1 || launch_in.ndir > 2) return 1;
+  RecurrenceLaunch L = launch_in;
+  for (int i = 0; i < L.ndir; ++i) L.dir[i].ang_vec = angles_vectorizable(L.dir[i]);
   const RecurrenceParams& p = L.dir[0];
-  if (L.ndir < 1 || L.ndir > 2) return 1;
   if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H, L.ndir)) return 1;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   const int a = alignment_class(L);

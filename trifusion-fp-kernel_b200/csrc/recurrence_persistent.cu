@@ -243,6 +243,11 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
 __device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
   return __ldcg(reinterpret_cast<const uint4*>(p));
 }
@@ -1141,12 +1146,14 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
     tmem_dealloc(tmem0, kTmemCols);
   }
   if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(ws_done, 1) == static_cast<int>(gridDim.x) - 1) {
-      *ws_ticket = 0;
-      *ws_done = 0;
-      __threadfence();
-      st_release_u32(ws_epoch, epoch + kEpochStep);
+    // One ordering point: the release half orders this CTA's ticket claims
+    // (same thread) before its count, and the acquire half lets the last CTA
+    // see every other CTA's claims before it resets the counters. What the next
+    // launch reads (counters, epoch) is ordered by the kernel boundary itself.
+    if (atom_add_acq_rel(ws_done, 1) == static_cast<int>(gridDim.x) - 1) {
+      *reinterpret_cast<volatile int*>(ws_ticket) = 0;
+      *reinterpret_cast<volatile int*>(ws_done) = 0;
+      *reinterpret_cast<volatile uint32_t*>(ws_epoch) = epoch + kEpochStep;
     }
   }
 }

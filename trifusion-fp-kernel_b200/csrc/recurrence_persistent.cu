@@ -56,6 +56,8 @@ constexpr int kThreads = 512;
 constexpr int kProducerThreads = 256;  // warps 0-7
 constexpr int kEpilogueThreads = 256;  // warps 8-15
 constexpr int kBarProducer = 1, kBarEpilogue = 2, kBarPair = 3;  // kBarPair + quarter: 3..6
+constexpr int kClaimThread = 224;      // producer thread that claims the next unit's ticket
+constexpr int kMmaThread = 192;        // producer thread that issues MMA 1
 constexpr int kLookbackChunks = 8;     // rows with more chunks publish outgoing states
 
 // ---- shared memory --------------------------------------------------------------
@@ -481,6 +483,31 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
     // without it a CTA whose first units were cheap runs one unit more than the
     // rest and sets the launch's end. A CTA at its quota stops claiming; the
     // others, below it, claim what is left (CTAs x quota >= non-empty units).
+    // MMA 1 (scores and state) of a finished slot. One thread of warp 6 issues it
+    // after the next iteration's first barriers, so the other 255 threads do not
+    // wait for the issue; warp 6 has slack there (warps 0-1 load the controls).
+    int pend = -1;
+    auto issue_mma1 = [&](int s) {
+      tc_fence_after();
+      const uint32_t sbs = base + s * kSlotBytes;
+      const uint32_t tm = tmem0 + s * kSlotCols;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t koff = (kk >> 2) * 8192u + (kk & 3) * 32u;
+        umma_f16(tm + kColS, desc_sw128(sbs + kSlotQ + koff, 0, 1024), desc_sw128(sbs + kSlotK + koff, 0, 1024),
+                 kIdScore, kk > 0);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_f16(tm + kColD, desc_sw128(sbs + kSlotK + kk * 2048u, 8192, 1024),
+                 desc_sw128(sbs + kSlotVH + kk * 2048u, 8192, 1024), kIdState, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_f16(tm + kColD, desc_sw128(sbs + kSlotK + kk * 2048u, 8192, 1024),
+                 desc_sw128(sbs + kSlotVL + kk * 2048u, 8192, 1024), kIdState, 1);
+      umma_commit(&mi.mma1[s]);
+      mbar_arrive(&mi.ready[s]);
+    };
     if (warp == 0) {
       long long nonempty = 0;
       if (p0.B <= kTeffTable) {
@@ -504,6 +531,10 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       bar_sync_n(kBarProducer, kProducerThreads);  // staged rows and the ticket are visible
       const int u = mi.next_ticket;
       bar_sync_n(kBarProducer, kProducerThreads);  // everyone has read the ticket
+      if (pend >= 0) {
+        if (tid == kMmaThread) issue_mma1(pend);
+        pend = -1;
+      }
       int my_next = shp.units;  // no further unit unless claimed below
       const int slot = k & 1;
       SlotHeader& hd = mi.hdr[slot];
@@ -527,12 +558,13 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       // flight while this unit's loads complete, and its rows are staged once
       // the controls are done.
       held += nv > 0;
-      if (tid == 0 && held < quota) my_next = atomicAdd(ws_ticket, 1);
+      // (Claimed by warp 7, which has less other single-thread work than warp 0.)
+      if (tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
       if (nv == 0) {
         // Whole chunk past the length: no tensor work, no slot; its rows are
         // zeroed after the loop. (Every later chunk of this row is empty too,
         // so nobody reads its state.)
-        if (tid == 0) mi.next_ticket = my_next;
+        if (tid == kClaimThread) mi.next_ticket = my_next;
         bar_sync_n(kBarProducer, kProducerThreads);
         stage_unit(mi.next_ticket);
         continue;
@@ -641,7 +673,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         mi.scale[tid] = c_dn * (1.f - sigmoidf_fast(c_tn)) + gm;
         hd.cs[tid] = x;
       }
-      if (tid == 0) mi.next_ticket = my_next;
+      if (tid == kClaimThread) mi.next_ticket = my_next;
       bar_sync_n(kBarProducer, kProducerThreads);  // also: every thread has read its staged rows
       stage_unit(mi.next_ticket);
       if (tid >= 32 && tid < kChunk) hd.cs[tid] += mi.wsum[0];
@@ -773,26 +805,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       fence_async_smem();
       tc_fence_before();
       bar_sync_n(kBarProducer, kProducerThreads);
-      if (tid == 0) {
-        tc_fence_after();
-        const uint32_t tm = tmem0 + slot * kSlotCols;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t koff = (kk >> 2) * 8192u + (kk & 3) * 32u;
-          umma_f16(tm + kColS, desc_sw128(sb + kSlotQ + koff, 0, 1024), desc_sw128(sb + kSlotK + koff, 0, 1024),
-                   kIdScore, kk > 0);
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tm + kColD, desc_sw128(sb + kSlotK + kk * 2048u, 8192, 1024),
-                   desc_sw128(sb + kSlotVH + kk * 2048u, 8192, 1024), kIdState, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tm + kColD, desc_sw128(sb + kSlotK + kk * 2048u, 8192, 1024),
-                   desc_sw128(sb + kSlotVL + kk * 2048u, 8192, 1024), kIdState, 1);
-        umma_commit(&mi.mma1[slot]);
-        mbar_arrive(&mi.ready[slot]);
-      }
+      pend = slot;  // MMA 1 is issued at the top of the next iteration
       ++k;
     }
     // Units wholly past their row's length: zero their output rows. A static

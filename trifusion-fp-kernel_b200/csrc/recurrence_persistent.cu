@@ -376,7 +376,7 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, 
 // kDirs: directions in the launch (1 or 2), a compile-time constant so that a
 // one-direction launch reads its parameters at fixed offsets. kExt: reversed
 // rows and in-launch controls are possible (otherwise compiled out).
-template <int kVec, int kDirs, bool kExt>
+template <int kVec, int kDirs, bool kExt, bool kLook>
 __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, const RecurrenceParams& pd1,
                                                 unsigned char* ws) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -391,7 +391,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
   const RecurrenceParams& p0 = pd0;
   const int nck = (p0.T + kChunk - 1) / kChunk;
   const Shape shp{p0.B, p0.H, nck, nck * kDirs * p0.B * p0.H, kDirs};
-  const bool lookback = shp.nck > kLookbackChunks;
+  constexpr bool lookback = kLook;  // rows longer than kLookbackChunks chunks (chosen by the launcher)
   // Valid length of every row (per direction), read once per CTA.
   int* teff_tab = reinterpret_cast<int*>(smem + kOffTeff);
   auto row_length = [&](const RecurrenceParams& pr, int bb) -> int {
@@ -967,6 +967,27 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           }
         }
       };
+      // This unit's own published dS (row n, this thread's half), rebuilt from the
+      // accumulator still in TMEM with the export's exponent and rounding, so it is
+      // bit for bit what successors read from the workspace (no L2 round trip).
+      auto own_ds = [&](uint4 (&w)[4], float& f) {
+        float r[32];
+        tmem_ld16(tmem_addr(tm, 32 * q4, kColD + 32 * chalf), *reinterpret_cast<float(*)[16]>(&r[0]));
+        tmem_ld16(tmem_addr(tm, 32 * q4, kColD + 32 * chalf + 16), *reinterpret_cast<float(*)[16]>(&r[16]));
+        tmem_wait_ld();
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(r[j]));
+        const int ae = pow2_scale_exponent(m);
+        const float as = exp2i(ae);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float* rr = &r[8 * q];
+          w[q] = make_uint4(pack_f16x2(rr[0] * as, rr[1] * as), pack_f16x2(rr[2] * as, rr[3] * as),
+                            pack_f16x2(rr[4] * as, rr[5] * as), pack_f16x2(rr[6] * as, rr[7] * as));
+        }
+        f = exp2i(-ae);
+      };
       // Loads of a predecessor whose dS is known to be published.
       auto fetch = [&](int x, uint4 (&w)[4], float& f, float& gx, float& th) {
         const unsigned char* xws = unit_ws(ws, unit_index(shp, x, dir, b, h));
@@ -1069,11 +1090,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         // Outgoing state S(c+1) = R(-theta_c) (2^total_c S(c) + dS_c) for look-back.
         if (lookback && !last()) {
           uint4 w[4];
-          const __half* agg = reinterpret_cast<const __half*>(uws + kUnitAgg) + n * 64 + 32 * chalf;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) w[q] = ld_cg_v4(agg + 8 * q);
-          fold_step(st, w, reinterpret_cast<const float*>(uws + kUnitExp)[128 * chalf + n], hd.gtot,
-                    hd.theta[(n >> 1) & 31u]);
+          float f;
+          own_ds(w, f);
+          fold_step(st, w, f, hd.gtot, hd.theta[(n >> 1) & 31u]);
           float* incl = reinterpret_cast<float*>(uws + kUnitIncl) + n * 64 + 32 * chalf;
 #pragma unroll
           for (int q = 0; q < 8; ++q)
@@ -1089,11 +1108,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
 #pragma unroll
           for (int j = 0; j < 32; ++j) st[j] = 0.f;
           uint4 w[4];
-          const __half* agg = reinterpret_cast<const __half*>(uws + kUnitAgg) + n * 64 + 32 * chalf;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) w[q] = ld_cg_v4(agg + 8 * q);
-          fold_step(st, w, reinterpret_cast<const float*>(uws + kUnitExp)[128 * chalf + n], 1.f,
-                    hd.theta[(n >> 1) & 31u]);
+          float f;
+          own_ds(w, f);
+          fold_step(st, w, f, 1.f, hd.theta[(n >> 1) & 31u]);
           float* incl = reinterpret_cast<float*>(uws + kUnitIncl) + n * 64 + 32 * chalf;
 #pragma unroll
           for (int q = 0; q < 8; ++q)
@@ -1171,18 +1188,19 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
   }
 }
 
-// One direction: a single parameter block (the launch copies less).
-template <int kVec, bool kExt>
+// One direction: a single parameter block (the launch copies less). kLook: rows
+// of more than kLookbackChunks chunks (outgoing states and look-back compiled in).
+template <int kVec, bool kExt, bool kLook>
 __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(const __grid_constant__ RecurrenceParams p,
                                                                               unsigned char* ws) {
-  recurrence_body<kVec, 1, kExt>(p, p, ws);
+  recurrence_body<kVec, 1, kExt, kLook>(p, p, ws);
 }
 // Both directions of a bidirectional pair in one launch.
-template <int kVec>
+template <int kVec, bool kLook>
 __global__ void __launch_bounds__(kThreads, 1) recurrence_pair_kernel(const __grid_constant__ RecurrenceParams p0,
                                                                         const __grid_constant__ RecurrenceParams p1,
                                                                         unsigned char* ws) {
-  recurrence_body<kVec, 2, true>(p0, p1, ws);
+  recurrence_body<kVec, 2, true, kLook>(p0, p1, ws);
 }
 
 int alignment_class_one(const RecurrenceParams& p) {
@@ -1234,12 +1252,13 @@ int launch(const RecurrenceLaunch& L, unsigned char* ws, cudaStream_t stream) {
   const RecurrenceParams& p = L.dir[0];
   const int units = ((p.T + kChunk - 1) / kChunk) * p.B * p.H * L.ndir;
   const int grid = units < sm_count() ? units : sm_count();
+  const bool look = (p.T + kChunk - 1) / kChunk > kLookbackChunks;
   if constexpr (kDirs == 2) {
-    auto kernel = recurrence_pair_kernel<kVec>;
+    auto kernel = look ? recurrence_pair_kernel<kVec, true> : recurrence_pair_kernel<kVec, false>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(L.dir[0], L.dir[1], ws);
   } else {
-    auto kernel = recurrence_persistent_kernel<kVec, kExt>;
+    auto kernel = look ? recurrence_persistent_kernel<kVec, kExt, true> : recurrence_persistent_kernel<kVec, kExt, false>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(L.dir[0], ws);
   }

@@ -1057,13 +1057,30 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
             ta = tb;
           }
         }
-        // FP16 S^T tile with one power-of-two exponent.
+        // FP16 S^T tile with one power-of-two exponent: this thread's part of the maximum.
         float m = 0.f;
 #pragma unroll
         for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(st[j]));
         m = warp_max(m);
         if (lane == 0) mi.ered[warp - 8] = m;
-        bar_sync_n(kBarEpilogue, kEpilogueThreads);
+        // Outgoing state S(c+1) = R(-theta_c) (2^total_c S(c) + dS_c) for look-back, published
+        // before the S tile is built: successors along the row wait for it.
+        if (lookback && !last()) {
+          float so[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) so[j] = st[j];
+          uint4 w[4];
+          float f;
+          own_ds(w, f);
+          fold_step(so, w, f, hd.gtot, hd.theta[(n >> 1) & 31u]);
+          float* incl = reinterpret_cast<float*>(uws + kUnitIncl) + n * 64 + 32 * chalf;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(so[4 * q], so[4 * q + 1], so[4 * q + 2], so[4 * q + 3]);
+        }
+        bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the maxima, and the outgoing-state stores
+        if (lookback && !last() && et == 0)  // cumulative over every thread's stores before the barrier
+          st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
 #pragma unroll
         for (int w8 = 0; w8 < 8; ++w8) m = fmaxf(m, mi.ered[w8]);
         const int se = pow2_scale_exponent(m);
@@ -1086,19 +1103,6 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
                      desc_sw128(sb + kSlotS + kk * 2048u, 8192, 1024), kIdInter, kk > 0);
           }
           umma_commit(&mi.mma3[slot]);
-        }
-        // Outgoing state S(c+1) = R(-theta_c) (2^total_c S(c) + dS_c) for look-back.
-        if (lookback && !last()) {
-          uint4 w[4];
-          float f;
-          own_ds(w, f);
-          fold_step(st, w, f, hd.gtot, hd.theta[(n >> 1) & 31u]);
-          float* incl = reinterpret_cast<float*>(uws + kUnitIncl) + n * 64 + 32 * chalf;
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(st[4 * q], st[4 * q + 1], st[4 * q + 2], st[4 * q + 3]);
-          bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the release below is cumulative over these stores
-          if (et == 0) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
         }
       } else {
         if (et == 0) mbar_arrive(&mi.mma3[slot]);  // no inter-chunk MMA; keep the phase in step

@@ -51,12 +51,16 @@ WORKLOADS = {
     "cfg4": dict(kind="box", clips=1024, max_batch=32, padded_seconds=120),
 }
 AUDIO_METRIC_UNIT = "audio-sec/s"
+# Default timed steps: each bounded to well under a minute of GPU time.
+DEFAULT_STEPS = {"cfg1": 20000, "cfg2": 20000, "cfg3": 200, "cfg4": 3}
 
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default per workload: cfg1/cfg2 20000 launches, cfg3 200 forwards, "
+                         "cfg4 3 sweeps of 1024 clips)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
@@ -64,7 +68,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-eager", type=int, default=0, metavar="K",
                     help="model workloads: run K untimed eager forwards and exit (for ncu launch lists)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = DEFAULT_STEPS[args.workload]
+    return args
 
 
 def peaks():

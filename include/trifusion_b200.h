@@ -287,6 +287,20 @@ int tf_interpolate_fwd(const void* low, const int64_t* left, const int64_t* righ
 int tf_front_norm_fwd(const void* x, int dtype, const float* w, const int64_t* lengths, void* y,
                       int batch, int time, int freq, int channels, float eps, int silu, void* stream);
 
+/* Stem of the first CNN stage (C_in = 1, C_out = 32, time stride 1): from the
+ * [B, T, F] FP32 spectrogram, the 3x3 convolution (stride (1, 2), padding 1;
+ * w1 [32, 1, 3, 3] FP32) and the 1x1 skip (stride (1, 2); ws [32] FP32), both as
+ * BF16 autocast convolutions (operands rounded to BF16, FP32 accumulation), and
+ * the conv branch's masked channel RMSNorm (norm_w [32]) and SiLU; writes
+ * h and skip, [B, T, (F-1)/2+1, 32] BF16 channels-last, 16-byte aligned.
+ * Replaces front.py:21,33,43 (`self.conv1(x)`, `front_norm(h, ..., silu=True)` of
+ * kernels/buffers.py:58-79, `self.skip(x)`) for the first stage (front.py:53);
+ * the convolution sums may differ from cuDNN's in summation order (one BF16
+ * rounding at most). */
+int tf_front_stem_fwd(const float* x, const float* w1, const float* ws, const float* norm_w,
+                      const int64_t* lengths, void* h, void* skip, int batch, int time, int freq, float eps,
+                      void* stream);
+
 /* Residual tail of a CNN stage: y = t < lengths[b] ? silu(h + skip) : 0, the sum
  * rounded to `dtype` before SiLU. Replaces front.py:43
  * (`clean(F.silu(h + clean(self.skip(x))))`). */

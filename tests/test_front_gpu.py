@@ -18,7 +18,7 @@ if not torch.cuda.is_available():
 
 from trifusion_b200.front import CNNStage  # noqa: E402
 from trifusion_b200.kernels import RMSNorm  # noqa: E402
-from trifusion_b200.kernels.buffers import front_norm, front_residual  # noqa: E402
+from trifusion_b200.kernels.buffers import front_norm, front_residual, front_stem  # noqa: E402
 from trifusion_b200.kernels.native import bands  # noqa: E402
 
 DEV = "cuda"
@@ -99,3 +99,28 @@ def test_cnn_stage_kernel_path_matches_reference_path():
         ref = ref_stage(x, lengths)
     assert y.shape == ref.shape
     torch.testing.assert_close(y.float(), ref.float(), atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("shape,lens", [((4, 401, 257), [401, 200, 1, 0]), ((2, 37, 33), [37, 5])])
+def test_front_stem_matches_cudnn_stage(shape, lens):
+    """The fused first-stage stem against cuDNN's BF16 convolutions followed by the
+    front-norm kernel: the skip is one exact product per channel (bit-exact); the
+    3x3 sums may round differently from cuDNN's (two BF16 ulps after norm + SiLU)."""
+    b, t, f = shape
+    torch.manual_seed(3)
+    stage = CNNStage(1, 32, 1, "l4").to(DEV)
+    with torch.no_grad():
+        stage.norm1.weight.copy_(1 + 0.02 * torch.randn(32))
+    x = seeded((b, 1, t, f), 4, scale=4.0, dtype=torch.float32)
+    lengths = torch.tensor(lens, device=DEV)
+    valid = (torch.arange(t, device=DEV)[None, :] < lengths[:, None])[:, None, :, None]
+    x = x.masked_fill(~valid, 0)
+    with torch.no_grad(), torch.autocast("cuda", dtype=BF):
+        h, s = front_stem(x, lengths, stage.conv1, stage.skip, stage.norm1)
+        x_cl = x.contiguous(memory_format=torch.channels_last)
+        h_ref = front_norm(stage.conv1(x_cl), lengths, stage.norm1, silu=True)
+        s_ref = stage.skip(x_cl)
+    assert h.shape == h_ref.shape and h.dtype == BF and s.dtype == BF
+    assert torch.equal(s.float(), s_ref.float())
+    close_bf16(h, h_ref, ulps=2, atol=ULP * 2.0 ** -6)
+    assert (h.permute(0, 2, 3, 1)[~valid[:, 0, :, 0]] == 0).all()

@@ -116,6 +116,90 @@ __global__ void __launch_bounds__(kThreads) front_norm_vec_kernel(const bf16* __
   }
 }
 
+// Stem of the first CNN stage (front.py:8-43 with C_in = 1, C_out = 32, time stride
+// 1; front.py:21,33,43): the 3x3 convolution (stride (1, 2), zero padding 1) and the 1x1 skip
+// (stride (1, 2)) of the [B, T, F] spectrogram, computed as the BF16 autocast
+// convolutions do (inputs and weights rounded to BF16, FP32 accumulation, BF16
+// result), then the conv branch's masked channel RMSNorm and SiLU in the rounding
+// and summation order of front_norm_vec_kernel<4>. One thread per output position,
+// its 32 channels in registers; both outputs channels-last [B, T, F2, 32] BF16.
+constexpr int kStemC = 32;
+__global__ void __launch_bounds__(kThreads) front_stem_kernel(const float* __restrict__ x,
+                                                              const float* __restrict__ w1,
+                                                              const float* __restrict__ ws,
+                                                              const float* __restrict__ nw,
+                                                              const int64_t* __restrict__ lengths,
+                                                              bf16* __restrict__ h, bf16* __restrict__ sk, int B,
+                                                              int Tn, int F, int F2, float eps) {
+  __shared__ float s_w1[kStemC * 9], s_ws[kStemC], s_nw[kStemC];
+  for (int i = threadIdx.x; i < kStemC * 9; i += kThreads) s_w1[i] = round_to<bf16>(w1[i]);
+  if (threadIdx.x < kStemC) {
+    s_ws[threadIdx.x] = round_to<bf16>(ws[threadIdx.x]);
+    s_nw[threadIdx.x] = nw[threadIdx.x];
+  }
+  __syncthreads();
+  const int64_t positions = static_cast<int64_t>(B) * Tn * F2;
+  for (int64_t pos = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; pos < positions;
+       pos += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int f2 = static_cast<int>(pos % F2);
+    const int64_t bt = pos / F2;
+    const int t = static_cast<int>(bt % Tn);
+    const int b = static_cast<int>(bt / Tn);
+    float xin[9];
+#pragma unroll
+    for (int dt = 0; dt < 3; ++dt) {
+      const int tt = t + dt - 1;
+#pragma unroll
+      for (int df = 0; df < 3; ++df) {
+        const int ff = 2 * f2 + df - 1;
+        xin[3 * dt + df] = (tt >= 0 && tt < Tn && ff >= 0 && ff < F)
+                               ? round_to<bf16>(x[(static_cast<int64_t>(b) * Tn + tt) * F + ff])
+                               : 0.f;
+      }
+    }
+    // Skip: one exact product per channel, rounded to BF16.
+    uint32_t so[kStemC / 2];
+#pragma unroll
+    for (int c = 0; c < kStemC; c += 2) so[c / 2] = pack_bf16x2(xin[4] * s_ws[c], xin[4] * s_ws[c + 1]);
+    bf16* srow = sk + pos * kStemC;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(srow + 8 * q) = make_uint4(so[4 * q], so[4 * q + 1], so[4 * q + 2], so[4 * q + 3]);
+    // Conv branch, then the norm (zero rows past the length) and SiLU.
+    const bool live = t < valid_len(lengths, b, Tn);
+    float v[kStemC];
+#pragma unroll
+    for (int c = 0; c < kStemC; ++c) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 9; ++k) acc = fmaf(xin[k], s_w1[c * 9 + k], acc);
+      v[c] = live ? round_to<bf16>(acc) : 0.f;
+    }
+    float g[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      g[q] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) g[q] = fmaf(v[8 * q + i], v[8 * q + i], g[q]);
+    }
+    const float ss = (g[0] + g[1]) + (g[2] + g[3]);
+    const float r = rsqrtf(ss / static_cast<float>(kStemC) + eps);
+    uint32_t ho[kStemC / 2];
+#pragma unroll
+    for (int c = 0; c < kStemC; c += 2) {
+      float a = round_to<bf16>(v[c] * r * s_nw[c]);
+      float d = round_to<bf16>(v[c + 1] * r * s_nw[c + 1]);
+      a = a * sigmoid_ieee(a);
+      d = d * sigmoid_ieee(d);
+      ho[c / 2] = pack_bf16x2(a, d);
+    }
+    bf16* hrow = h + pos * kStemC;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(hrow + 8 * q) = make_uint4(ho[4 * q], ho[4 * q + 1], ho[4 * q + 2], ho[4 * q + 3]);
+  }
+}
+
 // General form: one warp per row; C <= 32 * kMaxPerLane.
 template <typename T, int kMaxPerLane>
 __global__ void __launch_bounds__(kThreads) front_norm_kernel(const T* __restrict__ x,
@@ -277,6 +361,23 @@ int tf_front_norm_fwd(const void* x, int dtype, const float* w, const int64_t* l
   if (dtype == TF_F32)
     return tf::launch_front_norm<float>(x, w, lengths, y, batch, time, freq, channels, eps, silu, s);
   return tf::launch_front_norm<tf::bf16>(x, w, lengths, y, batch, time, freq, channels, eps, silu, s);
+}
+
+int tf_front_stem_fwd(const float* x, const float* w1, const float* ws, const float* norm_w,
+                      const int64_t* lengths, void* h, void* skip, int batch, int time, int freq, float eps,
+                      void* stream) {
+  if (batch < 0 || time < 0 || freq < 1) return TF_ERR_ARG;
+  if (batch == 0 || time == 0) return TF_OK;
+  if (!x || !w1 || !ws || !norm_w || !lengths || !h || !skip) return TF_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(h) % 16 || reinterpret_cast<uintptr_t>(skip) % 16) return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const int f2 = (freq - 1) / 2 + 1;
+  const int64_t positions = static_cast<int64_t>(batch) * time * f2;
+  tf::front_stem_kernel<<<tf::grid_for(positions, tf::kThreads), tf::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, w1, ws, norm_w, lengths, static_cast<tf::bf16*>(h), static_cast<tf::bf16*>(skip), batch, time, freq, f2,
+      eps);
+  return tf::launch_status();
 }
 
 int tf_front_residual_fwd(const void* h, const void* skip, int dtype, const int64_t* lengths, void* y,

@@ -38,13 +38,25 @@ class CNNStage(nn.Module):
         self.skip = nn.Conv2d(cin, cout, 1, stride=(stride, 2), bias=False)
         self.norm1, self.norm2 = RMSNorm(cout, backend=backend), RMSNorm(cout, backend=backend)
 
+    def _stem_fusable(self, x):
+        """The 1 -> 32 channel, time-stride-1 first stage under BF16 autocast."""
+        return (self.stride == 1 and x.shape[1] == 1 and self.conv1.weight.shape[0] == 32
+                and x.dtype == torch.float32 and torch.is_autocast_enabled("cuda")
+                and torch.get_autocast_dtype("cuda") == torch.bfloat16)
+
     def forward(self, x, lengths):
         lengths = (lengths + self.stride - 1) // self.stride
         if self.backend != "reference" and x.is_cuda:
             # Channels-last activations: each channel norm reads contiguous rows,
             # and mask + norm + SiLU (and the residual tail) are one pass each.
-            from .kernels.buffers import front_norm, front_residual
+            from .kernels.buffers import front_norm, front_residual, front_stem
 
+            if self._stem_fusable(x):
+                # First stage: both convolutions of the single input channel, the
+                # first norm and SiLU in one pass over the spectrogram.
+                h, skip = front_stem(x, lengths, self.conv1, self.skip, self.norm1)
+                h = front_norm(self.conv2(h), lengths, self.norm2)
+                return front_residual(h, skip, lengths)
             x = x.contiguous(memory_format=torch.channels_last)
             h = front_norm(self.conv1(x), lengths, self.norm1, silu=True)
             h = front_norm(self.conv2(h), lengths, self.norm2)

@@ -84,6 +84,28 @@ def front_norm(x, lengths, norm, silu=False):
     return y
 
 
+def front_stem(x, lengths, conv1, skip, norm):
+    """First CNN stage's conv3x3 (1 -> 32, stride (1, 2)) + masked channel norm + SiLU
+    and its 1x1 skip, from the [B, 1, T, F] spectrogram in one pass (reference
+    ``front.py:21,33,43``; BF16 autocast semantics). Returns (h, skip) as
+    [B, 32, T, F2] views of channels-last BF16 memory."""
+    dev = _lib.require_cuda("front_stem", x, lengths, conv1.weight)
+    b, c, t, f = x.shape
+    if c != 1 or tuple(conv1.weight.shape) != (32, 1, 3, 3) or tuple(skip.weight.shape) != (32, 1, 1, 1):
+        raise ValueError("front_stem: expected the 1 -> 32 channel first stage")
+    xs = x.float().reshape(b, t, f).contiguous()
+    f2 = (f - 1) // 2 + 1
+    w1 = conv1.weight.detach().float().reshape(32, 9).contiguous()
+    ws = skip.weight.detach().float().reshape(32).contiguous()
+    nw = norm.weight.detach().float().contiguous()
+    lengths = lengths.to(torch.int64).contiguous()
+    h = torch.empty((b, t, f2, 32), device=dev, dtype=torch.bfloat16)
+    s = torch.empty_like(h)
+    _lib.launch("tf_front_stem_fwd", dev, xs.data_ptr(), w1.data_ptr(), ws.data_ptr(), nw.data_ptr(),
+                lengths.data_ptr(), h.data_ptr(), s.data_ptr(), b, t, f, float(norm.eps))
+    return h.permute(0, 3, 1, 2), s.permute(0, 3, 1, 2)
+
+
 def front_residual(h, skip, lengths):
     """Residual tail of a front-end stage: ``silu(h + skip)`` zero past the
     lengths (reference ``front.py:43``), channels-last in and out."""

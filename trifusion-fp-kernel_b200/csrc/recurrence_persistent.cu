@@ -938,11 +938,13 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           umma_f16(tm + kColPV, desc_sw128(sb + kSlotPL + kk * 32u, 0, 1024),
                    desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, 1);
         umma_commit(&mi.mma2[slot]);
-        // Publish dS. Every epilogue thread's export stores precede the barrier
-        // above, and a release after a CTA barrier is cumulative over them, so
-        // one thread's gpu-scope release orders the whole export before the flag.
-        if (!last()) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
       }
+      // Publish dS (a thread of warp 15, in parallel with warp 8's MMA issue). Every
+      // epilogue thread's export stores precede the barrier above, and a release after
+      // a CTA barrier is cumulative over them, so one thread's gpu-scope release
+      // orders the whole export before the flag.
+      if (et == kEpilogueThreads - 32 && !last())
+        st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
       // ---- fold the predecessors' state contributions (row n, 32-column half) ---
       // One step: st = R(-theta) (g st + dS), dS from a published unit.
       auto fold_step = [&](float (&st)[32], const uint4 (&w)[4], float f, float gx, float th) {

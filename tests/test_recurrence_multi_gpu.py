@@ -136,3 +136,24 @@ def test_reversed_direction_against_oracle():
     pad = torch.arange(t)[None, :] >= lengths.cpu()[:, None]
     ref[pad] = 0
     assert_recurrence_close(reverse_rows(rev, lengths).float().cpu(), ref, "reversed direction")
+
+
+def test_reversed_direction_contiguous_inputs():
+    """Contiguous 16-byte-aligned inputs (rows staged by bulk copies): the reversed
+    direction equals the forward direction on reversed rows, bit for bit."""
+    from trifusion_b200.synthetic import recurrence_inputs
+
+    b, t = 4, 300
+    lengths = torch.tensor([300, 170, 64, 1], device=DEV)
+    names = ("q", "k", "v", "adt", "dt", "trap", "qb", "kb", "angles", "d", "z")
+    args = dict(zip(names, recurrence_inputs(b, t, H, kind="baseline", seed=11, device=DEV)))
+    prm = params(12)
+    rev = fused_recurrence_multi([dict(args, q_norm=prm["q_norm"], k_norm=prm["k_norm"], reverse=True)],
+                                 lengths=lengths)[0]
+    flipped = dict(args)
+    for name in ("q", "k", "v", "z", "angles"):
+        flipped[name] = reverse_rows(args[name], lengths).contiguous()
+    for name in ("adt", "dt", "trap"):  # [B, H, T]: reverse along the last axis
+        flipped[name] = reverse_rows(args[name].transpose(1, 2), lengths).transpose(1, 2).contiguous()
+    fwd = fused_recurrence_multi([dict(flipped, q_norm=prm["q_norm"], k_norm=prm["k_norm"])], lengths=lengths)[0]
+    assert torch.equal(rev, reverse_rows(fwd, lengths))

@@ -422,7 +422,11 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       mbar_init(&mi.mma3[s], 1);
     }
     fence_mbar_init();
+    // The first unit's ticket, claimed now so its round trip overlaps the epoch
+    // and length loads (the previous launch reset the counter before it ended).
+    const int first = atomicAdd(ws_ticket, 1);
     mi.epoch = ld_acquire_u32(ws_epoch);
+    mi.next_ticket = first;
   }
   tc_fence_before();
   __syncthreads();
@@ -519,7 +523,6 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       if (lane == 0) {
         const long long g = gridDim.x;
         mi.quota = p0.B <= kTeffTable ? static_cast<int>((nonempty + g - 1) / g) : 0x7fffffff;
-        mi.next_ticket = atomicAdd(ws_ticket, 1);
       }
     }
     bar_sync_n(kBarProducer, kProducerThreads);

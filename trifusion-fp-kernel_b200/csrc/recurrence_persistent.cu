@@ -2,10 +2,13 @@
 // chunk-parallel, warp-specialised.
 //
 // Work units. A unit is one 64-step chunk c of one (batch b, head h) row. Units
-// are numbered chunk-major, u = (c*B + b)*H + h, and handed out in increasing
-// order by an atomic ticket, so a unit only ever depends on units already held
-// by running CTAs: the kernel cannot deadlock, whether or not every CTA of the
-// grid is resident.
+// are numbered chunk-major, u = ((c*ndir + dir)*B + b)*H + h, and handed out in
+// increasing order by an atomic ticket, so a unit only ever depends on units
+// already held by running CTAs: the kernel cannot deadlock, whether or not every
+// CTA of the grid is resident. A CTA takes at most ceil(non-empty units / CTAs)
+// non-empty units (tickets are claimed one unit ahead; without the quota a CTA
+// whose first units were cheap would take one more than the rest), and chunks
+// wholly past their row's length are zeroed by a static share per CTA.
 //
 // Chunk-local frames. Each unit rotates q and k by the phase accumulated from
 // its own chunk start, so its scores and its state contribution
@@ -27,8 +30,11 @@
 // launches; the last CTA to finish advances the epoch and resets the ticket.
 //
 // Roles inside a CTA (512 threads, one CTA per SM, two pipeline slots):
-//   warps 0-7   producer: ticket, loads, controls, phases, FP16 operand tiles,
-//               then the scores / state MMAs (MMA 1);
+//   warps 0-7   producer: controls, phases, FP16 operand tiles from the rows
+//               staged in shared memory by cp.async during the previous unit;
+//               stages the next unit's rows; warp 7 claims its ticket, warp 6
+//               issues this unit's scores / state MMAs (MMA 1) after the next
+//               iteration's first barriers;
 //   warps 8-15  epilogue (two warps per TMEM lane quarter, one per 32-column
 //               half): export dS, decayed scores -> P tiles, MMA 2 (P v),
 //               fold -> S tile, MMA 3 (q S^T), gated output, release the slot.
@@ -483,10 +489,6 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         cp_async_commit();
       }
     };
-    // Quota: ceil(non-empty units / CTAs). Tickets are claimed one unit ahead, so
-    // without it a CTA whose first units were cheap runs one unit more than the
-    // rest and sets the launch's end. A CTA at its quota stops claiming; the
-    // others, below it, claim what is left (CTAs x quota >= non-empty units).
     // MMA 1 (scores and state) of a finished slot. One thread of warp 6 issues it
     // after the next iteration's first barriers, so the other 255 threads do not
     // wait for the issue; warp 6 has slack there (warps 0-1 load the controls).
@@ -512,6 +514,10 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       umma_commit(&mi.mma1[s]);
       mbar_arrive(&mi.ready[s]);
     };
+    // Quota: ceil(non-empty units / CTAs). Tickets are claimed one unit ahead, so
+    // without it a CTA whose first units were cheap runs one unit more than the
+    // rest and sets the launch's end. A CTA at its quota stops claiming; the
+    // others, below it, claim what is left (CTAs x quota >= non-empty units).
     if (warp == 0) {
       long long nonempty = 0;
       if (p0.B <= kTeffTable) {

@@ -187,6 +187,12 @@ def cpu_port_time(workload, inputs_np, lengths_np, qw, kw, budget_s=12.0):
     return n, el
 
 
+def _torch_threads():
+    import torch
+
+    return torch.get_num_threads()
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -232,7 +238,7 @@ def run_reference(args, wl):
         "data": "synthetic",
         "config": {"workload": args.workload, "B": b, "T": t, "H": h, "Hq": 1, "N": 128, "P": 64,
                    "R": 32, "step": "rms(q,k) -> fused recurrence -> length mask"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "torch_threads": _torch_threads(), "kind": "port",
                          "sample": f"{steps} full {args.workload} batches (B={b}, T={t}, H={h}), numpy FP32"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference arm: the oracle port of the reference arithmetic (mamba_fused.py:72-152, "
@@ -413,7 +419,7 @@ def run_recurrence(args, wl):
         import numpy as np
         np_in = [x.float().numpy() for x in base]
         n, el = cpu_port_time(args.workload, np_in, lengths_cpu.numpy(), qw_cpu.numpy(), kw_cpu.numpy())
-        cpu = {"value": b * t * n / el, "unit": "tokens/s", "cores": host_threads(), "kind": "port",
+        cpu = {"value": b * t * n / el, "unit": "tokens/s", "cores": host_threads(), "torch_threads": _torch_threads(), "kind": "port",
                "sample": f"{n} full {args.workload} batches through the numpy oracle (FP32), {el:.1f} s"}
 
     if world > 1:
@@ -721,7 +727,7 @@ def run_reference_model(args, wl):
         "n_gpus": args.gpus, "steps": steps, "warmup": 1, "ms_per_step": el / steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": args.workload, "student": STUDENT},
-        "cpu_baseline": {"value": value, "unit": AUDIO_METRIC_UNIT, "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": AUDIO_METRIC_UNIT, "cores": cores, "torch_threads": _torch_threads(), "kind": "port",
                          "sample": f"{steps} forwards of 2 clips (4 s, 3 s) on the host, FP32"},
         "e2e": {"value": value, "unit": AUDIO_METRIC_UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

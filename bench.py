@@ -394,9 +394,15 @@ def run_recurrence(args, wl):
         xs[8] = xs[8].expand(b, t, h, 32)  # [B,T,1,32] copied once; the heads share it
         fused_recurrence(*xs[:11], q_norm=qw, k_norm=kw, lengths=xs[11], out=out)
 
-    pipe = HostPipeline(e2e_call, host_in, (b, t, h, 64), torch.bfloat16, device=dev, writes_out=True)
+    # One pinned host block per step holding all inputs (filled once here), moved by one copy.
+    pipe = HostPipeline(e2e_call, host_in, (b, t, h, 64), torch.bfloat16, device=dev, writes_out=True,
+                        packed=True)
+    host_block, views = pipe.host_block()
+    for view, x in zip(views, host_in):
+        view.copy_(x)
+    h2d = host_block.numel()  # the bytes copied per step (inputs at 256-byte-aligned offsets)
     for i in range(4):
-        pipe.submit(host_in, host_outs[i % 2])
+        pipe.submit(host_block, host_outs[i % 2])
     pipe.synchronize()
     if world > 1:
         dist.barrier()
@@ -404,7 +410,7 @@ def run_recurrence(args, wl):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(pipe.copy_in)
     for i in range(args.e2e_steps):
-        pipe.submit(host_in, host_outs[i % 2])
+        pipe.submit(host_block, host_outs[i % 2])
     e1.record(pipe.copy_out)
     torch.cuda.synchronize(dev)
     e_ms = e0.elapsed_time(e1) / max(args.e2e_steps, 1)
@@ -449,7 +455,7 @@ def run_recurrence(args, wl):
                      "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": step_bytes},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "pipeline": "HostPipeline depth 2 (copies overlap kernels)"},
+                "d2h_bytes_per_step": d2h, "pipeline": "HostPipeline depth 2, packed (one input copy per step; copies overlap kernels)"},
         "gpu_launches": args.steps,
         "clocks": clocks,
     }

@@ -49,6 +49,42 @@ def test_recurrence_steps_equal_direct_calls():
 
 @gpu
 @needs_cuda
+def test_packed_block_equals_separate_copies():
+    """packed=True: one host block per step, one copy; same results as the direct calls."""
+    from trifusion_b200 import fused_recurrence
+    from trifusion_b200.synthetic import lengths_uniform, norm_weight, recurrence_inputs
+
+    b, t, h = 3, 130, 12
+    qw, kw = norm_weight(128, 1).cuda(), norm_weight(128, 2).cuda()
+    example = list(recurrence_inputs(b, t, h, kind="baseline", seed=0, device="cpu")) + [lengths_uniform(b, 5, t)]
+    example = [x.contiguous() for x in example]
+
+    def run(*xs, out):
+        return fused_recurrence(*xs[:11], q_norm=qw, k_norm=kw, lengths=xs[11], out=out)
+
+    pipe = HostPipeline(run, example, (b, t, h, 64), torch.bfloat16, writes_out=True, packed=True)
+    blocks, outs, refs = [], [], []
+    for s in range(4):
+        xs = [x.contiguous() for x in recurrence_inputs(b, t, h, kind="baseline", seed=s, device="cpu")]
+        xs.append(lengths_uniform(b, 5, t, seed=s))
+        block, views = pipe.host_block()
+        for v, x in zip(views, xs):
+            v.copy_(x)
+        dev = [x.cuda() for x in xs]
+        refs.append(fused_recurrence(*dev[:11], q_norm=qw, k_norm=kw, lengths=dev[11]).cpu())
+        blocks.append(block)
+        outs.append(torch.empty(b, t, h, 64, dtype=torch.bfloat16).pin_memory())
+    for block, o in zip(blocks, outs):
+        pipe.submit(block, o)
+    pipe.synchronize()
+    for o, r in zip(outs, refs):
+        assert torch.equal(o, r)
+    with pytest.raises(ValueError):
+        pipe.submit(torch.zeros(7, dtype=torch.uint8), outs[0])
+
+
+@gpu
+@needs_cuda
 def test_static_output_buffer_and_reused_host_inputs():
     static = torch.empty(1 << 20, device="cuda")
 

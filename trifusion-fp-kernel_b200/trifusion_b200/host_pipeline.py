@@ -19,6 +19,12 @@ Ordering, per buffer set j:
 The caller may rewrite a step's host inputs once ``inputs_consumed(handle)`` has
 fired, and read its host output once ``done(handle)`` has fired (or after
 ``synchronize()``).
+
+With ``packed=True`` every buffer set keeps all inputs in one device block (each
+input at a 256-byte-aligned offset), and ``host_block()`` returns a pinned host
+block of the same layout with views to fill; ``submit(block, host_out)`` then moves
+a step's inputs with a single copy instead of one per tensor (many small copies
+each pay a fixed cost on the host link).
 """
 
 from __future__ import annotations
@@ -46,7 +52,8 @@ class HostPipeline:
     returns a reused static buffer (a CUDA-graph engine) stays correct.
     """
 
-    def __init__(self, fn, example_inputs, out_shape, out_dtype, device=None, depth=2, writes_out=False):
+    def __init__(self, fn, example_inputs, out_shape, out_dtype, device=None, depth=2, writes_out=False,
+                 packed=False):
         if depth < 1:
             raise ValueError("depth must be at least 1")
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -56,11 +63,24 @@ class HostPipeline:
         self.device = device
         self.depth = depth
         self.writes_out = writes_out
+        self.packed = packed
+        self._layout = []  # (offset, nbytes, dtype, shape) per input
+        offset = 0
+        for x in example_inputs:
+            nbytes = x.numel() * x.element_size()
+            self._layout.append((offset, nbytes, x.dtype, tuple(x.shape)))
+            offset += (nbytes + 255) // 256 * 256
+        self.block_bytes = offset
         self.sets = []
         for _ in range(depth):
-            inputs = [torch.empty(x.shape, dtype=x.dtype, device=device) for x in example_inputs]
+            if packed:
+                block = torch.empty(self.block_bytes, dtype=torch.uint8, device=device)
+                inputs = self._views(block)
+            else:
+                block = None
+                inputs = [torch.empty(x.shape, dtype=x.dtype, device=device) for x in example_inputs]
             out = torch.empty(tuple(out_shape), dtype=out_dtype, device=device)
-            self.sets.append((inputs, out))
+            self.sets.append((inputs, out, block))
         self.copy_in = torch.cuda.Stream(device)
         self.compute = torch.cuda.Stream(device)
         self.copy_out = torch.cuda.Stream(device)
@@ -72,20 +92,39 @@ class HostPipeline:
             self._returned[j].record(current)
         self._n = 0
 
+    def _views(self, block):
+        return [block[o:o + n].view(dt).view(shape) for o, n, dt, shape in self._layout]
+
+    def host_block(self):
+        """A pinned host block in the packed layout and its per-input views (to fill)."""
+        if not self.packed:
+            raise ValueError("host_block() needs packed=True")
+        block = torch.empty(self.block_bytes, dtype=torch.uint8).pin_memory()
+        return block, self._views(block)
+
     def submit(self, host_inputs, host_out) -> StepHandle:
-        """Queue one step: copy ``host_inputs`` in, run, copy the result to ``host_out``."""
+        """Queue one step: copy ``host_inputs`` in (a list of tensors, or with
+        ``packed=True`` the block from ``host_block()``), run, copy the result to
+        ``host_out``."""
         j = self._n % self.depth
         self._n += 1
-        inputs, out = self.sets[j]
-        if len(host_inputs) != len(inputs):
+        inputs, out, block = self.sets[j]
+        single = isinstance(host_inputs, torch.Tensor)
+        if single and (not self.packed or host_inputs.numel() != self.block_bytes
+                       or host_inputs.dtype != torch.uint8):
+            raise ValueError("a single host tensor must be the packed block from host_block()")
+        if not single and len(host_inputs) != len(inputs):
             raise ValueError(f"expected {len(inputs)} inputs, got {len(host_inputs)}")
         arrived = torch.cuda.Event()
         consumed = torch.cuda.Event()
         finished = torch.cuda.Event()
         with torch.cuda.stream(self.copy_in):
             self.copy_in.wait_event(self._read[j])
-            for src, dst in zip(host_inputs, inputs):
-                dst.copy_(src, non_blocking=True)
+            if single:
+                block.copy_(host_inputs, non_blocking=True)
+            else:
+                for src, dst in zip(host_inputs, inputs):
+                    dst.copy_(src, non_blocking=True)
             arrived.record(self.copy_in)
             consumed.record(self.copy_in)
         with torch.cuda.stream(self.compute):

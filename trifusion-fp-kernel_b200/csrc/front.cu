@@ -124,15 +124,21 @@ __global__ void __launch_bounds__(kThreads) front_norm_vec_kernel(const bf16* __
 // and summation order of front_norm_vec_kernel<4>. One thread per output position,
 // its 32 channels in registers; both outputs channels-last [B, T, F2, 32] BF16.
 constexpr int kStemC = 32;
-__global__ void __launch_bounds__(kThreads) front_stem_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(kThreads, 2) front_stem_kernel(const float* __restrict__ x,
                                                               const float* __restrict__ w1,
                                                               const float* __restrict__ ws,
                                                               const float* __restrict__ nw,
                                                               const int64_t* __restrict__ lengths,
                                                               bf16* __restrict__ h, bf16* __restrict__ sk, int B,
                                                               int Tn, int F, int F2, float eps) {
-  __shared__ float s_w1[kStemC * 9], s_ws[kStemC], s_nw[kStemC];
-  for (int i = threadIdx.x; i < kStemC * 9; i += kThreads) s_w1[i] = round_to<bf16>(w1[i]);
+  // 3x3 weights padded to 12 per channel: three 16-byte shared loads per channel.
+  __shared__ __align__(16) float s_w1[kStemC * 12];
+  __shared__ __align__(16) float s_ws[kStemC];
+  __shared__ __align__(16) float s_nw[kStemC];
+  for (int i = threadIdx.x; i < kStemC * 12; i += kThreads) {
+    const int c = i / 12, k = i - 12 * (i / 12);
+    s_w1[i] = k < 9 ? round_to<bf16>(w1[c * 9 + k]) : 0.f;
+  }
   if (threadIdx.x < kStemC) {
     s_ws[threadIdx.x] = round_to<bf16>(ws[threadIdx.x]);
     s_nw[threadIdx.x] = nw[threadIdx.x];
@@ -160,7 +166,11 @@ __global__ void __launch_bounds__(kThreads) front_stem_kernel(const float* __res
     // Skip: one exact product per channel, rounded to BF16.
     uint32_t so[kStemC / 2];
 #pragma unroll
-    for (int c = 0; c < kStemC; c += 2) so[c / 2] = pack_bf16x2(xin[4] * s_ws[c], xin[4] * s_ws[c + 1]);
+    for (int c = 0; c < kStemC; c += 4) {
+      const float4 w4 = *reinterpret_cast<const float4*>(&s_ws[c]);
+      so[c / 2] = pack_bf16x2(xin[4] * w4.x, xin[4] * w4.y);
+      so[c / 2 + 1] = pack_bf16x2(xin[4] * w4.z, xin[4] * w4.w);
+    }
     bf16* srow = sk + pos * kStemC;
 #pragma unroll
     for (int q = 0; q < 4; ++q)
@@ -170,9 +180,13 @@ __global__ void __launch_bounds__(kThreads) front_stem_kernel(const float* __res
     float v[kStemC];
 #pragma unroll
     for (int c = 0; c < kStemC; ++c) {
+      const float4 wa = *reinterpret_cast<const float4*>(&s_w1[c * 12]);
+      const float4 wb = *reinterpret_cast<const float4*>(&s_w1[c * 12 + 4]);
+      const float4 wc = *reinterpret_cast<const float4*>(&s_w1[c * 12 + 8]);
+      const float wk[9] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w, wc.x};
       float acc = 0.f;
 #pragma unroll
-      for (int k = 0; k < 9; ++k) acc = fmaf(xin[k], s_w1[c * 9 + k], acc);
+      for (int k = 0; k < 9; ++k) acc = fmaf(xin[k], wk[k], acc);
       v[c] = live ? round_to<bf16>(acc) : 0.f;
     }
     float g[4];
@@ -186,12 +200,17 @@ __global__ void __launch_bounds__(kThreads) front_stem_kernel(const float* __res
     const float r = rsqrtf(ss / static_cast<float>(kStemC) + eps);
     uint32_t ho[kStemC / 2];
 #pragma unroll
-    for (int c = 0; c < kStemC; c += 2) {
-      float a = round_to<bf16>(v[c] * r * s_nw[c]);
-      float d = round_to<bf16>(v[c + 1] * r * s_nw[c + 1]);
-      a = a * sigmoid_ieee(a);
-      d = d * sigmoid_ieee(d);
-      ho[c / 2] = pack_bf16x2(a, d);
+    for (int c = 0; c < kStemC; c += 4) {
+      const float4 n4 = *reinterpret_cast<const float4*>(&s_nw[c]);
+      const float nw4[4] = {n4.x, n4.y, n4.z, n4.w};
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        float a = round_to<bf16>(v[c + e] * r * nw4[e]);
+        float d = round_to<bf16>(v[c + e + 1] * r * nw4[e + 1]);
+        a = a * sigmoid_ieee(a);
+        d = d * sigmoid_ieee(d);
+        ho[(c + e) / 2] = pack_bf16x2(a, d);
+      }
     }
     bf16* hrow = h + pos * kStemC;
 #pragma unroll

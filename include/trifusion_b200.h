@@ -213,6 +213,13 @@ int tf_mamba_controls_fwd(const void* a, const void* ddt, int dtype, const int64
                           const float* dt_bias, float a_floor, float* adt, float* dt, int batch,
                           int seqlen, int heads, void* stream);
 
+/* A8 fused into the block's residual tail: y[r, :] = mask[r] ? a[r, :] + b[r, :] : 0
+ * over rows of `width` (a multiple of 4), a and y FP32, b FP32 or BF16 (added
+ * exactly in FP32). Replaces model.py:199 `mask(r + down(f))` (the FP32 add and
+ * the `_mask` pass of kernels/buffers.py:6-10) with one pass. */
+int tf_masked_add_fwd(const float* a, const void* b, int b_dtype, const uint8_t* mask, float* y, int64_t rows,
+                      int width, void* stream);
+
 /* A8 length mask: row r of y = row r of x where mask[r] != 0, else zero bytes.
  * Replaces kernels/buffers.py:6-10 `mask_buffer` (`_mask`, primitives.py:65-70). */
 int tf_mask_rows_fwd(const void* x, const uint8_t* mask, void* y, int64_t rows,

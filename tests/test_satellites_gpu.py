@@ -22,7 +22,7 @@ if not torch.cuda.is_available():
 
 from trifusion_b200.kernels import gated_concat, reverse_valid, swiglu  # noqa: E402
 from trifusion_b200.kernels import native  # noqa: E402
-from trifusion_b200.kernels.buffers import Pool4, mamba_controls, mask_buffer  # noqa: E402
+from trifusion_b200.kernels.buffers import Pool4, mamba_controls, mask_buffer, masked_add  # noqa: E402
 
 DEV = "cuda"
 BF = torch.bfloat16
@@ -305,3 +305,16 @@ def test_interpolate_bit_exact_with_formula():
     y = interpolate(low, grids)
     ref = Grids.make(lengths, 101, 64, native_kernels=False).interpolate(low)
     assert torch.equal(y, ref)
+
+
+@pytest.mark.parametrize("b_dtype", [torch.bfloat16, torch.float32])
+def test_masked_add_is_exact(b_dtype):
+    """mask(a + b) in one pass equals PyTorch's FP32 add (b promoted) then the row mask, bit for bit."""
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(4, 37, 384, generator=g).to(DEV)
+    bb = torch.randn(4, 37, 384, generator=g).to(b_dtype).to(DEV)
+    lengths = torch.tensor([37, 20, 1, 0], device=DEV)
+    mask = torch.arange(37, device=DEV)[None, :] < lengths[:, None]
+    y = masked_add(a, bb, mask)
+    ref = torch.where(mask[..., None], a + bb, torch.zeros((), device=DEV))
+    assert y.dtype == torch.float32 and torch.equal(y, ref)

@@ -209,6 +209,27 @@ __global__ void __launch_bounds__(kThreads) mask_rows_kernel(const V* __restrict
   }
 }
 
+// Masked residual add (model.py:199 `mask(r + down(f))`): y[r, :] = a[r, :] + b[r, :]
+// in FP32 (b promoted exactly) where mask[r] != 0, else zero; a and y FP32. Four
+// elements per thread (width % 4 == 0, 16/8-byte aligned rows).
+template <typename TB>
+__global__ void __launch_bounds__(kThreads) masked_add_kernel(const float* __restrict__ a, const TB* __restrict__ b,
+                                                              const uint8_t* __restrict__ mask, float* __restrict__ y,
+                                                              int64_t rows, int width) {
+  const int quads = width / 4;
+  const int64_t total = rows * quads;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t r = i / quads;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (mask[r]) {
+      const float4 x = load4(a + 4 * i), z = load4(b + 4 * i);
+      v = make_float4(x.x + z.x, x.y + z.y, x.z + z.z, x.w + z.w);
+    }
+    store4(y + 4 * i, v);
+  }
+}
+
 __device__ __forceinline__ int64_t clamp_len(int64_t len, int T) {
   return len < 0 ? 0 : (len > T ? T : len);
 }
@@ -581,6 +602,25 @@ int tf_mask_rows_fwd(const void* x, const uint8_t* mask, void* y, int64_t rows,
   const int st = tf::check_device();
   if (st != TF_OK) return st;
   return tf::launch_mask_rows(x, mask, y, rows, row_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int tf_masked_add_fwd(const float* a, const void* b, int b_dtype, const uint8_t* mask, float* y, int64_t rows,
+                      int width, void* stream) {
+  if (rows < 0 || width < 0 || !valid_dtype(b_dtype)) return TF_ERR_ARG;
+  if (rows == 0 || width == 0) return TF_OK;
+  if (!a || !b || !mask || !y) return TF_ERR_ARG;
+  if (width % 4 || !tf::aligned(a, 16) || !tf::aligned(y, 16) || !tf::aligned(b, b_dtype == TF_F32 ? 16 : 8))
+    return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = tf::grid_for(rows * (width / 4), tf::kThreads);
+  if (b_dtype == TF_F32)
+    tf::masked_add_kernel<float><<<grid, tf::kThreads, 0, s>>>(a, static_cast<const float*>(b), mask, y, rows, width);
+  else
+    tf::masked_add_kernel<tf::bf16><<<grid, tf::kThreads, 0, s>>>(a, static_cast<const tf::bf16*>(b), mask, y, rows,
+                                                                  width);
+  return tf::launch_status();
 }
 
 int tf_reverse_valid_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,

@@ -110,7 +110,7 @@ class Frontend(nn.Module):
         with torch.autocast(device_type=audio.device.type, enabled=False):
             keep = time_mask(sample_lengths, n)[:, None, :]
             keep = keep & (torch.arange(c, device=audio.device)[None, :, None] < channels[:, None, None])
-            wave = torch.where(keep, audio.float(), torch.zeros((), device=audio.device))
+            wave = torch.where(keep, audio.float(), 0.0)
             spec = torch.stft(wave.reshape(b * c, n), n_fft=512, hop_length=160, win_length=400,
                               window=self.window.float(), center=True, pad_mode="constant",
                               return_complex=True)

@@ -65,7 +65,7 @@ def reverse_valid(x, lengths, backend="l4"):
         src = (lengths.unsqueeze(1) - 1 - steps).clamp(min=0)
         rows = torch.take_along_dim(x, src.unsqueeze(-1), dim=1)
         valid = (steps < lengths.unsqueeze(1)).unsqueeze(-1)
-        return torch.where(valid, rows, torch.zeros((), dtype=x.dtype, device=x.device))
+        return torch.where(valid, rows, 0.0)
     x = x.contiguous()
     dev = _lib.require_cuda("reverse_valid", x, lengths)
     b, t = x.shape[:2]

@@ -9,6 +9,45 @@ import torch
 from .. import _lib
 
 
+_BF16_PARAMS = {}
+
+
+def _param_bf16(param, shape):
+    """A contiguous BF16 copy of ``param`` reshaped to ``shape``, cached until the
+    parameter changes (its version counter or storage), so steady-state calls launch
+    no conversion kernel."""
+    key = (id(param), shape)
+    stamp = (param._version, param.data_ptr(), param.device)
+    hit = _BF16_PARAMS.get(key)
+    if hit is None or hit[0] != stamp:
+        hit = (stamp, param.detach().to(torch.bfloat16).reshape(shape).contiguous())
+        _BF16_PARAMS[key] = hit
+    return hit[1]
+
+
+def _mask_bytes(mask):
+    """The mask as one byte per row, without a conversion pass for bool masks."""
+    m = mask.contiguous()
+    return m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
+
+
+def masked_add(a, b, mask):
+    """``mask(a + b)``: FP32 ``a`` plus ``b`` (FP32 or BF16, added exactly in FP32) on
+    rows where ``mask`` ([B, T] bool) is set, zero rows elsewhere; FP32 result
+    (reference ``model.py:199``, the residual add and the ``_mask`` of ``buffers.py:6-10``)."""
+    a, b = a.contiguous(), b.contiguous()
+    dev = _lib.require_cuda("masked_add", a, b, mask)
+    if a.dtype != torch.float32 or a.shape != b.shape or a.shape[-1] % 4:
+        raise ValueError("masked_add: a must be FP32, b the same shape, width a multiple of 4")
+    rows = mask.numel()
+    if rows == 0 or a.numel() % rows:
+        raise ValueError("masked_add: mask must have one entry per row")
+    y = torch.empty_like(a)
+    _lib.launch("tf_masked_add_fwd", dev, a.data_ptr(), b.data_ptr(), _lib.dtype_code(b, "masked_add"),
+                _mask_bytes(mask).data_ptr(), y.data_ptr(), rows, a.numel() // rows)
+    return y
+
+
 def mask_buffer(x, mask):
     """Rows of ``x`` where ``mask`` ([B, T] bool) is False become zero; the
     others are copied bit for bit (reference ``buffers.py:6-10``)."""
@@ -19,7 +58,7 @@ def mask_buffer(x, mask):
         if x.numel() == 0:
             return torch.empty_like(x)
         raise ValueError("mask_buffer: mask must have one entry per row of x")
-    m = mask.contiguous().to(torch.uint8)
+    m = _mask_bytes(mask)
     y = torch.empty_like(x)
     row_bytes = x.numel() // rows * x.element_size()
     _lib.launch("tf_mask_rows_fwd", dev, x.data_ptr(), m.data_ptr(), y.data_ptr(), rows, row_bytes)
@@ -131,8 +170,8 @@ def depthwise_masked(x, layer, lengths):
     k = layer.weight.shape[-1]
     if layer.groups != c or layer.weight.shape[0] != c or 2 * layer.padding[0] + 1 != k:
         raise ValueError("depthwise_masked: expected a depthwise Conv1d with 'same' padding")
-    w = layer.weight.detach().to(torch.bfloat16).reshape(c, k).contiguous()
-    bias = None if layer.bias is None else layer.bias.detach().to(torch.bfloat16).contiguous()
+    w = _param_bf16(layer.weight, (c, k))
+    bias = None if layer.bias is None else _param_bf16(layer.bias, (c,))
     lengths = lengths.to(torch.int64).contiguous()
     y = torch.empty((b, t, c), device=dev, dtype=torch.bfloat16)
     _lib.launch("tf_depthwise_masked_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "depthwise_masked"),

@@ -50,7 +50,8 @@ def evidence_norm(x, value, gate, weight, mask, eps=1e-5):
     if value.shape != x.shape or gate.shape != x.shape or mask.numel() != rows:
         raise ValueError("evidence_norm: value/gate must match x and mask must have one entry per row")
     w = _weight(weight, d, "evidence_norm")
-    m = mask.contiguous().to(torch.uint8)
+    m = mask.contiguous()
+    m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
     y = torch.empty(x.shape, device=dev, dtype=torch.float32)
     _lib.launch("tf_evidence_norm_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "evidence_norm"),
                 value.data_ptr(), gate.data_ptr(), _lib.dtype_code(value, "evidence_norm"),

@@ -123,6 +123,17 @@ def fused_recurrence(q, k, v, adt, dt, trap, qb, kb, angles, d, z, *, q_norm=Non
     return out
 
 
+_STAND_INS = {}
+
+
+def _stand_in(device):
+    """A cached one-element FP32 tensor per device (never read or written by the launch)."""
+    t = _STAND_INS.get(device)
+    if t is None:
+        t = _STAND_INS[device] = torch.zeros(1, device=device)
+    return t
+
+
 def fused_recurrence_multi(directions, *, lengths=None, eps=1e-5):
     """One launch for one or two recurrences over the same ``[B, T, H]`` shape —
     the two directions of a bidirectional block — returning their outputs.
@@ -149,7 +160,7 @@ def fused_recurrence_multi(directions, *, lengths=None, eps=1e-5):
         dt = d_.get("dt")
         if raw:  # adt/dt are computed in the launch: pass a one-element stand-in
             b_, t_, h_ = d_["a_raw"].shape
-            adt = dt = torch.zeros(1, device=d_["v"].device).expand(b_, h_, t_)
+            adt = dt = _stand_in(d_["v"].device).expand(b_, h_, t_)
         (q, k, v, adt_, dt_, trap, qb, kb, angles, d, z), dims = _prep(
             d_["q"], d_["k"], d_["v"], adt, dt, d_["trap"], d_["qb"], d_["kb"], d_["angles"], d_["d"],
             d_["z"])

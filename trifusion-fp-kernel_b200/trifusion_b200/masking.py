@@ -17,7 +17,7 @@ def time_mask(lengths, time):
 
 def masked(x, mask):
     """Zero the rows of ``x`` ([B, T, ...]) where ``mask`` is False (``masking.py:10-11``)."""
-    return torch.where(mask.unsqueeze(-1), x, torch.zeros((), dtype=x.dtype, device=x.device))
+    return torch.where(mask.unsqueeze(-1), x, 0.0)  # a Python scalar: no device fill per call
 
 
 def rotary_table(steps, head_dim, device):

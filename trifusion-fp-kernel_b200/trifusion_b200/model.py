@@ -176,14 +176,16 @@ class TriFusionBlock(nn.Module):
             for layer in (self.merge, self.down):
                 layer.weight.mul_(1 / math.sqrt(2 * c.depth))
 
-    def forward(self, x, grids):
+    def forward(self, x, grids, input_masked=False):
+        """``input_masked``: the rows of ``x`` past each length are already zero (the
+        previous block's output on the optimized path), so the input mask is skipped."""
         mask, lengths = grids.mask, grids.lengths
         opt = self.backend != "reference"
 
         def keep_zero(value):  # the optimized path's operators already keep padded rows at zero
             return value if opt else masked(value, mask)
 
-        if opt:
+        if opt and not input_masked:
             x = _mask_rows(x, mask, True)
         h = keep_zero(self.pre(x))
         cn = keep_zero(self.cn(self.local(h, mask, lengths)))
@@ -217,7 +219,13 @@ class TriFusionBlock(nn.Module):
         conv = _depthwise(v, self.merge_dw, mask, lengths, opt)
         r = keep_zero(x + self.dropout(self.merge(v + conv)))
         f = swiglu(self.gate_up(self.ff_norm(r)), self.backend)
-        out = _mask_rows(r + self.dropout(self.down(f)), mask, opt)
+        y = self.dropout(self.down(f))
+        if opt and r.is_cuda and r.dtype == torch.float32 and r.shape[-1] % 4 == 0:
+            from .kernels.buffers import masked_add
+
+            out = masked_add(r, y, mask)  # one pass: the residual add and the length mask
+        else:
+            out = _mask_rows(r + y, mask, opt)
         return out, mf, mb
 
 
@@ -266,8 +274,9 @@ class TriFusion(nn.Module):
                            self.config.buffer_fusion and optimized,
                            self.config.native_kernels and optimized)
         mf = mb = None
-        for block in self.blocks:
-            x, mf, mb = block(x, grids)
+        for i, block in enumerate(self.blocks):
+            # Each optimized block's output is zero past the lengths: the next one needn't mask it.
+            x, mf, mb = block(x, grids, input_masked=optimized and i > 0)
         return x, fine, grids, fine_lengths, mf, mb
 
     def forward(self, audio, lengths, channels):

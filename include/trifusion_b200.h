@@ -256,6 +256,20 @@ int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* 
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
                       int64_t row_bytes, void* stream);
 
+/* RMSNorm as tf_rms_fwd with the output type chosen (`y_dtype` TF_F32 or TF_BF16):
+ * a BF16 result is the FP32 result rounded once, i.e. what autocast would feed the
+ * next projection. Replaces `RMSNorm` (kernels/__init__.py:23-27) followed by the
+ * autocast cast of its output before model.py:198 `gate_up`. */
+int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtype, int64_t rows, int width,
+                   float eps, void* stream);
+
+/* Evidence norm as tf_evidence_norm_fwd with the output type chosen (TF_F32 or
+ * TF_BF16, the FP32 result rounded once). Replaces native.py:73-74 followed by the
+ * autocast cast before the Mamba in_proj (mamba.py:42). */
+int tf_evidence_norm_out_fwd(const void* x, int x_dtype, const void* value, const void* gate, int vg_dtype,
+                             const float* w, const uint8_t* mask, void* y, int y_dtype, int64_t rows, int width,
+                             float eps, void* stream);
+
 /* Depthwise Conv1d over time on [B, T, C] rows with zero padding outside [0, T):
  * y[b,t,c] = t < lengths[b] ? sum_k x[b, t+k-K/2, c] w[c,k] + bias[c] : 0, inputs
  * rounded to BF16, BF16 out; w [C, K] and bias [C] (may be NULL) BF16; K in
@@ -264,6 +278,12 @@ int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch,
 int tf_depthwise_masked_fwd(const void* x, int dtype, const void* w, const void* bias,
                             const int64_t* lengths, void* y, int batch, int seqlen, int channels,
                             int taps, void* stream);
+
+/* As tf_depthwise_masked_fwd, plus the input itself: y = bf16(x + bf16(conv(x))),
+ * the sum in FP32. Replaces model.py:188-189 (`v + depthwise_masked(v)` rounded by
+ * autocast before the merge projection). */
+int tf_depthwise_residual_fwd(const void* x, int dtype, const void* w, const void* bias, const int64_t* lengths,
+                              void* y, int batch, int seqlen, int channels, int taps, void* stream);
 
 /* Rotary q/k of the attention branch: x [B, T, 3, H, D] BF16 (the qkv projection)
  * -> y [3, B, H, T, D] FP32 holding BF16-rounded values; q and k pairs rotated by

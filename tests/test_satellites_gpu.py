@@ -318,3 +318,25 @@ def test_masked_add_is_exact(b_dtype):
     y = masked_add(a, bb, mask)
     ref = torch.where(mask[..., None], a + bb, torch.zeros((), device=DEV))
     assert y.dtype == torch.float32 and torch.equal(y, ref)
+
+
+def test_bf16_outputs_equal_cast_fp32_outputs():
+    """The BF16-output forms (norms feeding a projection, depthwise plus its input) equal
+    the FP32 forms followed by the autocast cast, bit for bit."""
+    from trifusion_b200.kernels.buffers import depthwise_masked
+
+    g = torch.Generator().manual_seed(9)
+    x = (torch.randn(3, 41, 384, generator=g) * 2).to(DEV)
+    w = (1 + 0.05 * torch.randn(384, generator=g)).to(DEV)
+    assert torch.equal(native.rms(x, w, 1e-5, out_dtype=torch.bfloat16), native.rms(x, w, 1e-5).to(torch.bfloat16))
+    value = torch.randn(3, 41, 384, generator=g).to(torch.bfloat16).to(DEV)
+    gate = torch.randn(3, 41, 384, generator=g).to(torch.bfloat16).to(DEV)
+    lengths = torch.tensor([41, 17, 0], device=DEV)
+    mask = torch.arange(41, device=DEV)[None, :] < lengths[:, None]
+    e32 = native.evidence_norm(x, value, gate, w, mask, 1e-5)
+    e16 = native.evidence_norm(x, value, gate, w, mask, 1e-5, out_dtype=torch.bfloat16)
+    assert e16.dtype == torch.bfloat16 and torch.equal(e16, e32.to(torch.bfloat16))
+    conv = torch.nn.Conv1d(384, 384, 3, padding=1, groups=384).to(DEV)
+    xm = torch.where(mask[..., None], x, 0.0)
+    fused = depthwise_masked(xm, conv, lengths, residual=True)
+    assert torch.equal(fused, (xm + depthwise_masked(xm, conv, lengths).float()).to(torch.bfloat16))

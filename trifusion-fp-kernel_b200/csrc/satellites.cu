@@ -394,7 +394,9 @@ __global__ void __launch_bounds__(kThreads) masked_mean_kernel(const T* __restri
 // zero padding outside [0, T). Inputs are rounded to BF16 first (the autocast
 // type the reference converts to), each product and sum is rounded separately
 // as in the reference kernel, and the result is BF16. Four channels per thread.
-template <typename TI, int K>
+// kResidual: y = bf16(x + bf16(conv)) instead (model.py:188-189 `v + conv` before the
+// merge projection, whose autocast input is that sum rounded to BF16).
+template <typename TI, int K, bool kResidual = false>
 __global__ void __launch_bounds__(kThreads) depthwise_kernel(const TI* __restrict__ x,
                                                              const bf16* __restrict__ w,
                                                              const bf16* __restrict__ bias,
@@ -425,21 +427,28 @@ __global__ void __launch_bounds__(kThreads) depthwise_kernel(const TI* __restric
         for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], __bfloat162float(bias[c + j]));
       }
     }
+    if (kResidual) {
+      const float4 xc = load4(x + bt * C + c);
+      acc[0] = xc.x + bf16_round(acc[0]);
+      acc[1] = xc.y + bf16_round(acc[1]);
+      acc[2] = xc.z + bf16_round(acc[2]);
+      acc[3] = xc.w + bf16_round(acc[3]);
+    }
     store4(y + bt * C + c, make_float4(acc[0], acc[1], acc[2], acc[3]));
   }
 }
 
 }  // namespace
 
-template <typename TI>
+template <typename TI, bool kResidual = false>
 int launch_depthwise(const void* x, const bf16* w, const bf16* bias, const int64_t* lengths, bf16* y,
                      int B, int T, int C, int K, cudaStream_t s) {
   const int grid = grid_for(static_cast<int64_t>(B) * T * (C / 4), kThreads);
   auto X = static_cast<const TI*>(x);
   switch (K) {
-    case 3: depthwise_kernel<TI, 3><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
-    case 5: depthwise_kernel<TI, 5><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
-    case 7: depthwise_kernel<TI, 7><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 3: depthwise_kernel<TI, 3, kResidual><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 5: depthwise_kernel<TI, 5, kResidual><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 7: depthwise_kernel<TI, 7, kResidual><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
     default: return TF_ERR_ARG;
   }
   return launch_status();
@@ -538,6 +547,47 @@ int tf_rms_fwd(const void* x, int dtype, const float* w, void* y, int64_t rows, 
   if (dtype == TF_F32)
     return tf::launch_row_norm<0, float, float, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
   return tf::launch_row_norm<0, tf::bf16, tf::bf16, tf::bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+}
+
+int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtype, int64_t rows, int width,
+                   float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(dtype) || !valid_dtype(y_dtype)) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !w || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  if (dtype == TF_F32 && y_dtype == TF_F32)
+    return tf::launch_row_norm<0, float, float, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+  if (dtype == TF_F32)
+    return tf::launch_row_norm<0, float, float, bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+  if (y_dtype == TF_F32)
+    return tf::launch_row_norm<0, bf16, bf16, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+  return tf::launch_row_norm<0, bf16, bf16, bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+}
+
+int tf_evidence_norm_out_fwd(const void* x, int x_dtype, const void* value, const void* gate, int vg_dtype,
+                             const float* w, const uint8_t* mask, void* y, int y_dtype, int64_t rows, int width,
+                             float eps, void* stream) {
+  if (y_dtype == TF_F32)
+    return tf_evidence_norm_fwd(x, x_dtype, value, gate, vg_dtype, w, mask, static_cast<float*>(y), rows, width, eps,
+                                stream);
+  if (rows < 0 || width <= 0 || !valid_dtype(x_dtype) || !valid_dtype(vg_dtype) || y_dtype != TF_BF16)
+    return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !value || !gate || !w || !mask || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  if (x_dtype == TF_F32 && vg_dtype == TF_F32)
+    return tf::launch_row_norm<1, float, float, bf16>(x, value, gate, w, mask, y, rows, width, eps, s);
+  if (x_dtype == TF_F32)
+    return tf::launch_row_norm<1, float, bf16, bf16>(x, value, gate, w, mask, y, rows, width, eps, s);
+  if (vg_dtype == TF_F32)
+    return tf::launch_row_norm<1, bf16, float, bf16>(x, value, gate, w, mask, y, rows, width, eps, s);
+  return tf::launch_row_norm<1, bf16, bf16, bf16>(x, value, gate, w, mask, y, rows, width, eps, s);
 }
 
 int tf_evidence_norm_fwd(const void* x, int x_dtype, const void* value, const void* gate,
@@ -715,6 +765,26 @@ int tf_depthwise_masked_fwd(const void* x, int dtype, const void* w, const void*
   auto Y = static_cast<tf::bf16*>(y);
   if (dtype == TF_F32) return tf::launch_depthwise<float>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
   return tf::launch_depthwise<tf::bf16>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
+}
+
+int tf_depthwise_residual_fwd(const void* x, int dtype, const void* w, const void* bias, const int64_t* lengths,
+                              void* y, int batch, int seqlen, int channels, int taps, void* stream) {
+  if (batch < 0 || seqlen < 0 || channels < 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (taps != 3 && taps != 5 && taps != 7) return TF_ERR_ARG;
+  if (channels % 4) return TF_ERR_LAYOUT;
+  if (batch == 0 || seqlen == 0 || channels == 0) return TF_OK;
+  if (!x || !w || !lengths || !y) return TF_ERR_ARG;
+  const uintptr_t align = dtype == TF_F32 ? 16 : 8;
+  if (reinterpret_cast<uintptr_t>(x) % align || reinterpret_cast<uintptr_t>(y) % 8) return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto W = static_cast<const tf::bf16*>(w);
+  auto Bs = static_cast<const tf::bf16*>(bias);
+  auto Y = static_cast<tf::bf16*>(y);
+  if (dtype == TF_F32)
+    return tf::launch_depthwise<float, true>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
+  return tf::launch_depthwise<tf::bf16, true>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
 }
 
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,

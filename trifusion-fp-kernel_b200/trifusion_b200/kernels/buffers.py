@@ -160,10 +160,11 @@ def front_residual(h, skip, lengths):
     return y
 
 
-def depthwise_masked(x, layer, lengths):
+def depthwise_masked(x, layer, lengths, residual=False):
     """Depthwise Conv1d (``layer``: groups = channels, odd kernel, 'same'
     padding) over the time axis of [B, T, C] rows, with bias, zero past the
-    lengths; BF16 result (reference ``buffers.py:13-32``)."""
+    lengths; BF16 result (reference ``buffers.py:13-32``). ``residual``: the
+    input is added (``bf16(x + conv)``, model.py:188-189)."""
     x = x.contiguous()
     dev = _lib.require_cuda("depthwise_masked", x, lengths, layer.weight)
     b, t, c = x.shape
@@ -174,7 +175,8 @@ def depthwise_masked(x, layer, lengths):
     bias = None if layer.bias is None else _param_bf16(layer.bias, (c,))
     lengths = lengths.to(torch.int64).contiguous()
     y = torch.empty((b, t, c), device=dev, dtype=torch.bfloat16)
-    _lib.launch("tf_depthwise_masked_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "depthwise_masked"),
+    _lib.launch("tf_depthwise_residual_fwd" if residual else "tf_depthwise_masked_fwd", dev, x.data_ptr(),
+                _lib.dtype_code(x, "depthwise_masked"),
                 w.data_ptr(), None if bias is None else bias.data_ptr(), lengths.data_ptr(), y.data_ptr(),
                 b, t, c, k)
     return y

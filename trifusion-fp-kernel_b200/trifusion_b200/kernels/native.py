@@ -25,23 +25,30 @@ def _weight(weight, d, op):
     return w
 
 
-def rms(x, weight, eps=1e-5):
+def rms(x, weight, eps=1e-5, out_dtype=None):
     """``x * rsqrt(mean(x^2) + eps) * weight``; output dtype = ``x.dtype``
-    (reference ``native.py:69-70``)."""
+    (reference ``native.py:69-70``), or ``out_dtype`` (FP32/BF16: the FP32 result
+    rounded once, what autocast would pass to the next projection)."""
     x = x.contiguous()
     dev = _lib.require_cuda("rms", x, weight)
     code = _lib.dtype_code(x, "rms")
     rows, d = _rows(x)
     w = _weight(weight, d, "rms")
-    y = torch.empty_like(x)
-    _lib.launch("tf_rms_fwd", dev, x.data_ptr(), code, w.data_ptr(), y.data_ptr(), rows, d,
-                float(eps))
+    if out_dtype is None or out_dtype == x.dtype:
+        y = torch.empty_like(x)
+        _lib.launch("tf_rms_fwd", dev, x.data_ptr(), code, w.data_ptr(), y.data_ptr(), rows, d,
+                    float(eps))
+        return y
+    y = torch.empty(x.shape, device=dev, dtype=out_dtype)
+    _lib.launch("tf_rms_out_fwd", dev, x.data_ptr(), code, w.data_ptr(), y.data_ptr(),
+                _lib.dtype_code(y, "rms"), rows, d, float(eps))
     return y
 
 
-def evidence_norm(x, value, gate, weight, mask, eps=1e-5):
+def evidence_norm(x, value, gate, weight, mask, eps=1e-5, out_dtype=torch.float32):
     """RMSNorm of ``x + value * 2 sigmoid(gate)`` on rows where ``mask`` is set
-    (zero rows elsewhere); FP32 output (reference ``native.py:73-74``)."""
+    (zero rows elsewhere); FP32 output (reference ``native.py:73-74``), or BF16 (the
+    FP32 result rounded once) with ``out_dtype``."""
     x, value, gate = x.contiguous(), value.contiguous(), gate.contiguous()
     if value.dtype != gate.dtype:
         gate = gate.to(value.dtype)
@@ -52,10 +59,11 @@ def evidence_norm(x, value, gate, weight, mask, eps=1e-5):
     w = _weight(weight, d, "evidence_norm")
     m = mask.contiguous()
     m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
-    y = torch.empty(x.shape, device=dev, dtype=torch.float32)
-    _lib.launch("tf_evidence_norm_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "evidence_norm"),
+    y = torch.empty(x.shape, device=dev, dtype=out_dtype)
+    _lib.launch("tf_evidence_norm_out_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "evidence_norm"),
                 value.data_ptr(), gate.data_ptr(), _lib.dtype_code(value, "evidence_norm"),
-                w.data_ptr(), m.data_ptr(), y.data_ptr(), rows, d, float(eps))
+                w.data_ptr(), m.data_ptr(), y.data_ptr(), _lib.dtype_code(y, "evidence_norm"), rows, d,
+                float(eps))
     return y
 
 

@@ -90,6 +90,21 @@ def _depthwise(x, conv, mask, lengths, optimized):
     return masked(y.transpose(1, 2), mask)
 
 
+def _bf16_autocast(x):
+    return x.is_cuda and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+
+
+def _plus_depthwise(x, conv, mask, lengths, optimized):
+    """``x + depthwise(x)`` as the next projection's input. On the optimized path under
+    BF16 autocast this is one kernel returning the sum rounded to BF16 — what autocast
+    would pass to the projection; otherwise the FP32 sum."""
+    if optimized and _bf16_autocast(x) and x.dtype == torch.float32 and x.shape[-1] % 4 == 0:
+        from .kernels.buffers import depthwise_masked
+
+        return depthwise_masked(x, conv, lengths, residual=True)
+    return x + _depthwise(x, conv, mask, lengths, optimized)
+
+
 class LocalCNN(nn.Module):
     """GLU up-projection, depthwise conv (k=7), RMSNorm, SiLU, out-projection."""
 
@@ -194,8 +209,11 @@ class TriFusionBlock(nn.Module):
         if opt and x.is_cuda:
             from .kernels import native
 
+            # u feeds only the Mamba in_proj GEMMs: under BF16 autocast it is written in BF16
+            # (the FP32 result rounded once, as autocast would) instead of being cast twice.
             u = native.evidence_norm(x, self.e_value(z), self.e_gate(z), self.u_norm.weight, mask,
-                                     self.u_norm.eps)
+                                     self.u_norm.eps,
+                                     out_dtype=torch.bfloat16 if _bf16_autocast(x) else torch.float32)
             # Both directions in one launch; the recurrence zeroes rows past each length
             # itself (out_proj has no bias) and runs the backward direction reversed.
             fwd, bwd = self.forward_mamba, self.backward_mamba
@@ -216,9 +234,15 @@ class TriFusionBlock(nn.Module):
             mn = keep_zero(self.mn((mf.float() + mb.float()) * 0.5))
         s = torch.cat((cn, mn, an), -1)
         v = keep_zero(gated_concat(s, self.gate(s), self.backend))
-        conv = _depthwise(v, self.merge_dw, mask, lengths, opt)
-        r = keep_zero(x + self.dropout(self.merge(v + conv)))
-        f = swiglu(self.gate_up(self.ff_norm(r)), self.backend)
+        r = keep_zero(x + self.dropout(self.merge(_plus_depthwise(v, self.merge_dw, mask, lengths, opt))))
+        if opt and _bf16_autocast(r) and r.dtype == torch.float32:
+            from .kernels import native
+
+            # ff_norm feeds only gate_up: BF16 out, the FP32 norm rounded once (as autocast would).
+            normed = native.rms(r, self.ff_norm.weight, self.ff_norm.eps, out_dtype=torch.bfloat16)
+        else:
+            normed = self.ff_norm(r)
+        f = swiglu(self.gate_up(normed), self.backend)
         y = self.dropout(self.down(f))
         if opt and r.is_cuda and r.dtype == torch.float32 and r.shape[-1] % 4 == 0:
             from .kernels.buffers import masked_add

@@ -246,6 +246,11 @@ int tf_gated_concat_fwd(const void* x, int dtype, const void* gate, int gate_dty
 int tf_pool4_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int batch, int seqlen,
                  int width, void* stream);
 
+/* Pool4 with the output type chosen: FP32 x, BF16 y (the FP32 means rounded once,
+ * what autocast passes to the attention's qkv projection, model.py:127-129). */
+int tf_pool4_out_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int y_dtype, int batch, int seqlen,
+                     int width, void* stream);
+
 /* A13 masked time mean: y[b,:] = sum_{t<len} x[b,t,:] / len, FP32 [B,D].
  * Replaces decoder.py:60-62 (`(x.float() * mask).sum(1) / lengths`). */
 int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* y, int batch,
@@ -262,6 +267,12 @@ int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch,
  * autocast cast of its output before model.py:198 `gate_up`. */
 int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtype, int64_t rows, int width,
                    float eps, void* stream);
+
+/* RMSNorm then SiLU: a = rms(x) * w rounded to x's type, y = a / (1 + e^-a) (PyTorch's
+ * silu on the norm's output tensor); y has x's type. Replaces model.py:120
+ * `F.silu(self.norm(h))` (RMSNorm of kernels/__init__.py:23-27 and the SiLU). */
+int tf_rms_silu_fwd(const void* x, int dtype, const float* w, void* y, int64_t rows, int width, float eps,
+                    void* stream);
 
 /* Evidence norm as tf_evidence_norm_fwd with the output type chosen (TF_F32 or
  * TF_BF16, the FP32 result rounded once). Replaces native.py:73-74 followed by the

@@ -340,3 +340,17 @@ def test_bf16_outputs_equal_cast_fp32_outputs():
     xm = torch.where(mask[..., None], x, 0.0)
     fused = depthwise_masked(xm, conv, lengths, residual=True)
     assert torch.equal(fused, (xm + depthwise_masked(xm, conv, lengths).float()).to(torch.bfloat16))
+
+
+def test_pool4_bf16_and_rms_silu_exact():
+    """Pool4 into BF16 equals the FP32 means cast once; rms_silu equals PyTorch's silu
+    applied to the norm's BF16 output, bit for bit."""
+    import torch.nn.functional as F
+
+    g = torch.Generator().manual_seed(13)
+    x = (torch.randn(4, 101, 384, generator=g) * 1.5).to(DEV)
+    lengths = torch.tensor([101, 57, 3, 0], device=DEV)
+    assert torch.equal(Pool4.apply(x, lengths, torch.bfloat16), Pool4.apply(x, lengths).to(torch.bfloat16))
+    h = (torch.randn(4, 101, 384, generator=g) * 3).to(torch.bfloat16).to(DEV)
+    w = (1 + 0.05 * torch.randn(384, generator=g)).to(DEV)
+    assert torch.equal(native.rms_silu(h, w, 1e-5), F.silu(native.rms(h, w, 1e-5)))

@@ -9,6 +9,7 @@
 //   * index and copy operators move raw bits (bit-exact by construction).
 // The reference formula each kernel follows is cited at the kernel.
 #include <cstdint>
+#include <type_traits>
 #include <cstdio>
 
 #include "../../include/trifusion_b200.h"
@@ -64,6 +65,8 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 //   kMode 1 (evidence_norm): x' = x + a * 2 sigmoid(b) on rows whose mask is set,
 //                            0 elsewhere; y = rms(x') * w            (FP32 out)
 //   kMode 2 (mean_norm):     x' = (x + a) / 2; y = rms(x') * w       (FP32 out)
+//   kMode 3 (rms + SiLU):    a = round(rms(x) * w); y = a / (1 + e^-a)  (PyTorch's silu on the
+//                            norm's output tensor, model.py:120 `silu(self.norm(h))`)
 // The row is read twice (sum of squares, then scale); the second read hits L1.
 // ---------------------------------------------------------------------------
 template <int kMode, typename TX, typename TA, typename TY, bool kVec4>
@@ -117,17 +120,25 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
     }
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / static_cast<float>(width) + eps);
+    auto silu_of_rounded = [](float t) -> float {
+      float a = t;
+      if constexpr (!std::is_same<TY, float>::value) a = bf16_round(t);
+      return a / (1.f + expf(-a));
+    };
     if (kVec4) {
       for (int c = lane * 4; c < width; c += 128) {
         float4 v = live ? value4(base + c) : make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 wv = load4(w + c);
         v = make_float4(v.x * r * wv.x, v.y * r * wv.y, v.z * r * wv.z, v.w * r * wv.w);
+        if (kMode == 3)
+          v = make_float4(silu_of_rounded(v.x), silu_of_rounded(v.y), silu_of_rounded(v.z), silu_of_rounded(v.w));
         store4(y + base + c, v);
       }
     } else {
       for (int c = lane; c < width; c += 32) {
         const float v = live ? value(base + c) : 0.f;
-        store_f(y + base + c, v * r * w[c]);
+        const float t = v * r * w[c];
+        store_f(y + base + c, kMode == 3 ? silu_of_rounded(t) : t);
       }
     }
   }
@@ -342,10 +353,10 @@ __global__ void __launch_bounds__(kThreads) gated_concat_kernel(const T* __restr
 // The sum runs in the reference's order (k = 0..3, FP32) and the divide is
 // IEEE, so the result equals the reference kernel's bit for bit.
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, typename TY = T>
 __global__ void __launch_bounds__(kThreads) pool4_kernel(const T* __restrict__ x,
                                                          const int64_t* __restrict__ lengths,
-                                                         T* __restrict__ y, int B, int T_, int LT,
+                                                         TY* __restrict__ y, int B, int T_, int LT,
                                                          int D) {
   const int64_t total = static_cast<int64_t>(B) * LT * D;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
@@ -567,6 +578,20 @@ int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtyp
   return tf::launch_row_norm<0, bf16, bf16, bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
 }
 
+int tf_rms_silu_fwd(const void* x, int dtype, const float* w, void* y, int64_t rows, int width, float eps,
+                    void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(dtype)) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !w || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == TF_F32)
+    return tf::launch_row_norm<3, float, float, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+  return tf::launch_row_norm<3, tf::bf16, tf::bf16, tf::bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps,
+                                                            s);
+}
+
 int tf_evidence_norm_out_fwd(const void* x, int x_dtype, const void* value, const void* gate, int vg_dtype,
                              const float* w, const uint8_t* mask, void* y, int y_dtype, int64_t rows, int width,
                              float eps, void* stream) {
@@ -726,6 +751,21 @@ int tf_pool4_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int 
   else
     tf::pool4_kernel<tf::bf16><<<grid, tf::kThreads, 0, s>>>(static_cast<const tf::bf16*>(x), lengths,
                                                              static_cast<tf::bf16*>(y), batch, seqlen, lt, width);
+  return tf::launch_status();
+}
+
+int tf_pool4_out_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int y_dtype, int batch, int seqlen,
+                     int width, void* stream) {
+  if (y_dtype == dtype) return tf_pool4_fwd(x, dtype, lengths, y, batch, seqlen, width, stream);
+  if (batch < 0 || seqlen < 0 || width < 0 || dtype != TF_F32 || y_dtype != TF_BF16) return TF_ERR_ARG;
+  if (batch == 0 || seqlen == 0 || width == 0) return TF_OK;
+  if (!x || !lengths || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const int lt = (seqlen + 3) / 4;
+  const int grid = tf::grid_for(static_cast<int64_t>(batch) * lt * width, tf::kThreads);
+  tf::pool4_kernel<float, tf::bf16><<<grid, tf::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float*>(x), lengths, static_cast<tf::bf16*>(y), batch, seqlen, lt, width);
   return tf::launch_status();
 }
 

@@ -69,14 +69,21 @@ class Pool4:
     """Mean over groups of 4 valid frames (reference ``buffers.py:35-43``)."""
 
     @staticmethod
-    def apply(x, lengths):
+    def apply(x, lengths, out_dtype=None):
+        """``out_dtype`` BF16 for FP32 ``x``: the FP32 means rounded once (what autocast
+        passes to the next projection)."""
         x = x.contiguous()
         dev = _lib.require_cuda("Pool4", x, lengths)
         b, t, d = x.shape
         lengths = lengths.to(torch.int64).contiguous()
-        y = x.new_empty((b, (t + 3) // 4, d))
-        _lib.launch("tf_pool4_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "Pool4"),
-                    lengths.data_ptr(), y.data_ptr(), b, t, d)
+        if out_dtype is None or out_dtype == x.dtype:
+            y = x.new_empty((b, (t + 3) // 4, d))
+            _lib.launch("tf_pool4_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "Pool4"),
+                        lengths.data_ptr(), y.data_ptr(), b, t, d)
+            return y
+        y = torch.empty((b, (t + 3) // 4, d), device=dev, dtype=out_dtype)
+        _lib.launch("tf_pool4_out_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "Pool4"), lengths.data_ptr(),
+                    y.data_ptr(), _lib.dtype_code(y, "Pool4"), b, t, d)
         return y
 
 

@@ -45,6 +45,19 @@ def rms(x, weight, eps=1e-5, out_dtype=None):
     return y
 
 
+def rms_silu(x, weight, eps=1e-5):
+    """``silu(rms(x))`` with the norm rounded to x's type first, as PyTorch's silu
+    sees the norm's output tensor (model.py:120)."""
+    x = x.contiguous()
+    dev = _lib.require_cuda("rms_silu", x, weight)
+    rows, d = _rows(x)
+    w = _weight(weight, d, "rms_silu")
+    y = torch.empty_like(x)
+    _lib.launch("tf_rms_silu_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "rms_silu"), w.data_ptr(), y.data_ptr(),
+                rows, d, float(eps))
+    return y
+
+
 def evidence_norm(x, value, gate, weight, mask, eps=1e-5, out_dtype=torch.float32):
     """RMSNorm of ``x + value * 2 sigmoid(gate)`` on rows where ``mask`` is set
     (zero rows elsewhere); FP32 output (reference ``native.py:73-74``), or BF16 (the

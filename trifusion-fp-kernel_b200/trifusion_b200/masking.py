@@ -59,18 +59,19 @@ class Grids:
         return cls(lengths, time_mask(lengths, time), low_lengths, time_mask(low_lengths, low_time),
                    left, right, src - left, cos, sin, buffer_fusion, native_kernels)
 
-    def pool(self, x):
-        """Mean over groups of 4 valid frames → ``[B, ceil(T/4), D]``."""
+    def pool(self, x, out_dtype=None):
+        """Mean over groups of 4 valid frames → ``[B, ceil(T/4), D]`` (in ``out_dtype``:
+        the means rounded once, or x's type)."""
         if self.buffer_fusion:
             from .kernels.buffers import Pool4
 
-            return Pool4.apply(x.contiguous(), self.lengths)
+            return Pool4.apply(x.contiguous(), self.lengths, out_dtype)
         b, t, d = x.shape
         pad = (-t) % 4
         xs = torch.nn.functional.pad(masked(x, self.mask).float(), (0, 0, 0, pad))
         ms = torch.nn.functional.pad(self.mask, (0, pad)).view(b, -1, 4)
         total = xs.view(b, -1, 4, d).sum(2)
-        return (total / ms.sum(2).clamp(min=1).unsqueeze(-1)).to(x.dtype)
+        return (total / ms.sum(2).clamp(min=1).unsqueeze(-1)).to(out_dtype or x.dtype)
 
     def interpolate(self, low):
         """Back to the main grid: ``a + (b - a) * alpha`` of the two nearest pooled

@@ -123,7 +123,12 @@ class LocalCNN(nn.Module):
         if self.backend == "reference":
             h = masked(h, mask)
         h = _depthwise(h, self.dw, mask, lengths, self.backend != "reference")
-        y = self.out(F.silu(self.norm(h)))
+        if self.backend != "reference" and h.is_cuda:
+            from .kernels import native
+
+            y = self.out(native.rms_silu(h, self.norm.weight, self.norm.eps))  # norm and SiLU, one pass
+        else:
+            y = self.out(F.silu(self.norm(h)))
         return masked(y, mask) if self.backend == "reference" else y
 
 
@@ -139,7 +144,9 @@ class GlobalAttention(nn.Module):
         self.out = nn.Linear(c.dim, c.dim, bias=False)
 
     def forward(self, x, grids):
-        p = grids.pool(x)
+        # The pooled rows feed only the qkv projection: BF16 under autocast on the optimized path.
+        bf16 = self.backend != "reference" and _bf16_autocast(x) and x.dtype == torch.float32
+        p = grids.pool(x, torch.bfloat16 if bf16 else None)
         b, t = p.shape[:2]
         qkv = self.qkv(p)
         mask = grids.low_mask[:, None, None, :]

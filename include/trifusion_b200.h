@@ -268,6 +268,13 @@ int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch,
 int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtype, int64_t rows, int width,
                    float eps, void* stream);
 
+/* Residual add and RMSNorm in one pass: sum = x + a (FP32; a FP32 or BF16, added
+ * exactly) written to `sum`, y = rms(sum) * w in `y_dtype` (rounded once).
+ * Replaces model.py:197-198 (`r = x + merge(...)`, then `ff_norm(r)` and autocast's
+ * cast before gate_up). width % 4 == 0, `sum` 16-byte aligned. */
+int tf_add_rms_fwd(const float* x, const void* a, int a_dtype, const float* w, float* sum, void* y, int y_dtype,
+                   int64_t rows, int width, float eps, void* stream);
+
 /* RMSNorm then SiLU: a = rms(x) * w rounded to x's type, y = a / (1 + e^-a) (PyTorch's
  * silu on the norm's output tensor); y has x's type. Replaces model.py:120
  * `F.silu(self.norm(h))` (RMSNorm of kernels/__init__.py:23-27 and the SiLU). */

@@ -354,3 +354,15 @@ def test_pool4_bf16_and_rms_silu_exact():
     h = (torch.randn(4, 101, 384, generator=g) * 3).to(torch.bfloat16).to(DEV)
     w = (1 + 0.05 * torch.randn(384, generator=g)).to(DEV)
     assert torch.equal(native.rms_silu(h, w, 1e-5), F.silu(native.rms(h, w, 1e-5)))
+
+
+def test_add_rms_exact():
+    """x + a and its RMSNorm in one pass equal PyTorch's FP32 add then the norm kernel, bit for bit."""
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(3, 57, 384, generator=g).to(DEV)
+    a = torch.randn(3, 57, 384, generator=g).to(torch.bfloat16).to(DEV)
+    w = (1 + 0.05 * torch.randn(384, generator=g)).to(DEV)
+    total, y = native.add_rms(x, a, w, 1e-5)
+    ref_total = x + a
+    assert torch.equal(total, ref_total)
+    assert torch.equal(y, native.rms(ref_total, w, 1e-5, out_dtype=torch.bfloat16))

@@ -67,6 +67,8 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 //   kMode 2 (mean_norm):     x' = (x + a) / 2; y = rms(x') * w       (FP32 out)
 //   kMode 3 (rms + SiLU):    a = round(rms(x) * w); y = a / (1 + e^-a)  (PyTorch's silu on the
 //                            norm's output tensor, model.py:120 `silu(self.norm(h))`)
+//   kMode 4 (add + rms):     x' = x + a (FP32, a promoted exactly), written to xo; y = rms(x') * w
+//                            (model.py:197-198 `r = x + merge(...)`, `ff_norm(r)`)
 // The row is read twice (sum of squares, then scale); the second read hits L1.
 // ---------------------------------------------------------------------------
 template <int kMode, typename TX, typename TA, typename TY, bool kVec4>
@@ -76,13 +78,14 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
                                                             const float* __restrict__ w,
                                                             const uint8_t* __restrict__ mask,
                                                             TY* __restrict__ y, int64_t rows,
-                                                            int width, float eps) {
+                                                            int width, float eps, float* __restrict__ xo = nullptr) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
   auto value = [&](int64_t off) -> float {
     float v = load_f(x + off);
     if (kMode == 1) v = v + load_f(a + off) * (2.f * sigmoid_ieee(load_f(b + off)));
     if (kMode == 2) v = (v + load_f(a + off)) * 0.5f;
+    if (kMode == 4) v = v + load_f(a + off);
     return v;
   };
   auto value4 = [&](int64_t off) -> float4 {
@@ -98,6 +101,10 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
       const float4 av = load4(a + off);
       v = make_float4((v.x + av.x) * 0.5f, (v.y + av.y) * 0.5f, (v.z + av.z) * 0.5f,
                       (v.w + av.w) * 0.5f);
+    }
+    if (kMode == 4) {
+      const float4 av = load4(a + off);
+      v = make_float4(v.x + av.x, v.y + av.y, v.z + av.z, v.w + av.w);
     }
     return v;
   };
@@ -128,6 +135,7 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
     if (kVec4) {
       for (int c = lane * 4; c < width; c += 128) {
         float4 v = live ? value4(base + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kMode == 4) store4(xo + base + c, v);
         const float4 wv = load4(w + c);
         v = make_float4(v.x * r * wv.x, v.y * r * wv.y, v.z * r * wv.z, v.w * r * wv.w);
         if (kMode == 3)
@@ -137,6 +145,7 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
     } else {
       for (int c = lane; c < width; c += 32) {
         const float v = live ? value(base + c) : 0.f;
+        if (kMode == 4) xo[base + c] = v;
         const float t = v * r * w[c];
         store_f(y + base + c, kMode == 3 ? silu_of_rounded(t) : t);
       }
@@ -147,7 +156,7 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
 template <int kMode, typename TX, typename TA, typename TY>
 int launch_row_norm(const void* x, const void* a, const void* b, const float* w,
                     const uint8_t* mask, void* y, int64_t rows, int width, float eps,
-                    cudaStream_t s) {
+                    cudaStream_t s, float* xo = nullptr) {
   const bool v4 = width % 4 == 0 && aligned(x, 4 * sizeof(TX)) && aligned(y, 4 * sizeof(TY)) &&
                   aligned(w, 16) && (kMode == 0 || aligned(a, 4 * sizeof(TA))) &&
                   (kMode != 1 || aligned(b, 4 * sizeof(TA)));
@@ -157,9 +166,9 @@ int launch_row_norm(const void* x, const void* a, const void* b, const float* w,
   auto B = static_cast<const TA*>(b);
   auto Y = static_cast<TY*>(y);
   if (v4)
-    row_norm_kernel<kMode, TX, TA, TY, true><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps);
+    row_norm_kernel<kMode, TX, TA, TY, true><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo);
   else
-    row_norm_kernel<kMode, TX, TA, TY, false><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps);
+    row_norm_kernel<kMode, TX, TA, TY, false><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo);
   return launch_status();
 }
 
@@ -576,6 +585,25 @@ int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtyp
   if (y_dtype == TF_F32)
     return tf::launch_row_norm<0, bf16, bf16, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
   return tf::launch_row_norm<0, bf16, bf16, bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+}
+
+int tf_add_rms_fwd(const float* x, const void* a, int a_dtype, const float* w, float* sum, void* y, int y_dtype,
+                   int64_t rows, int width, float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(a_dtype) || !valid_dtype(y_dtype)) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !a || !w || !sum || !y) return TF_ERR_ARG;
+  if (width % 4 || !tf::aligned(sum, 16)) return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  if (a_dtype == TF_BF16 && y_dtype == TF_BF16)
+    return tf::launch_row_norm<4, float, bf16, bf16>(x, a, nullptr, w, nullptr, y, rows, width, eps, s, sum);
+  if (a_dtype == TF_BF16)
+    return tf::launch_row_norm<4, float, bf16, float>(x, a, nullptr, w, nullptr, y, rows, width, eps, s, sum);
+  if (y_dtype == TF_BF16)
+    return tf::launch_row_norm<4, float, float, bf16>(x, a, nullptr, w, nullptr, y, rows, width, eps, s, sum);
+  return tf::launch_row_norm<4, float, float, float>(x, a, nullptr, w, nullptr, y, rows, width, eps, s, sum);
 }
 
 int tf_rms_silu_fwd(const void* x, int dtype, const float* w, void* y, int64_t rows, int width, float eps,

@@ -59,6 +59,7 @@ SIGNATURES = {
     "tf_evidence_norm_out_fwd": [_p, _i, _p, _p, _i, _p, _p, _p, _i, _q, _i, _f, _p],
     "tf_depthwise_residual_fwd": [_p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _p],
     "tf_rms_silu_fwd": [_p, _i, _p, _p, _q, _i, _f, _p],
+    "tf_add_rms_fwd": [_p, _p, _i, _p, _p, _p, _i, _q, _i, _f, _p],
     "tf_pool4_out_fwd": [_p, _i, _p, _p, _i, _i, _i, _i, _p],
     "tf_front_residual_fwd": [_p, _p, _i, _p, _p, _i, _i, _i, _i, _p],
     "tf_bands_fwd": [_p, _i, _p, _i, _i, _i, _i, _p],

@@ -45,6 +45,22 @@ def rms(x, weight, eps=1e-5, out_dtype=None):
     return y
 
 
+def add_rms(x, a, weight, eps=1e-5, out_dtype=torch.bfloat16):
+    """``(x + a, rms(x + a))``: the FP32 residual sum (x FP32, a FP32 or BF16) and its
+    RMSNorm in ``out_dtype`` (rounded once), in one pass (model.py:197-198)."""
+    x, a = x.contiguous(), a.contiguous()
+    dev = _lib.require_cuda("add_rms", x, a, weight)
+    if x.dtype != torch.float32 or a.shape != x.shape:
+        raise ValueError("add_rms: x must be FP32 and a of the same shape")
+    rows, d = _rows(x)
+    w = _weight(weight, d, "add_rms")
+    total = torch.empty_like(x)
+    y = torch.empty(x.shape, device=dev, dtype=out_dtype)
+    _lib.launch("tf_add_rms_fwd", dev, x.data_ptr(), a.data_ptr(), _lib.dtype_code(a, "add_rms"), w.data_ptr(),
+                total.data_ptr(), y.data_ptr(), _lib.dtype_code(y, "add_rms"), rows, d, float(eps))
+    return total, y
+
+
 def rms_silu(x, weight, eps=1e-5):
     """``silu(rms(x))`` with the norm rounded to x's type first, as PyTorch's silu
     sees the norm's output tensor (model.py:120)."""

@@ -241,13 +241,15 @@ class TriFusionBlock(nn.Module):
             mn = keep_zero(self.mn((mf.float() + mb.float()) * 0.5))
         s = torch.cat((cn, mn, an), -1)
         v = keep_zero(gated_concat(s, self.gate(s), self.backend))
-        r = keep_zero(x + self.dropout(self.merge(_plus_depthwise(v, self.merge_dw, mask, lengths, opt))))
-        if opt and _bf16_autocast(r) and r.dtype == torch.float32:
+        merged = self.dropout(self.merge(_plus_depthwise(v, self.merge_dw, mask, lengths, opt)))
+        if opt and _bf16_autocast(x) and x.dtype == torch.float32 and x.shape[-1] % 4 == 0:
             from .kernels import native
 
-            # ff_norm feeds only gate_up: BF16 out, the FP32 norm rounded once (as autocast would).
-            normed = native.rms(r, self.ff_norm.weight, self.ff_norm.eps, out_dtype=torch.bfloat16)
+            # The residual sum and ff_norm in one pass; ff_norm feeds only gate_up, so it is
+            # written in BF16 (the FP32 norm rounded once, as autocast would).
+            r, normed = native.add_rms(x, merged, self.ff_norm.weight, self.ff_norm.eps)
         else:
+            r = keep_zero(x + merged)
             normed = self.ff_norm(r)
         f = swiglu(self.gate_up(normed), self.backend)
         y = self.dropout(self.down(f))

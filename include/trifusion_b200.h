@@ -275,6 +275,29 @@ int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtyp
 int tf_add_rms_fwd(const float* x, const void* a, int a_dtype, const float* w, float* sum, void* y, int y_dtype,
                    int64_t rows, int width, float eps, void* stream);
 
+/* RMSNorm as tf_rms_out_fwd, written into the slice of a wider row: output row r
+ * starts at y + r * y_pitch (elements, >= width). With `y2` non-NULL the same
+ * values are also written, rounded once to BF16, at y2 + r * y2_pitch. Replaces
+ * model.py:159-161 (`cn`, `an`, then `torch.cat((cn, an))` for e_down): each norm
+ * writes its half of e_down's input row and its third of the gate's BF16 input
+ * row directly. */
+int tf_rms_pitched_fwd(const void* x, int dtype, const float* w, void* y, int y_dtype, int64_t y_pitch,
+                       void* y2, int64_t y2_pitch, int64_t rows, int width, float eps, void* stream);
+
+/* mean_norm (tf_mean_norm_fwd, FP32 y [rows, width]) that also writes y rounded
+ * once to BF16 at y2 + r * y2_pitch: the middle third of the gate's input row,
+ * which model.py:185-186 forms as `torch.cat((cn, mn, an))` cast by autocast. */
+int tf_mean_norm_copy_fwd(const void* a, const void* b, int dtype, const float* w, float* y, void* y2,
+                          int64_t y2_pitch, int64_t rows, int width, float eps, void* stream);
+
+/* Branch gate (tf_gated_concat_fwd) over three separate branch tensors instead of
+ * their concatenation: branch 0 at x0 + r * pitches[0], branch 1 (FP32) at
+ * x1 + r * pitches[1], branch 2 at x2 + r * pitches[2]; x0/x2 of type `dtype`;
+ * y [rows, 3d] FP32. Bit-equal to tf_gated_concat_fwd on the FP32 concatenation.
+ * Replaces model.py:185-186 `gated_concat(torch.cat((cn, mn, an)), gate)`. */
+int tf_gated_branches_fwd(const void* x0, const float* x1, const void* x2, int dtype, const int64_t* pitches,
+                          const void* gate, int gate_dtype, float* y, int64_t rows, int d, void* stream);
+
 /* RMSNorm then SiLU: a = rms(x) * w rounded to x's type, y = a / (1 + e^-a) (PyTorch's
  * silu on the norm's output tensor); y has x's type. Replaces model.py:120
  * `F.silu(self.norm(h))` (RMSNorm of kernels/__init__.py:23-27 and the SiLU). */

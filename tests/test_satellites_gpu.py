@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available():
     pytest.skip("needs a CUDA GPU", allow_module_level=True)
 
-from trifusion_b200.kernels import gated_concat, reverse_valid, swiglu  # noqa: E402
+from trifusion_b200.kernels import gated_branches, gated_concat, reverse_valid, swiglu  # noqa: E402
 from trifusion_b200.kernels import native  # noqa: E402
 from trifusion_b200.kernels.buffers import Pool4, mamba_controls, mask_buffer, masked_add  # noqa: E402
 
@@ -366,3 +366,33 @@ def test_add_rms_exact():
     ref_total = x + a
     assert torch.equal(total, ref_total)
     assert torch.equal(y, native.rms(ref_total, w, 1e-5, out_dtype=torch.bfloat16))
+
+
+@pytest.mark.parametrize("width", [384, 30])
+def test_norms_into_concatenated_rows_and_branch_gate_exact(width):
+    """The block's concatenations written in place: cn/an norms into slices of e_down's
+    and the gate's input rows, mean_norm's BF16 copy, and the branch gate read from the
+    three pieces, each equal bit for bit to the torch.cat forms (width 30: scalar path)."""
+    g = torch.Generator().manual_seed(23)
+    b, t, d = 2, 75, width
+    lc = torch.randn(b, t, d, generator=g).to(torch.bfloat16).to(DEV)
+    at = torch.randn(b, t, d, generator=g).to(torch.bfloat16).to(DEV)
+    mf = torch.randn(b, t, d, generator=g).to(torch.bfloat16).to(DEV)
+    mb = torch.randn(b, t, d, generator=g).to(torch.bfloat16).to(DEV)
+    wc, wa, wm = [(1 + 0.05 * torch.randn(d, generator=g)).to(DEV) for _ in range(3)]
+    gate = torch.randn(b, t, 3, generator=g).to(torch.bfloat16).to(DEV)
+    e_in = torch.full((b, t, 2 * d), float("nan"), dtype=torch.bfloat16, device=DEV)
+    s16 = torch.full((b, t, 3 * d), float("nan"), dtype=torch.bfloat16, device=DEV)
+    cn = native.rms_into(lc, wc, 1e-5, e_in[..., :d], s16[..., :d])
+    an = native.rms_into(at, wa, 1e-5, e_in[..., d:], s16[..., 2 * d:])
+    mn = native.mean_norm(mf, mb, wm, 1e-5, copy_to=s16[..., d:2 * d])
+    rc, ra = native.rms(lc, wc, 1e-5), native.rms(at, wa, 1e-5)
+    rm = native.mean_norm(mf, mb, wm, 1e-5)
+    assert torch.equal(mn, rm)
+    assert torch.equal(e_in, torch.cat((rc, ra), -1))
+    s = torch.cat((rc, rm, ra), -1)
+    assert torch.equal(s16, s.to(torch.bfloat16))
+    assert torch.equal(gated_branches(cn, mn, an, gate), gated_concat(s, gate))
+    f32 = torch.empty(b, t, 2 * d, device=DEV)
+    native.rms_into(lc, wc, 1e-5, f32[..., d:])
+    assert torch.equal(f32[..., d:], native.rms(lc, wc, 1e-5, out_dtype=torch.float32))

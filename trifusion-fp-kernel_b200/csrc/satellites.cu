@@ -70,6 +70,9 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 //   kMode 4 (add + rms):     x' = x + a (FP32, a promoted exactly), written to xo; y = rms(x') * w
 //                            (model.py:197-198 `r = x + merge(...)`, `ff_norm(r)`)
 // The row is read twice (sum of squares, then scale); the second read hits L1.
+// Output rows start every `yp` elements (0: every `width`), so a norm can write its
+// slice of a concatenated row in place; `y2` (optional, BF16, rows every `y2p`)
+// receives the same values rounded once, the copy autocast would make for a projection.
 // ---------------------------------------------------------------------------
 template <int kMode, typename TX, typename TA, typename TY, bool kVec4>
 __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict__ x,
@@ -78,7 +81,9 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
                                                             const float* __restrict__ w,
                                                             const uint8_t* __restrict__ mask,
                                                             TY* __restrict__ y, int64_t rows,
-                                                            int width, float eps, float* __restrict__ xo = nullptr) {
+                                                            int width, float eps, float* __restrict__ xo = nullptr,
+                                                            int64_t yp = 0, bf16* __restrict__ y2 = nullptr,
+                                                            int64_t y2p = 0) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
   auto value = [&](int64_t off) -> float {
@@ -110,6 +115,7 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
   };
   for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
     const int64_t base = row * width;
+    const int64_t ybase = row * (yp ? yp : width);
     const bool live = kMode != 1 || mask[row] != 0;
     float ss = 0.f;
     if (live) {
@@ -140,14 +146,16 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
         v = make_float4(v.x * r * wv.x, v.y * r * wv.y, v.z * r * wv.z, v.w * r * wv.w);
         if (kMode == 3)
           v = make_float4(silu_of_rounded(v.x), silu_of_rounded(v.y), silu_of_rounded(v.z), silu_of_rounded(v.w));
-        store4(y + base + c, v);
+        store4(y + ybase + c, v);
+        if (y2) store4(y2 + row * y2p + c, v);
       }
     } else {
       for (int c = lane; c < width; c += 32) {
         const float v = live ? value(base + c) : 0.f;
         if (kMode == 4) xo[base + c] = v;
         const float t = v * r * w[c];
-        store_f(y + base + c, kMode == 3 ? silu_of_rounded(t) : t);
+        store_f(y + ybase + c, kMode == 3 ? silu_of_rounded(t) : t);
+        if (y2) store_f(y2 + row * y2p + c, t);
       }
     }
   }
@@ -156,19 +164,23 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
 template <int kMode, typename TX, typename TA, typename TY>
 int launch_row_norm(const void* x, const void* a, const void* b, const float* w,
                     const uint8_t* mask, void* y, int64_t rows, int width, float eps,
-                    cudaStream_t s, float* xo = nullptr) {
+                    cudaStream_t s, float* xo = nullptr, int64_t yp = 0, bf16* y2 = nullptr,
+                    int64_t y2p = 0) {
   const bool v4 = width % 4 == 0 && aligned(x, 4 * sizeof(TX)) && aligned(y, 4 * sizeof(TY)) &&
                   aligned(w, 16) && (kMode == 0 || aligned(a, 4 * sizeof(TA))) &&
-                  (kMode != 1 || aligned(b, 4 * sizeof(TA)));
+                  (kMode != 1 || aligned(b, 4 * sizeof(TA))) && yp % 4 == 0 &&
+                  (!y2 || (aligned(y2, 8) && y2p % 4 == 0));
   const int grid = grid_for(rows, kThreads / 32);
   auto X = static_cast<const TX*>(x);
   auto A = static_cast<const TA*>(a);
   auto B = static_cast<const TA*>(b);
   auto Y = static_cast<TY*>(y);
   if (v4)
-    row_norm_kernel<kMode, TX, TA, TY, true><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo);
+    row_norm_kernel<kMode, TX, TA, TY, true><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo,
+                                                                      yp, y2, y2p);
   else
-    row_norm_kernel<kMode, TX, TA, TY, false><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo);
+    row_norm_kernel<kMode, TX, TA, TY, false><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo,
+                                                                       yp, y2, y2p);
   return launch_status();
 }
 
@@ -531,6 +543,58 @@ int launch_swiglu(const void* x, void* y, int64_t rows, int d, cudaStream_t s) {
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Branch gate over three separate branch tensors (model.py:185-186
+// `s = cat((cn, mn, an))`, `gated_concat(s, gate(s))`): branch j is read from its
+// own rows (pitch p_j elements), so the FP32 concatenation is never written.
+// Branches 0 and 2 have type T02, branch 1 is FP32; the output is the FP32
+// [rows, 3 d] row the concatenated form produces (every branch value promotes to
+// FP32 exactly, so the result equals it bit for bit).
+// ---------------------------------------------------------------------------
+template <typename T02, typename TG, bool kVec4>
+__global__ void __launch_bounds__(kThreads) gated_branches_kernel(const T02* __restrict__ x0, int64_t p0,
+                                                                  const float* __restrict__ x1, int64_t p1,
+                                                                  const T02* __restrict__ x2, int64_t p2,
+                                                                  const TG* __restrict__ gate,
+                                                                  float* __restrict__ y, int64_t rows, int d) {
+  const int step = kVec4 ? 4 : 1;
+  const int64_t per_branch = d / step;
+  const int64_t total = rows * 3 * per_branch;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t branch_row = i / per_branch;  // r * 3 + j
+    const int64_t r = branch_row / 3;
+    const int j = static_cast<int>(branch_row - r * 3);
+    const int c = static_cast<int>(i % per_branch) * step;
+    const float s = 2.f * sigmoid_ieee(load_f(gate + branch_row));
+    const int64_t off = branch_row * d + c;
+    if (kVec4) {
+      const float4 v = j == 1 ? load4(x1 + r * p1 + c) : load4((j == 0 ? x0 + r * p0 : x2 + r * p2) + c);
+      store4(y + off, make_float4(v.x * s, v.y * s, v.z * s, v.w * s));
+    } else {
+      const float v = j == 1 ? x1[r * p1 + c] : load_f((j == 0 ? x0 + r * p0 : x2 + r * p2) + c);
+      y[off] = v * s;
+    }
+  }
+}
+
+template <typename T02, typename TG>
+int launch_gated_branches(const void* x0, int64_t p0, const float* x1, int64_t p1, const void* x2, int64_t p2,
+                          const void* g, float* y, int64_t rows, int d, cudaStream_t s) {
+  const bool v4 = d % 4 == 0 && p0 % 4 == 0 && p1 % 4 == 0 && p2 % 4 == 0 && aligned(x0, 4 * sizeof(T02)) &&
+                  aligned(x1, 16) && aligned(x2, 4 * sizeof(T02)) && aligned(y, 16);
+  const int64_t items = rows * 3 * (v4 ? d / 4 : d);
+  const int grid = grid_for(items, kThreads);
+  auto X0 = static_cast<const T02*>(x0);
+  auto X2 = static_cast<const T02*>(x2);
+  auto G = static_cast<const TG*>(g);
+  if (v4)
+    gated_branches_kernel<T02, TG, true><<<grid, kThreads, 0, s>>>(X0, p0, x1, p1, X2, p2, G, y, rows, d);
+  else
+    gated_branches_kernel<T02, TG, false><<<grid, kThreads, 0, s>>>(X0, p0, x1, p1, X2, p2, G, y, rows, d);
+  return launch_status();
+}
+
 template <typename T, typename TG>
 int launch_gated_concat(const void* x, const void* g, void* y, int64_t rows, int d, cudaStream_t s) {
   const bool v4 = d % 4 == 0 && aligned(x, 4 * sizeof(T)) && aligned(y, 4 * sizeof(T));
@@ -585,6 +649,30 @@ int tf_rms_out_fwd(const void* x, int dtype, const float* w, void* y, int y_dtyp
   if (y_dtype == TF_F32)
     return tf::launch_row_norm<0, bf16, bf16, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
   return tf::launch_row_norm<0, bf16, bf16, bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s);
+}
+
+int tf_rms_pitched_fwd(const void* x, int dtype, const float* w, void* y, int y_dtype, int64_t y_pitch,
+                       void* y2, int64_t y2_pitch, int64_t rows, int width, float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(dtype) || !valid_dtype(y_dtype)) return TF_ERR_ARG;
+  if (y_pitch < width || (y2 && y2_pitch < width)) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !w || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  auto Y2 = static_cast<bf16*>(y2);
+  if (dtype == TF_F32 && y_dtype == TF_F32)
+    return tf::launch_row_norm<0, float, float, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s,
+                                                       nullptr, y_pitch, Y2, y2_pitch);
+  if (dtype == TF_F32)
+    return tf::launch_row_norm<0, float, float, bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s,
+                                                      nullptr, y_pitch, Y2, y2_pitch);
+  if (y_dtype == TF_F32)
+    return tf::launch_row_norm<0, bf16, bf16, float>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s,
+                                                     nullptr, y_pitch, Y2, y2_pitch);
+  return tf::launch_row_norm<0, bf16, bf16, bf16>(x, nullptr, nullptr, w, nullptr, y, rows, width, eps, s,
+                                                  nullptr, y_pitch, Y2, y2_pitch);
 }
 
 int tf_add_rms_fwd(const float* x, const void* a, int a_dtype, const float* w, float* sum, void* y, int y_dtype,
@@ -675,6 +763,22 @@ int tf_mean_norm_fwd(const void* a, const void* b, int dtype, const float* w, fl
   return tf::launch_row_norm<2, tf::bf16, tf::bf16, float>(a, b, nullptr, w, nullptr, y, rows, width, eps, s);
 }
 
+int tf_mean_norm_copy_fwd(const void* a, const void* b, int dtype, const float* w, float* y, void* y2,
+                          int64_t y2_pitch, int64_t rows, int width, float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(dtype) || y2_pitch < width) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!a || !b || !w || !y || !y2) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto Y2 = static_cast<tf::bf16*>(y2);
+  if (dtype == TF_F32)
+    return tf::launch_row_norm<2, float, float, float>(a, b, nullptr, w, nullptr, y, rows, width, eps, s, nullptr,
+                                                       0, Y2, y2_pitch);
+  return tf::launch_row_norm<2, tf::bf16, tf::bf16, float>(a, b, nullptr, w, nullptr, y, rows, width, eps, s,
+                                                           nullptr, 0, Y2, y2_pitch);
+}
+
 int tf_mamba_controls_fwd(const void* a, const void* ddt, int dtype, const int64_t* strides,
                           const float* dt_bias, float a_floor, float* adt, float* dt, int batch,
                           int seqlen, int heads, void* stream) {
@@ -761,6 +865,25 @@ int tf_gated_concat_fwd(const void* x, int dtype, const void* gate, int gate_dty
   if (dtype == TF_F32) return tf::launch_gated_concat<float, bf16>(x, gate, y, rows, d, s);
   if (gate_dtype == TF_F32) return tf::launch_gated_concat<bf16, float>(x, gate, y, rows, d, s);
   return tf::launch_gated_concat<bf16, bf16>(x, gate, y, rows, d, s);
+}
+
+int tf_gated_branches_fwd(const void* x0, const float* x1, const void* x2, int dtype, const int64_t* pitches,
+                          const void* gate, int gate_dtype, float* y, int64_t rows, int d, void* stream) {
+  if (rows < 0 || d < 0 || !valid_dtype(dtype) || !valid_dtype(gate_dtype) || !pitches) return TF_ERR_ARG;
+  if (pitches[0] < d || pitches[1] < d || pitches[2] < d) return TF_ERR_ARG;
+  if (rows == 0 || d == 0) return TF_OK;
+  if (!x0 || !x1 || !x2 || !gate || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  const int64_t p0 = pitches[0], p1 = pitches[1], p2 = pitches[2];
+  if (dtype == TF_F32 && gate_dtype == TF_F32)
+    return tf::launch_gated_branches<float, float>(x0, p0, x1, p1, x2, p2, gate, y, rows, d, s);
+  if (dtype == TF_F32) return tf::launch_gated_branches<float, bf16>(x0, p0, x1, p1, x2, p2, gate, y, rows, d, s);
+  if (gate_dtype == TF_F32)
+    return tf::launch_gated_branches<bf16, float>(x0, p0, x1, p1, x2, p2, gate, y, rows, d, s);
+  return tf::launch_gated_branches<bf16, bf16>(x0, p0, x1, p1, x2, p2, gate, y, rows, d, s);
 }
 
 int tf_pool4_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int batch, int seqlen,

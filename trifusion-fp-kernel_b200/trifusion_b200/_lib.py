@@ -46,6 +46,9 @@ SIGNATURES = {
     "tf_reverse_valid_fwd": [_p, _p, _p, _i, _i, _q, _p],
     "tf_swiglu_fwd": [_p, _i, _p, _q, _i, _p],
     "tf_gated_concat_fwd": [_p, _i, _p, _i, _p, _q, _i, _p],
+    "tf_gated_branches_fwd": [_p, _p, _p, _i, _p, _p, _i, _p, _q, _i, _p],
+    "tf_rms_pitched_fwd": [_p, _i, _p, _p, _i, _q, _p, _q, _q, _i, _f, _p],
+    "tf_mean_norm_copy_fwd": [_p, _p, _i, _p, _p, _p, _q, _q, _i, _f, _p],
     "tf_pool4_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
     "tf_masked_mean_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
     "tf_end_gather_fwd": [_p, _p, _p, _i, _i, _q, _p],

@@ -93,3 +93,28 @@ def gated_concat(x, gate, backend="l4"):
     _lib.launch("tf_gated_concat_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "gated_concat"),
                 gate.data_ptr(), _lib.dtype_code(gate, "gated_concat"), y.data_ptr(), rows, d)
     return y
+
+
+def gated_branches(x0, x1, x2, gate):
+    """``gated_concat(torch.cat((x0, x1, x2), -1), gate)`` without the concatenation:
+    x0 and x2 share a dtype (they may be slices of a wider row buffer), x1 is FP32, the
+    result is the FP32 ``[..., 3 d]`` row, bit-equal to the concatenated form
+    (reference ``model.py:185-186``)."""
+    from .native import _row_pitch
+
+    dev = _lib.require_cuda("gated_branches", x0, x1, x2, gate)
+    d = x1.shape[-1]
+    x1 = x1.contiguous()
+    if x1.dtype != torch.float32 or x0.dtype != x2.dtype or x0.shape != x1.shape or x2.shape != x1.shape:
+        raise ValueError("gated_branches: x1 must be FP32, x0/x2 of one dtype, all of one shape")
+    if gate.shape != (*x1.shape[:-1], 3):
+        raise ValueError("gated_branches: gate must be [..., 3]")
+    gate = gate.contiguous()
+    rows = gate.numel() // 3
+    pitches = _lib.int64_array([_row_pitch(x0, d, "gated_branches"), _row_pitch(x1, d, "gated_branches"),
+                                _row_pitch(x2, d, "gated_branches")])
+    y = torch.empty((*x1.shape[:-1], 3 * d), device=dev, dtype=torch.float32)
+    _lib.launch("tf_gated_branches_fwd", dev, x0.data_ptr(), x1.data_ptr(), x2.data_ptr(),
+                _lib.dtype_code(x0, "gated_branches"), pitches, gate.data_ptr(),
+                _lib.dtype_code(gate, "gated_branches"), y.data_ptr(), rows, d)
+    return y

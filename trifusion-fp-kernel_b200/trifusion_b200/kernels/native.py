@@ -45,6 +45,47 @@ def rms(x, weight, eps=1e-5, out_dtype=None):
     return y
 
 
+def _row_pitch(t, width, op):
+    """Elements between consecutive rows of ``t`` (all leading dims flattened into rows):
+    ``t`` may be the slice of a wider row buffer, but its last dim must be contiguous
+    and its rows evenly spaced."""
+    if t.dim() < 1 or t.shape[-1] != width or (width > 1 and t.stride(-1) != 1):
+        raise ValueError(f"{op}: output must be [..., {width}] with a contiguous last dim")
+    lead = [(t.shape[i], t.stride(i)) for i in range(t.dim() - 1) if t.shape[i] > 1]
+    if not lead:
+        return width
+    pitch = expected = lead[-1][1]
+    for size, stride in reversed(lead):
+        if stride != expected:
+            raise ValueError(f"{op}: output rows must be evenly spaced")
+        expected *= size
+    if pitch < width:
+        raise ValueError(f"{op}: output rows overlap")
+    return pitch
+
+
+def rms_into(x, weight, eps, out, out2=None):
+    """RMSNorm of ``x``'s rows written into ``out`` (FP32 or BF16; may be the slice of a
+    wider concatenated row) and, when ``out2`` is given, the same values rounded once
+    into the BF16 view ``out2``: the norm writes its part of a ``torch.cat`` input
+    in place (model.py:159-161, 185). Returns ``out``."""
+    x = x.contiguous()
+    dev = _lib.require_cuda("rms_into", x, weight, out)
+    rows, d = _rows(x)
+    w = _weight(weight, d, "rms_into")
+    if out.shape != x.shape:
+        raise ValueError("rms_into: out must have x's shape")
+    pitch = _row_pitch(out, d, "rms_into")
+    ptr2, pitch2 = None, 0
+    if out2 is not None:
+        if out2.shape != x.shape or out2.dtype != torch.bfloat16 or out2.device != out.device:
+            raise ValueError("rms_into: out2 must be a BF16 tensor of x's shape on out's device")
+        ptr2, pitch2 = out2.data_ptr(), _row_pitch(out2, d, "rms_into")
+    _lib.launch("tf_rms_pitched_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "rms_into"), w.data_ptr(),
+                out.data_ptr(), _lib.dtype_code(out, "rms_into"), pitch, ptr2, pitch2, rows, d, float(eps))
+    return out
+
+
 def add_rms(x, a, weight, eps=1e-5, out_dtype=torch.bfloat16):
     """``(x + a, rms(x + a))``: the FP32 residual sum (x FP32, a FP32 or BF16) and its
     RMSNorm in ``out_dtype`` (rounded once), in one pass (model.py:197-198)."""
@@ -96,8 +137,10 @@ def evidence_norm(x, value, gate, weight, mask, eps=1e-5, out_dtype=torch.float3
     return y
 
 
-def mean_norm(a, b, weight, eps=1e-5):
-    """RMSNorm of ``(a + b) / 2``; FP32 output (reference ``native.py:77-78``)."""
+def mean_norm(a, b, weight, eps=1e-5, copy_to=None):
+    """RMSNorm of ``(a + b) / 2``; FP32 output (reference ``native.py:77-78``). With
+    ``copy_to`` (a BF16 view of the output's shape, rows evenly spaced) the result is
+    also written there rounded once."""
     a, b = a.contiguous(), b.contiguous()
     if b.dtype != a.dtype:
         b = b.to(a.dtype)
@@ -107,6 +150,13 @@ def mean_norm(a, b, weight, eps=1e-5):
     rows, d = _rows(a)
     w = _weight(weight, d, "mean_norm")
     y = torch.empty(a.shape, device=dev, dtype=torch.float32)
+    if copy_to is not None:
+        if copy_to.shape != a.shape or copy_to.dtype != torch.bfloat16 or copy_to.device != y.device:
+            raise ValueError("mean_norm: copy_to must be a BF16 tensor of the output's shape")
+        _lib.launch("tf_mean_norm_copy_fwd", dev, a.data_ptr(), b.data_ptr(), _lib.dtype_code(a, "mean_norm"),
+                    w.data_ptr(), y.data_ptr(), copy_to.data_ptr(), _row_pitch(copy_to, d, "mean_norm"), rows, d,
+                    float(eps))
+        return y
     _lib.launch("tf_mean_norm_fwd", dev, a.data_ptr(), b.data_ptr(), _lib.dtype_code(a, "mean_norm"),
                 w.data_ptr(), y.data_ptr(), rows, d, float(eps))
     return y

@@ -25,7 +25,7 @@ from torch import nn
 
 from .attention import masked_attention
 from .front import Frontend
-from .kernels import RMSNorm, gated_concat, reverse_valid, swiglu
+from .kernels import RMSNorm, gated_branches, gated_concat, reverse_valid, swiglu
 from .masking import Grids, masked
 
 
@@ -210,9 +210,25 @@ class TriFusionBlock(nn.Module):
         if opt and not input_masked:
             x = _mask_rows(x, mask, True)
         h = keep_zero(self.pre(x))
-        cn = keep_zero(self.cn(self.local(h, mask, lengths)))
-        an = keep_zero(self.an(self.attention(h, grids)))
-        z = F.silu(self.e_down(torch.cat((cn, an), -1)))
+        local, attended = self.local(h, mask, lengths), self.attention(h, grids)
+        d = local.shape[-1]
+        # BF16 branch outputs on the GPU: the cn/an norms write their parts of e_down's
+        # input row and of the gate's BF16 input row in place of the two concatenations
+        # (and of autocast's cast of the FP32 one); every value is the same.
+        split = (opt and x.is_cuda and local.dtype == torch.bfloat16 and attended.dtype == torch.bfloat16
+                 and d % 4 == 0)
+        if split:
+            from .kernels import native
+
+            e_in = local.new_empty(*local.shape[:-1], 2 * d)
+            s16 = local.new_empty(*local.shape[:-1], 3 * d)
+            cn = native.rms_into(local, self.cn.weight, self.cn.eps, e_in[..., :d], s16[..., :d])
+            an = native.rms_into(attended, self.an.weight, self.an.eps, e_in[..., d:], s16[..., 2 * d:])
+            z = F.silu(self.e_down(e_in))
+        else:
+            cn = keep_zero(self.cn(local))
+            an = keep_zero(self.an(attended))
+            z = F.silu(self.e_down(torch.cat((cn, an), -1)))
         if opt and x.is_cuda:
             from .kernels import native
 
@@ -231,7 +247,8 @@ class TriFusionBlock(nn.Module):
             else:
                 mf = fwd(u, lengths)
                 mb = reverse_valid(bwd(reverse_valid(u, lengths), lengths), lengths)
-            mn = native.mean_norm(mf, mb, self.mn.weight, self.mn.eps)
+            mn = native.mean_norm(mf, mb, self.mn.weight, self.mn.eps,
+                                  copy_to=s16[..., d:2 * d] if split else None)
         else:
             evidence = self.e_value(z).float() * (2 * torch.sigmoid(self.e_gate(z).float()))
             u = _mask_rows(self.u_norm(x + evidence), mask, opt)
@@ -239,8 +256,11 @@ class TriFusionBlock(nn.Module):
             mb = reverse_valid(self.backward_mamba(reverse_valid(u, lengths, self.backend)),
                                lengths, self.backend)
             mn = keep_zero(self.mn((mf.float() + mb.float()) * 0.5))
-        s = torch.cat((cn, mn, an), -1)
-        v = keep_zero(gated_concat(s, self.gate(s), self.backend))
+        if split:
+            v = gated_branches(cn, mn, an, self.gate(s16))
+        else:
+            s = torch.cat((cn, mn, an), -1)
+            v = keep_zero(gated_concat(s, self.gate(s), self.backend))
         merged = self.dropout(self.merge(_plus_depthwise(v, self.merge_dw, mask, lengths, opt)))
         if opt and _bf16_autocast(x) and x.dtype == torch.float32 and x.shape[-1] % 4 == 0:
             from .kernels import native

@@ -298,6 +298,19 @@ int tf_mean_norm_copy_fwd(const void* a, const void* b, int dtype, const float* 
 int tf_gated_branches_fwd(const void* x0, const float* x1, const void* x2, int dtype, const int64_t* pitches,
                           const void* gate, int gate_dtype, float* y, int64_t rows, int d, void* stream);
 
+/* Branch gate with its three-output projection, one warp per row: from the BF16
+ * gate-input row s (width 3d, rows every s_pitch elements), g_j = bf16(s . w[j] +
+ * bias[j]) with FP32 products and sums (w [3, 3d] BF16, bias [3] BF16 or NULL),
+ * then y[r, j, :] = x_j * 2 sigmoid(g_j) into FP32 y [rows, 3d], with branches 0
+ * and 2 read from s and branch 1 from the FP32 rows x1 (x1_pitch). g [rows, 3]
+ * BF16 receives the gate values when non-NULL. d % 4 == 0, s/w 8-byte and x1/y
+ * 16-byte aligned, pitches multiples of 4 (else TF_ERR_LAYOUT). Replaces
+ * model.py:185-186 `gated_concat(s, self.gate(s))` under BF16 autocast (the
+ * nn.Linear(3d, 3) GEMM and kernels/__init__.py:57-81); g equals the GEMM's
+ * output up to FP32 summation order. */
+int tf_gate_branches_fwd(const void* s, int64_t s_pitch, const float* x1, int64_t x1_pitch, const void* w,
+                         const void* bias, float* y, void* g, int64_t rows, int d, void* stream);
+
 /* RMSNorm then SiLU: a = rms(x) * w rounded to x's type, y = a / (1 + e^-a) (PyTorch's
  * silu on the norm's output tensor); y has x's type. Replaces model.py:120
  * `F.silu(self.norm(h))` (RMSNorm of kernels/__init__.py:23-27 and the SiLU). */

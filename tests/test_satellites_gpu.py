@@ -396,3 +396,54 @@ def test_norms_into_concatenated_rows_and_branch_gate_exact(width):
     f32 = torch.empty(b, t, 2 * d, device=DEV)
     native.rms_into(lc, wc, 1e-5, f32[..., d:])
     assert torch.equal(f32[..., d:], native.rms(lc, wc, 1e-5, out_dtype=torch.float32))
+
+
+def test_gate_projection_and_branch_gate_in_one_pass():
+    """The gate's three-output projection computed per row (FP32 sums) is within one
+    BF16 ulp of the FP32 projection rounded once, and the gated row equals the branch
+    gate applied with those gate values, bit for bit. (cuBLAS's BF16 GEMM for N = 3
+    may reduce split-K partial sums in BF16, PyTorch's default
+    allow_bf16_reduced_precision_reduction, so it is compared more loosely.)"""
+    from trifusion_b200.kernels import gate_branches
+
+    g = torch.Generator().manual_seed(29)
+    b, t, d = 3, 91, 384
+    s16 = torch.randn(b, t, 3 * d, generator=g).to(torch.bfloat16).to(DEV)
+    mn = torch.randn(b, t, d, generator=g).to(DEV)
+    w = (0.05 * torch.randn(3, 3 * d, generator=g)).to(torch.bfloat16).to(DEV)
+    bias = torch.randn(3, generator=g).to(torch.bfloat16).to(DEV)
+    gate = torch.empty(b, t, 3, dtype=torch.bfloat16, device=DEV)
+    v = gate_branches(s16, mn, w, bias, gate_out=gate)
+    ref = torch.nn.functional.linear(s16.float(), w.float(), bias.float()).to(torch.bfloat16)
+    ulp = torch.finfo(torch.bfloat16).eps * ref.float().abs().clamp_min(2.0 ** -126)
+    assert ((gate.float() - ref.float()).abs() <= ulp * 1.01 + 1e-5).all()  # 1 ulp; near-cancelling sums aside
+    assert torch.equal(v, gated_branches(s16[..., :d], mn, s16[..., 2 * d:], gate))
+    # without gate_out and bias, on a slice of a wider row buffer
+    wide = torch.zeros(b, t, 3 * d + 8, dtype=torch.bfloat16, device=DEV)
+    wide[..., 4:4 + 3 * d] = s16
+    gate2 = torch.empty_like(gate)
+    v2 = gate_branches(wide[..., 4:4 + 3 * d], mn, w, gate_out=gate2)
+    ref2 = torch.nn.functional.linear(s16.float(), w.float()).to(torch.bfloat16)
+    ulp2 = torch.finfo(torch.bfloat16).eps * ref2.float().abs().clamp_min(2.0 ** -126)
+    assert ((gate2.float() - ref2.float()).abs() <= ulp2 * 1.01 + 1e-5).all()
+    assert torch.equal(v2, gated_branches(s16[..., :d], mn, s16[..., 2 * d:], gate2))
+
+
+def test_stacked_in_proj_matches_separate_projections():
+    """Both directions' in_proj as one GEMM over zero-padded, stacked weights: the
+    views equal the separate projections to BF16 rounding, and their rows are
+    16-byte aligned."""
+    from types import SimpleNamespace
+
+    from trifusion_b200.mamba import projections
+
+    g = torch.Generator().manual_seed(31)
+    mods = [SimpleNamespace(in_proj=torch.nn.Linear(384, 1860, bias=False).to(DEV)) for _ in range(2)]
+    u = torch.randn(4, 77, 384, generator=g).to(torch.bfloat16).to(DEV)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        pf, pb = projections(mods, u)
+        rf, rb = mods[0].in_proj(u), mods[1].in_proj(u)
+    assert pf.shape == rf.shape and pf.stride(-2) == 2 * 1864 and pf.stride(-2) * 2 % 16 == 0
+    for got, ref in ((pf, rf), (pb, rb)):
+        assert got.dtype == ref.dtype == torch.bfloat16
+        torch.testing.assert_close(got.float(), ref.float(), atol=2e-2, rtol=1e-2)

@@ -595,6 +595,66 @@ int launch_gated_branches(const void* x0, int64_t p0, const float* x1, int64_t p
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Branch gate with its projection (model.py:185-186: `gate(s)` under BF16 autocast,
+// then `gated_concat`, kernels/__init__.py:57-81). One warp per row computes
+//   g_j = bf16(sum_k s[r, k] w[j, k] + bias[j])     (j = 0..2; FP32 products and sums)
+// from the BF16 gate-input row s (rows every `sp` elements, width 3 d), then writes
+//   y[r, j, :] = x_j[r, :] * 2 sigmoid(g_j)          (FP32, [rows, 3 d])
+// where branches 0 and 2 are read back from s (the BF16 values the concatenation
+// holds) and branch 1 from the FP32 rows x1. The second read of s hits L1. The
+// three-output projection would otherwise be a GEMM with N = 3, for which the
+// library's kernels are far from the roofline. `g` (optional) receives the gate values.
+// Requires d % 4 == 0 and 8-/16-byte aligned rows (checked by the entry point).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) gate_branches_kernel(const bf16* __restrict__ s, int64_t sp,
+                                                                 const float* __restrict__ x1, int64_t p1,
+                                                                 const bf16* __restrict__ w,
+                                                                 const bf16* __restrict__ bias,
+                                                                 float* __restrict__ y, bf16* __restrict__ g,
+                                                                 int64_t rows, int d) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  const int width = 3 * d;
+  for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const bf16* sr = s + row * sp;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+    for (int c = lane * 4; c < width; c += 128) {
+      const float4 v = load4(sr + c);
+      const float4 w0 = load4(w + c), w1 = load4(w + width + c), w2 = load4(w + 2 * width + c);
+      a0 = fmaf(v.x, w0.x, a0); a0 = fmaf(v.y, w0.y, a0); a0 = fmaf(v.z, w0.z, a0); a0 = fmaf(v.w, w0.w, a0);
+      a1 = fmaf(v.x, w1.x, a1); a1 = fmaf(v.y, w1.y, a1); a1 = fmaf(v.z, w1.z, a1); a1 = fmaf(v.w, w1.w, a1);
+      a2 = fmaf(v.x, w2.x, a2); a2 = fmaf(v.y, w2.y, a2); a2 = fmaf(v.z, w2.z, a2); a2 = fmaf(v.w, w2.w, a2);
+    }
+    a0 = warp_sum(a0);
+    a1 = warp_sum(a1);
+    a2 = warp_sum(a2);
+    if (bias) {
+      a0 += __bfloat162float(bias[0]);
+      a1 += __bfloat162float(bias[1]);
+      a2 += __bfloat162float(bias[2]);
+    }
+    const float g0 = bf16_round(a0), g1 = bf16_round(a1), g2 = bf16_round(a2);
+    const float s0 = 2.f * sigmoid_ieee(g0), s1 = 2.f * sigmoid_ieee(g1), s2 = 2.f * sigmoid_ieee(g2);
+    float* yr = y + row * width;
+    const float* xr = x1 + row * p1;
+    for (int c = lane * 4; c < width; c += 128) {
+      const int j = c / d;  // d % 4 == 0: a 4-vector never straddles two branches
+      const float4 v = j == 1 ? load4(xr + (c - d)) : load4(sr + c);
+      const float sc = j == 0 ? s0 : (j == 1 ? s1 : s2);
+      store4(yr + c, make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc));
+    }
+    if (g && lane < 3) g[row * 3 + lane] = __float2bfloat16_rn(lane == 0 ? g0 : (lane == 1 ? g1 : g2));
+  }
+}
+
+int launch_gate_branches(const bf16* s, int64_t sp, const float* x1, int64_t p1, const bf16* w, const bf16* bias,
+                         float* y, bf16* g, int64_t rows, int d, cudaStream_t st) {
+  const int grid = grid_for(rows, kThreads / 32);
+  gate_branches_kernel<<<grid, kThreads, 0, st>>>(s, sp, x1, p1, w, bias, y, g, rows, d);
+  return launch_status();
+}
+
 template <typename T, typename TG>
 int launch_gated_concat(const void* x, const void* g, void* y, int64_t rows, int d, cudaStream_t s) {
   const bool v4 = d % 4 == 0 && aligned(x, 4 * sizeof(T)) && aligned(y, 4 * sizeof(T));
@@ -884,6 +944,24 @@ int tf_gated_branches_fwd(const void* x0, const float* x1, const void* x2, int d
   if (gate_dtype == TF_F32)
     return tf::launch_gated_branches<bf16, float>(x0, p0, x1, p1, x2, p2, gate, y, rows, d, s);
   return tf::launch_gated_branches<bf16, bf16>(x0, p0, x1, p1, x2, p2, gate, y, rows, d, s);
+}
+
+int tf_gate_branches_fwd(const void* s, int64_t s_pitch, const float* x1, int64_t x1_pitch, const void* w,
+                         const void* bias, float* y, void* g, int64_t rows, int d, void* stream) {
+  if (rows < 0 || d < 0) return TF_ERR_ARG;
+  if (s_pitch < 3 * static_cast<int64_t>(d) || x1_pitch < d) return TF_ERR_ARG;
+  if (rows == 0 || d == 0) return TF_OK;
+  if (!s || !x1 || !w || !y) return TF_ERR_ARG;
+  using tf::aligned;
+  if (d % 4 || s_pitch % 4 || x1_pitch % 4 || !aligned(s, 8) || !aligned(w, 8) || !aligned(x1, 16) ||
+      !aligned(y, 16))
+    return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  using tf::bf16;
+  return tf::launch_gate_branches(static_cast<const bf16*>(s), s_pitch, x1, x1_pitch, static_cast<const bf16*>(w),
+                                  static_cast<const bf16*>(bias), y, static_cast<bf16*>(g), rows, d,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 int tf_pool4_fwd(const void* x, int dtype, const int64_t* lengths, void* y, int batch, int seqlen,

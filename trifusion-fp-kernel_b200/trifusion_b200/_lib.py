@@ -47,6 +47,7 @@ SIGNATURES = {
     "tf_swiglu_fwd": [_p, _i, _p, _q, _i, _p],
     "tf_gated_concat_fwd": [_p, _i, _p, _i, _p, _q, _i, _p],
     "tf_gated_branches_fwd": [_p, _p, _p, _i, _p, _p, _i, _p, _q, _i, _p],
+    "tf_gate_branches_fwd": [_p, _q, _p, _q, _p, _p, _p, _p, _q, _i, _p],
     "tf_rms_pitched_fwd": [_p, _i, _p, _p, _i, _q, _p, _q, _q, _i, _f, _p],
     "tf_mean_norm_copy_fwd": [_p, _p, _i, _p, _p, _p, _q, _q, _i, _f, _p],
     "tf_pool4_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],

@@ -95,6 +95,39 @@ def gated_concat(x, gate, backend="l4"):
     return y
 
 
+def gate_branches(s, x1, weight, bias=None, gate_out=None):
+    """``gated_concat(cat(s0, x1, s2), linear(s, weight, bias))`` in one pass under BF16
+    arithmetic: ``s`` is the BF16 gate-input row ``[..., 3 d]`` (rows evenly spaced;
+    its first and last thirds are the gated branches 0 and 2), ``x1`` the FP32 branch 1,
+    ``weight`` ``[3, 3 d]`` and ``bias`` ``[3]`` BF16. The gate values are the BF16
+    projection with FP32 sums (the GEMM's up to summation order), written to
+    ``gate_out`` ([..., 3] BF16) when given. Returns the FP32 ``[..., 3 d]`` row
+    (reference ``model.py:185-186``)."""
+    from .native import _row_pitch
+
+    dev = _lib.require_cuda("gate_branches", s, x1, weight)
+    d = x1.shape[-1]
+    x1 = x1.contiguous()
+    if s.dtype != torch.bfloat16 or s.shape[:-1] != x1.shape[:-1] or s.shape[-1] != 3 * d:
+        raise ValueError("gate_branches: s must be BF16 [..., 3 d] with x1 [..., d]")
+    if x1.dtype != torch.float32 or weight.dtype != torch.bfloat16 or tuple(weight.shape) != (3, 3 * d):
+        raise ValueError("gate_branches: x1 must be FP32 and weight BF16 [3, 3 d]")
+    weight = weight.contiguous()
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or bias.numel() != 3:
+            raise ValueError("gate_branches: bias must be BF16 [3]")
+        bias = bias.contiguous()
+    rows = x1.numel() // d if d else 0
+    y = torch.empty((*x1.shape[:-1], 3 * d), device=dev, dtype=torch.float32)
+    if gate_out is not None and (gate_out.dtype != torch.bfloat16 or gate_out.shape != (*x1.shape[:-1], 3)
+                                 or not gate_out.is_contiguous()):
+        raise ValueError("gate_branches: gate_out must be a contiguous BF16 [..., 3] tensor")
+    _lib.launch("tf_gate_branches_fwd", dev, s.data_ptr(), _row_pitch(s, 3 * d, "gate_branches"), x1.data_ptr(),
+                d, weight.data_ptr(), None if bias is None else bias.data_ptr(), y.data_ptr(),
+                None if gate_out is None else gate_out.data_ptr(), rows, d)
+    return y
+
+
 def gated_branches(x0, x1, x2, gate):
     """``gated_concat(torch.cat((x0, x1, x2), -1), gate)`` without the concatenation:
     x0 and x2 share a dtype (they may be slices of a wider row buffer), x1 is FP32, the

@@ -2,7 +2,8 @@
 ``mamba.py``), running the B200 recurrence.
 
 Optimized path (``fused_recurrence=True``, what ``load_student`` sets): one
-cuBLAS GEMM (``in_proj``), ONE recurrence launch that also computes the A/dt
+cuBLAS GEMM (``in_proj``, both directions of a pair in one, rows padded to 16 bytes),
+ONE recurrence launch that also computes the A/dt
 controls from the projection, applies the C/B RMSNorm of the raw q/k rows and
 the length mask, and one cuBLAS GEMM (``out_proj``); ``bidirectional_pair``
 runs a block's two directions in one launch. With ``fused_recurrence=False``
@@ -18,6 +19,43 @@ import torch.nn.functional as F
 from torch import nn
 
 from .kernels import RMSNorm
+
+
+_STACKED = {}
+
+
+def _stacked_in_proj(mods, dtype):
+    """The ``in_proj`` weights of ``mods`` as one ``[len(mods) * pitch, dim]`` matrix of
+    ``dtype``, each ``[width, dim]`` weight followed by zero rows up to ``pitch`` (width
+    rounded up to a multiple of 8), so every projection row starts on a 16-byte
+    boundary. Cached until a weight changes (version counter or storage)."""
+    ws = [m.in_proj.weight for m in mods]
+    key = (tuple(id(w) for w in ws), dtype)
+    stamp = tuple((w._version, w.data_ptr(), w.device) for w in ws)
+    hit = _STACKED.get(key)
+    if hit is None or hit[0] != stamp:
+        width, dim = ws[0].shape
+        pitch = (width + 7) // 8 * 8
+        stacked = torch.zeros(len(ws) * pitch, dim, dtype=dtype, device=ws[0].device)
+        for i, w in enumerate(ws):
+            stacked[i * pitch:i * pitch + width] = w.detach().to(dtype)
+        hit = (stamp, stacked, pitch)
+        _STACKED[key] = hit
+    return hit[1], hit[2]
+
+
+def projections(mods, u):
+    """``[m.in_proj(u) for m in mods]`` as ONE GEMM over the stacked, padded weights:
+    views of a ``[..., len(mods) * pitch]`` output whose rows are 16-byte aligned
+    (the in_proj width, 1860 at dim 384, is not a multiple of 8; cuBLAS then falls
+    back to kernels without TMA). The operands are what ``in_proj`` would use: under
+    autocast the weights in the autocast type, otherwise in their own type."""
+    dev = u.device.type
+    dtype = torch.get_autocast_dtype(dev) if torch.is_autocast_enabled(dev) else mods[0].in_proj.weight.dtype
+    w, pitch = _stacked_in_proj(mods, dtype)
+    width = mods[0].in_proj.weight.shape[0]
+    p = F.linear(u, w)
+    return [p[..., i * pitch:i * pitch + width] for i in range(len(mods))]
 
 
 class Mamba3Inference(nn.Module):
@@ -73,12 +111,13 @@ class Mamba3Inference(nn.Module):
         """``u`` [B, T, dim] → [B, T, dim]. With ``lengths`` ([B] int64), rows at
         or past each length come out zero (the block's length mask)."""
         b, t, _ = u.shape
-        p = self.in_proj(u)
         if self.fused_recurrence and self.backend != "reference":
             from .mamba_fused import fused_recurrence_multi
 
+            p = projections([self], u)[0] if u.is_cuda else self.in_proj(u)
             y = fused_recurrence_multi([self._direction(p, b, t)], lengths=lengths, eps=self.C_norm.eps)[0]
             return self._out(y, b, t)
+        p = self.in_proj(u)
         z, v, k, q, ddt, a, trap, angles = self._split(p)
         adt, dt = self._controls(a, ddt)
         angles = angles.unsqueeze(2).expand(b, t, self.nheads, self.num_rope_angles)
@@ -114,7 +153,7 @@ def bidirectional_pair(fwd, bwd, u, lengths):
     from .mamba_fused import fused_recurrence_multi
 
     b, t, _ = u.shape
-    pf, pb = fwd.in_proj(u), bwd.in_proj(u)
+    pf, pb = projections([fwd, bwd], u) if u.is_cuda else (fwd.in_proj(u), bwd.in_proj(u))
     yf, yb = fused_recurrence_multi([fwd._direction(pf, b, t), bwd._direction(pb, b, t, reverse=True)],
                                     lengths=lengths, eps=fwd.C_norm.eps)
     return fwd._out(yf, b, t), bwd._out(yb, b, t)

@@ -25,7 +25,7 @@ from torch import nn
 
 from .attention import masked_attention
 from .front import Frontend
-from .kernels import RMSNorm, gated_branches, gated_concat, reverse_valid, swiglu
+from .kernels import RMSNorm, gate_branches, gated_concat, reverse_valid, swiglu
 from .masking import Grids, masked
 
 
@@ -257,7 +257,12 @@ class TriFusionBlock(nn.Module):
                                lengths, self.backend)
             mn = keep_zero(self.mn((mf.float() + mb.float()) * 0.5))
         if split:
-            v = gated_branches(cn, mn, an, self.gate(s16))
+            from .kernels.buffers import _param_bf16
+
+            # The three-output gate projection and the branch gate in one pass (one warp
+            # per row) instead of a GEMM with N = 3 and a second pass.
+            v = gate_branches(s16, mn, _param_bf16(self.gate.weight, tuple(self.gate.weight.shape)),
+                              None if self.gate.bias is None else _param_bf16(self.gate.bias, (3,)))
         else:
             s = torch.cat((cn, mn, an), -1)
             v = keep_zero(gated_concat(s, self.gate(s), self.backend))

@@ -256,6 +256,20 @@ int tf_pool4_out_fwd(const void* x, int dtype, const int64_t* lengths, void* y, 
 int tf_masked_mean_fwd(const void* x, int dtype, const int64_t* lengths, float* y, int batch,
                        int seqlen, int width, void* stream);
 
+/* Decoder query read: 10 queries x 8 heads of width 32 (q [10, 256] BF16, head c at
+ * columns 32c) attend in FP32 over keys and values read from the BF16 projection rows
+ * kv [batch, time, >= 512] (row pitch kv_pitch elements, a multiple of 8, base 16-byte
+ * aligned; k of head c at column 32c, v at 256 + 32c); key j is valid when
+ * j < min(time, lengths[b] * keys_per_length). y [batch, 10, 256] BF16 (row i holds the
+ * 8 heads' outputs side by side); a row with no valid key is NaN, like the reference's
+ * softmax. `state` is FP32 scratch of tf_query_read_state_floats(batch, time) floats.
+ * Replaces decoder.py:26-30 (the kv permute, q expand, attention.py:8-18
+ * `masked_attention` and the transpose/reshape before `out`); equal to it up to FP32
+ * summation order. */
+int64_t tf_query_read_state_floats(int batch, int time);
+int tf_query_read_fwd(const void* q, const void* kv, int64_t kv_pitch, const int64_t* lengths, int keys_per_length,
+                      float* state, int64_t state_floats, void* y, int batch, int time, void* stream);
+
 /* A13 end gather: y[b] = x[b, len-1] (len = 0 reads row T-1, like PyTorch's -1 index).
  * Replaces decoder.py:63 (`mf[arange(b), lengths - 1]`). */
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,

@@ -447,3 +447,34 @@ def test_stacked_in_proj_matches_separate_projections():
     for got, ref in ((pf, rf), (pb, rb)):
         assert got.dtype == ref.dtype == torch.bfloat16
         torch.testing.assert_close(got.float(), ref.float(), atol=2e-2, rtol=1e-2)
+
+
+def _query_read_f64(q, kv, lengths, keys_per_length):
+    """FP64 restatement of decoder.py:26-30 on the same BF16 operands."""
+    qd, kvd = q.double().cpu(), kv.double().cpu()
+    b, t, _ = kvd.shape
+    k = kvd[..., :256].view(b, t, 8, 32).permute(0, 2, 1, 3)
+    v = kvd[..., 256:512].view(b, t, 8, 32).permute(0, 2, 1, 3)
+    qh = qd.view(10, 8, 32).transpose(0, 1)
+    s = torch.einsum("hid,bhjd->bhij", qh, k) / 32 ** 0.5
+    valid = torch.arange(t)[None, :] < (lengths.cpu() * keys_per_length)[:, None]
+    s = s.masked_fill(~valid[:, None, None, :], float("-inf"))
+    h = torch.einsum("bhij,bhjd->bhid", s.softmax(-1), v)
+    return h.transpose(1, 2).reshape(b, 10, 256)
+
+
+@pytest.mark.parametrize("batch,time,kpl,lens", [(3, 200, 1, [200, 57, 1]), (2, 1608, 8, [201, 13]),
+                                                  (2, 700, 1, [700, 256])])
+def test_query_read_matches_float64_attention(batch, time, kpl, lens):
+    """Split-key decoder attention: within one BF16 ulp of the FP64 softmax attention
+    on the same BF16 operands, masked by lengths (8 keys per frame for the fine read),
+    from contiguous and from pitched projection rows."""
+    g = torch.Generator().manual_seed(37)
+    q = (0.5 * torch.randn(10, 256, generator=g)).to(torch.bfloat16).to(DEV)
+    wide = torch.randn(batch, time, 520, generator=g).to(torch.bfloat16).to(DEV)
+    lengths = torch.tensor(lens, device=DEV)
+    for kv in (wide[..., :512].contiguous(), wide[..., 8:520]):
+        y = native.query_read(q, kv, lengths, kpl)
+        ref = _query_read_f64(q, kv, lengths, kpl)
+        err = (y.double().cpu() - ref).abs()
+        assert (err <= 2.0 ** -7 * ref.abs() + 1e-6).all(), float(err.max())

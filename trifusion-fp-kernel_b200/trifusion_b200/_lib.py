@@ -48,6 +48,8 @@ SIGNATURES = {
     "tf_gated_concat_fwd": [_p, _i, _p, _i, _p, _q, _i, _p],
     "tf_gated_branches_fwd": [_p, _p, _p, _i, _p, _p, _i, _p, _q, _i, _p],
     "tf_gate_branches_fwd": [_p, _q, _p, _q, _p, _p, _p, _p, _q, _i, _p],
+    "tf_query_read_state_floats": [_i, _i],
+    "tf_query_read_fwd": [_p, _p, _q, _p, _i, _p, _q, _p, _i, _i, _p],
     "tf_rms_pitched_fwd": [_p, _i, _p, _p, _i, _q, _p, _q, _q, _i, _f, _p],
     "tf_mean_norm_copy_fwd": [_p, _p, _i, _p, _p, _p, _q, _q, _i, _f, _p],
     "tf_pool4_fwd": [_p, _i, _p, _p, _i, _i, _i, _p],
@@ -70,7 +72,8 @@ SIGNATURES = {
 }
 _RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p,
              "tf_recurrence_workspace_size": ctypes.c_size_t,
-             "tf_recurrence_workspace_size_multi": ctypes.c_size_t}
+             "tf_recurrence_workspace_size_multi": ctypes.c_size_t,
+             "tf_query_read_state_floats": ctypes.c_int64}
 
 
 class RecurrenceIO(ctypes.Structure):

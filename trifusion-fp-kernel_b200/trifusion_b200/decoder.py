@@ -30,10 +30,22 @@ class QueryRead(nn.Module):
         self.q = nn.Linear(256, 256, bias=False)
         self.out = nn.Linear(256, 256, bias=False)
 
-    def forward(self, query, x, mask):
+    def forward(self, query, x, mask, lengths=None, keys_per_length=1):
+        """``mask`` [B, T] bool, or None with ``lengths`` given (key j valid when
+        ``j < lengths * keys_per_length``). With ``lengths`` on the GPU under BF16
+        arithmetic the attention runs as one split-key kernel over the projection
+        rows (``native.query_read``)."""
         b, t, _ = x.shape
-        k, v = self.kv(x).view(b, t, 2, 8, 32).permute(2, 0, 3, 1, 4).unbind(0)
-        q = self.q(query).view(10, 8, 32).transpose(0, 1).unsqueeze(0).expand(b, -1, -1, -1)
+        kv, qp = self.kv(x), self.q(query)
+        if lengths is not None and x.is_cuda and kv.dtype == torch.bfloat16 and qp.dtype == torch.bfloat16:
+            from .kernels.native import query_read
+
+            h = self.out(query_read(qp, kv, lengths, keys_per_length))
+            return h[:, :4].mean(1), h[:, 4:8].mean(1), h[:, 8:].mean(1)
+        if mask is None:
+            mask = time_mask(lengths * keys_per_length, t)
+        k, v = kv.view(b, t, 2, 8, 32).permute(2, 0, 3, 1, 4).unbind(0)
+        q = qp.view(10, 8, 32).transpose(0, 1).unsqueeze(0).expand(b, -1, -1, -1)
         h = masked_attention(q, k, v, mask[:, None, None, :])
         h = self.out(h.transpose(1, 2).reshape(b, 10, 256))
         return h[:, :4].mean(1), h[:, 4:8].mean(1), h[:, 8:].mean(1)
@@ -65,11 +77,15 @@ class Decoder(nn.Module):
     def forward(self, x, fine, grids, fine_lengths, mf, mb):
         b, tf_, _, _ = fine.shape
         fine_mask = time_mask(fine_lengths, tf_)
-        deep_q = self.deep_read(self.query, x, grids.mask)
+        native = self.native_kernels and x.is_cuda
+        deep_q = self.deep_read(self.query, x, grids.mask, grids.lengths if native else None)
         fp = (fine + sin_position(tf_, 64, fine.device)[None, :, None, :].to(fine.dtype)
               + self.band.to(fine.dtype)[None, None, :, :])
-        fine_q = self.fine_read(self.query, fp.flatten(1, 2),
-                                fine_mask[:, :, None].expand(b, tf_, 8).reshape(b, -1))
+        if native:  # key t * 8 + band is valid when t < fine_lengths
+            fine_q = self.fine_read(self.query, fp.flatten(1, 2), None, fine_lengths, keys_per_length=8)
+        else:
+            fine_q = self.fine_read(self.query, fp.flatten(1, 2),
+                                    fine_mask[:, :, None].expand(b, tf_, 8).reshape(b, -1))
         mean, end = self._pooled(x, mf, grids.lengths, grids.mask)
         global_feature = self.global_proj(mean)
         memory = self.memory_proj(torch.cat((end, mb[:, 0]), -1))

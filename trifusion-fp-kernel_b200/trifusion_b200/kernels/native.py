@@ -175,6 +175,32 @@ def masked_mean(x, lengths):
     return y
 
 
+def query_read(q, kv, lengths, keys_per_length=1):
+    """The decoder's query-read attention (reference ``decoder.py:26-30``): ``q`` the
+    BF16 ``[10, 256]`` query projection, ``kv`` the BF16 ``[B, T, 512]`` key/value
+    projection (rows may be the slices of wider rows), key j of batch entry b valid
+    when ``j < lengths[b] * keys_per_length``. Returns the BF16 ``[B, 10, 256]`` rows
+    the out projection reads (the 8 heads side by side), FP32 softmax inside."""
+    dev = _lib.require_cuda("query_read", q, kv, lengths)
+    if q.dtype != torch.bfloat16 or kv.dtype != torch.bfloat16 or tuple(q.shape) != (10, 256):
+        raise ValueError("query_read: q must be BF16 [10, 256] and kv BF16 [B, T, 512]")
+    if kv.dim() != 3 or kv.shape[-1] != 512:
+        raise ValueError("query_read: kv must be [B, T, 512]")
+    q = q.contiguous()
+    b, t, _ = kv.shape
+    pitch = _row_pitch(kv, 512, "query_read")
+    if kv.data_ptr() % 16 or pitch % 8:
+        kv = kv.contiguous()
+        pitch = 512
+    lengths = lengths.to(torch.int64).contiguous()
+    n = int(_lib.lib().tf_query_read_state_floats(b, t))
+    state = torch.empty(max(n, 1), device=dev, dtype=torch.float32)
+    y = torch.empty((b, 10, 256), device=dev, dtype=torch.bfloat16)
+    _lib.launch("tf_query_read_fwd", dev, q.data_ptr(), kv.data_ptr(), pitch, lengths.data_ptr(),
+                int(keys_per_length), state.data_ptr(), n, y.data_ptr(), b, t)
+    return y
+
+
 def end_gather(x, lengths):
     """``x[arange(B), lengths - 1]`` — the last valid row of each batch entry
     (reference ``decoder.py:63``); bit-exact."""

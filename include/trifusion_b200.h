@@ -338,6 +338,14 @@ int tf_evidence_norm_out_fwd(const void* x, int x_dtype, const void* value, cons
                              const float* w, const uint8_t* mask, void* y, int y_dtype, int64_t rows, int width,
                              float eps, void* stream);
 
+/* Evidence norm as tf_evidence_norm_out_fwd with `value` and `gate` rows every
+ * vg_pitch elements (>= width), e.g. the two halves of one stacked projection row
+ * [rows, 2 * width]. Replaces native.py:73-74 fed by model.py:163-166's two
+ * projections `e_value(z)`, `e_gate(z)` (here one GEMM over both weights). */
+int tf_evidence_norm_pitched_fwd(const void* x, int x_dtype, const void* value, const void* gate, int vg_dtype,
+                                 int64_t vg_pitch, const float* w, const uint8_t* mask, void* y, int y_dtype,
+                                 int64_t rows, int width, float eps, void* stream);
+
 /* Depthwise Conv1d over time on [B, T, C] rows with zero padding outside [0, T):
  * y[b,t,c] = t < lengths[b] ? sum_k x[b, t+k-K/2, c] w[c,k] + bias[c] : 0, inputs
  * rounded to BF16, BF16 out; w [C, K] and bias [C] (may be NULL) BF16; K in
@@ -360,6 +368,18 @@ int tf_depthwise_residual_fwd(const void* x, int dtype, const void* w, const voi
  * kernels/primitives.py:116-150) and the FP32 widening of attention.py:14-16. */
 int tf_rotary_qkv_fwd(const void* x, const float* cosv, const float* sinv, float* y, int batch,
                       int time, int heads, int head_dim, void* stream);
+
+/* Rotary q/k and FP32 masked attention over the pooled rows in one kernel: x
+ * [B, LT, 3, H, 64] BF16 (the qkv projection); q and k rotated as tf_rotary_qkv_fwd
+ * (cosv/sinv [>= LT, 32] FP32) and rounded to BF16, v as is; key j valid when
+ * j < lengths[b]; scores scaled by 1/8, softmax and sums in FP32. y [B, LT, H*64]
+ * BF16 (the heads side by side, the out projection's input rows); a row with no
+ * valid key is NaN, like the reference's softmax. head_dim must be 64. Replaces
+ * model.py:127-133 after `qkv` (kernels/buffers.py:46-55 `RotaryQKV.apply`,
+ * attention.py:8-18 `masked_attention`, the transpose/reshape before `out`); equal
+ * to it up to FP32 summation order. */
+int tf_pooled_attention_fwd(const void* x, const float* cosv, const float* sinv, const int64_t* lengths, void* y,
+                            int batch, int low_time, int heads, int head_dim, void* stream);
 
 /* Interpolation from the pooled grid: y[b, t] = t < lengths[b] ?
  * a + (z - a) alpha[b, t] : 0 with a = low[b, left[b, t]], z = low[b, right[b, t]];

@@ -124,3 +124,19 @@ def test_front_stem_matches_cudnn_stage(shape, lens):
     assert torch.equal(s.float(), s_ref.float())
     close_bf16(h, h_ref, ulps=2, atol=ULP * 2.0 ** -6)
     assert (h.permute(0, 2, 3, 1)[~valid[:, 0, :, 0]] == 0).all()
+
+
+@pytest.mark.parametrize("cin,cout,t,f", [(32, 64, 401, 129), (64, 128, 201, 65)])
+def test_strided_skip_as_gemm(cin, cout, t, f):
+    """The stride-2 stages' 1x1 skip convolution as a gather of the subsampled
+    channels-last rows and one BF16 GEMM: equal to cuDNN's convolution up to FP32
+    summation order (one BF16 ulp)."""
+    from trifusion_b200.front import CNNStage
+
+    torch.manual_seed(3)
+    st = CNNStage(cin, cout, 2, "l4").cuda().to(torch.bfloat16).to(memory_format=torch.channels_last)
+    x = torch.randn(2, cin, t, f, device="cuda").to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        ref, got = st.skip(x), st._skip_rows(x)
+    assert got.shape == ref.shape and got.is_contiguous(memory_format=torch.channels_last)
+    torch.testing.assert_close(got.float(), ref.float(), atol=1e-2, rtol=2 ** -7)

@@ -478,3 +478,53 @@ def test_query_read_matches_float64_attention(batch, time, kpl, lens):
         ref = _query_read_f64(q, kv, lengths, kpl)
         err = (y.double().cpu() - ref).abs()
         assert (err <= 2.0 ** -7 * ref.abs() + 1e-6).all(), float(err.max())
+
+
+@pytest.mark.parametrize("batch,low_time,lens", [(3, 50, [50, 17, 1]), (2, 130, [130, 33])])
+def test_pooled_attention_matches_float64(batch, low_time, lens):
+    """Rotary + FP32 masked attention over the pooled rows in one kernel: within one
+    BF16 ulp of FP64 attention on the rotated BF16 q/k (the rotary kernel's output,
+    itself bit-exact with the reference formula), keys masked by the lengths."""
+    from trifusion_b200.kernels.buffers import RotaryQKV
+    from trifusion_b200.masking import rotary_table
+
+    heads = 6
+    g = torch.Generator().manual_seed(41)
+    qkv = torch.randn(batch, low_time, 3 * heads * 64, generator=g).to(torch.bfloat16).to(DEV)
+    cos, sin = rotary_table(low_time, 64, DEV)
+    lengths = torch.tensor(lens, device=DEV)
+    y = native.pooled_attention(qkv, cos, sin, lengths, heads)
+    q, k, v = RotaryQKV.apply(qkv, cos, sin, heads, torch.float32).double().cpu().unbind(0)
+    s = q @ k.transpose(-1, -2) / 8.0
+    valid = torch.arange(low_time)[None, :] < lengths.cpu()[:, None]
+    s = s.masked_fill(~valid[:, None, None, :], float("-inf"))
+    ref = (s.softmax(-1) @ v).transpose(1, 2).reshape(batch, low_time, heads * 64)
+    err = (y.double().cpu() - ref).abs()
+    assert (err <= 2.0 ** -7 * ref.abs() + 1e-6).all(), float(err.max())
+
+
+def test_evidence_norm_reads_stacked_halves_in_place():
+    """value/gate as the two halves of one stacked projection row: equal bit for bit
+    to the same values passed as separate contiguous tensors; the stacked GEMM equals
+    the two projections to BF16 rounding."""
+    from trifusion_b200.kernels.buffers import stacked_linear
+
+    g = torch.Generator().manual_seed(43)
+    b, t, d, r = 3, 70, 384, 48
+    x = torch.randn(b, t, d, generator=g).to(DEV)
+    z = torch.randn(b, t, r, generator=g).to(torch.bfloat16).to(DEV)
+    ev_v, ev_g = torch.nn.Linear(r, d).to(DEV), torch.nn.Linear(r, d).to(DEV)
+    w = (1 + 0.05 * torch.randn(d, generator=g)).to(DEV)
+    mask = torch.arange(t, device=DEV)[None, :] < torch.tensor([70, 31, 1], device=DEV)[:, None]
+    wst, bst, pitch = stacked_linear([ev_v, ev_g], torch.bfloat16)
+    assert pitch == d and wst.shape == (2 * d, r) and bst.shape == (2 * d,)
+    ev = torch.nn.functional.linear(z, wst, bst)
+    for out_dtype in (torch.float32, torch.bfloat16):
+        got = native.evidence_norm(x, ev[..., :d], ev[..., d:], w, mask, 1e-5, out_dtype=out_dtype)
+        ref = native.evidence_norm(x, ev[..., :d].contiguous(), ev[..., d:].contiguous(), w, mask, 1e-5,
+                                   out_dtype=out_dtype)
+        assert torch.equal(got, ref)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        sv, sg = ev_v(z), ev_g(z)
+    torch.testing.assert_close(ev[..., :d].float(), sv.float(), atol=1e-2, rtol=2 ** -7)
+    torch.testing.assert_close(ev[..., d:].float(), sg.float(), atol=1e-2, rtol=2 ** -7)

@@ -91,10 +91,126 @@ __global__ void __launch_bounds__(kThreads) interpolate_kernel(const bf16* __res
   }
 }
 
+// ---------------------------------------------------------------------------
+// Attention over the pooled rows of one block (model.py:127-133 `GlobalAttention`
+// after the qkv projection; kernels/primitives.py:116-150 rotary; attention.py:8-18
+// FP32 masked attention): per batch entry b and head h,
+//   q, k = rotary(qkv[b, :, 0|1, h]) rounded to BF16 (as rotary_qkv_kernel),
+//   y[b, i, 64 h + d] = sum_{j < low_len[b]} softmax_j(q_i . k_j / 8) v[b, j, h, d],
+// FP32 throughout, rounded once to BF16 in the [B, LT, H*64] row layout the out
+// projection reads. One CTA per (64-row query tile, head, batch): warp w owns query
+// rows 8w..8w+7 of the tile; keys come in tiles of 32 (lane l scores key l) with an
+// online softmax; keys past the length are never loaded (their weight is exactly 0).
+// ---------------------------------------------------------------------------
+constexpr int kAttnD = 64;
+constexpr int kAttnRows = 64;  // query rows per CTA
+constexpr int kAttnKeys = 32;  // keys per tile
+
+__global__ void __launch_bounds__(256) pooled_attention_kernel(const bf16* __restrict__ x,
+                                                               const float* __restrict__ cosv,
+                                                               const float* __restrict__ sinv,
+                                                               const int64_t* __restrict__ lengths,
+                                                               bf16* __restrict__ y, int LT, int H) {
+  __shared__ float qs[kAttnRows][kAttnD];
+  __shared__ float ks[kAttnKeys][kAttnD + 1];
+  __shared__ float vs[kAttnKeys][kAttnD];
+  const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int half = kAttnD / 2;
+  int64_t len = lengths[b];
+  if (len > LT) len = LT;
+  if (len < 0) len = 0;
+  const int64_t row_stride = 3ll * H * kAttnD;
+  const bf16* xb = x + static_cast<int64_t>(b) * LT * row_stride;
+  auto rotated = [&](int t, int which, int pr) -> float2 {
+    const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(
+        xb + t * row_stride + (static_cast<int64_t>(which) * H + h) * kAttnD + 2 * pr));
+    const float cs = cosv[static_cast<int64_t>(t) * half + pr], sn = sinv[static_cast<int64_t>(t) * half + pr];
+    return make_float2(bf16_round(__fsub_rn(__fmul_rn(v.x, cs), __fmul_rn(v.y, sn))),
+                       bf16_round(__fadd_rn(__fmul_rn(v.x, sn), __fmul_rn(v.y, cs))));
+  };
+  for (int e = tid; e < kAttnRows * half; e += 256) {
+    const int r = e / half, pr = e % half;
+    const int t = tile * kAttnRows + r;
+    const float2 q = t < LT ? rotated(t, 0, pr) : make_float2(0.f, 0.f);
+    qs[r][2 * pr] = q.x;
+    qs[r][2 * pr + 1] = q.y;
+  }
+  float m[8], l[8], o0[8], o1[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) { m[r] = -INFINITY; l[r] = 0.f; o0[r] = 0.f; o1[r] = 0.f; }
+  for (int k0 = 0; k0 < len; k0 += kAttnKeys) {
+    __syncthreads();  // previous tile consumed (and, the first time, the q tile written)
+    for (int e = tid; e < kAttnKeys * half; e += 256) {
+      const int j = e / half, pr = e % half;
+      const int t = k0 + j;
+      const float2 k = t < len ? rotated(t, 1, pr) : make_float2(0.f, 0.f);
+      ks[j][2 * pr] = k.x;
+      ks[j][2 * pr + 1] = k.y;
+      float2 v = make_float2(0.f, 0.f);
+      if (t < len)
+        v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xb + t * row_stride + (2ll * H + h) * kAttnD + 2 * pr));
+      vs[j][2 * pr] = v.x;
+      vs[j][2 * pr + 1] = v.y;
+    }
+    __syncthreads();
+    const bool valid = k0 + lane < len;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int qr = warp * 8 + r;
+      float s = 0.f;
+#pragma unroll 16
+      for (int d = 0; d < kAttnD; ++d) s = fmaf(qs[qr][d], ks[lane][d], s);
+      s = valid ? s * 0.125f : -INFINITY;
+      float mt = s;
+#pragma unroll
+      for (int w = 16; w > 0; w >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, w));
+      const float mn = fmaxf(m[r], mt);  // finite: this tile holds at least one valid key
+      const float scale = m[r] == -INFINITY ? 0.f : expf(m[r] - mn);
+      const float p = valid ? expf(s - mn) : 0.f;
+      l[r] = l[r] * scale + warp_sum(p);
+      float a0 = o0[r] * scale, a1 = o1[r] * scale;
+#pragma unroll 8
+      for (int j = 0; j < kAttnKeys; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        a0 = fmaf(pj, vs[j][lane], a0);
+        a1 = fmaf(pj, vs[j][lane + 32], a1);
+      }
+      o0[r] = a0;
+      o1[r] = a1;
+      m[r] = mn;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int t = tile * kAttnRows + warp * 8 + r;
+    if (t >= LT) break;
+    // No valid key (length 0): NaN, as the reference's softmax over an all-masked row.
+    const float inv = l[r] > 0.f ? 1.f / l[r] : __int_as_float(0x7fc00000);
+    bf16* yr = y + (static_cast<int64_t>(b) * LT + t) * H * kAttnD + h * kAttnD;
+    yr[lane] = __float2bfloat16_rn(o0[r] * inv);
+    yr[lane + 32] = __float2bfloat16_rn(o1[r] * inv);
+  }
+}
+
 }  // namespace
 }  // namespace tf
 
 extern "C" {
+
+int tf_pooled_attention_fwd(const void* x, const float* cosv, const float* sinv, const int64_t* lengths, void* y,
+                            int batch, int low_time, int heads, int head_dim, void* stream) {
+  if (batch < 0 || low_time < 0 || heads < 0 || head_dim != tf::kAttnD) return TF_ERR_ARG;
+  if (batch == 0 || low_time == 0 || heads == 0) return TF_OK;
+  if (!x || !cosv || !sinv || !lengths || !y) return TF_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) % 4) return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const dim3 grid((low_time + tf::kAttnRows - 1) / tf::kAttnRows, heads, batch);
+  tf::pooled_attention_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const tf::bf16*>(x), cosv, sinv, lengths, static_cast<tf::bf16*>(y), low_time, heads);
+  return tf::launch_status();
+}
 
 int tf_rotary_qkv_fwd(const void* x, const float* cosv, const float* sinv, float* y, int batch,
                       int time, int heads, int head_dim, void* stream) {

@@ -73,6 +73,8 @@ bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) 
 // Output rows start every `yp` elements (0: every `width`), so a norm can write its
 // slice of a concatenated row in place; `y2` (optional, BF16, rows every `y2p`)
 // receives the same values rounded once, the copy autocast would make for a projection.
+// The second and third inputs (a, b) may have their own row pitch `ap` (0: `width`),
+// e.g. the two halves of one stacked projection row.
 // ---------------------------------------------------------------------------
 template <int kMode, typename TX, typename TA, typename TY, bool kVec4>
 __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict__ x,
@@ -83,32 +85,32 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
                                                             TY* __restrict__ y, int64_t rows,
                                                             int width, float eps, float* __restrict__ xo = nullptr,
                                                             int64_t yp = 0, bf16* __restrict__ y2 = nullptr,
-                                                            int64_t y2p = 0) {
+                                                            int64_t y2p = 0, int64_t ap = 0) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
-  auto value = [&](int64_t off) -> float {
+  auto value = [&](int64_t off, int64_t aoff) -> float {
     float v = load_f(x + off);
-    if (kMode == 1) v = v + load_f(a + off) * (2.f * sigmoid_ieee(load_f(b + off)));
-    if (kMode == 2) v = (v + load_f(a + off)) * 0.5f;
-    if (kMode == 4) v = v + load_f(a + off);
+    if (kMode == 1) v = v + load_f(a + aoff) * (2.f * sigmoid_ieee(load_f(b + aoff)));
+    if (kMode == 2) v = (v + load_f(a + aoff)) * 0.5f;
+    if (kMode == 4) v = v + load_f(a + aoff);
     return v;
   };
-  auto value4 = [&](int64_t off) -> float4 {
+  auto value4 = [&](int64_t off, int64_t aoff) -> float4 {
     float4 v = load4(x + off);
     if (kMode == 1) {
-      const float4 av = load4(a + off), bv = load4(b + off);
+      const float4 av = load4(a + aoff), bv = load4(b + aoff);
       v.x += av.x * (2.f * sigmoid_ieee(bv.x));
       v.y += av.y * (2.f * sigmoid_ieee(bv.y));
       v.z += av.z * (2.f * sigmoid_ieee(bv.z));
       v.w += av.w * (2.f * sigmoid_ieee(bv.w));
     }
     if (kMode == 2) {
-      const float4 av = load4(a + off);
+      const float4 av = load4(a + aoff);
       v = make_float4((v.x + av.x) * 0.5f, (v.y + av.y) * 0.5f, (v.z + av.z) * 0.5f,
                       (v.w + av.w) * 0.5f);
     }
     if (kMode == 4) {
-      const float4 av = load4(a + off);
+      const float4 av = load4(a + aoff);
       v = make_float4(v.x + av.x, v.y + av.y, v.z + av.z, v.w + av.w);
     }
     return v;
@@ -116,17 +118,18 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
   for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
     const int64_t base = row * width;
     const int64_t ybase = row * (yp ? yp : width);
+    const int64_t abase = row * (ap ? ap : width);
     const bool live = kMode != 1 || mask[row] != 0;
     float ss = 0.f;
     if (live) {
       if (kVec4) {
         for (int c = lane * 4; c < width; c += 128) {
-          const float4 v = value4(base + c);
+          const float4 v = value4(base + c, abase + c);
           ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
       } else {
         for (int c = lane; c < width; c += 32) {
-          const float v = value(base + c);
+          const float v = value(base + c, abase + c);
           ss += v * v;
         }
       }
@@ -140,7 +143,7 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
     };
     if (kVec4) {
       for (int c = lane * 4; c < width; c += 128) {
-        float4 v = live ? value4(base + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 v = live ? value4(base + c, abase + c) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (kMode == 4) store4(xo + base + c, v);
         const float4 wv = load4(w + c);
         v = make_float4(v.x * r * wv.x, v.y * r * wv.y, v.z * r * wv.z, v.w * r * wv.w);
@@ -151,7 +154,7 @@ __global__ void __launch_bounds__(kThreads) row_norm_kernel(const TX* __restrict
       }
     } else {
       for (int c = lane; c < width; c += 32) {
-        const float v = live ? value(base + c) : 0.f;
+        const float v = live ? value(base + c, abase + c) : 0.f;
         if (kMode == 4) xo[base + c] = v;
         const float t = v * r * w[c];
         store_f(y + ybase + c, kMode == 3 ? silu_of_rounded(t) : t);
@@ -165,10 +168,10 @@ template <int kMode, typename TX, typename TA, typename TY>
 int launch_row_norm(const void* x, const void* a, const void* b, const float* w,
                     const uint8_t* mask, void* y, int64_t rows, int width, float eps,
                     cudaStream_t s, float* xo = nullptr, int64_t yp = 0, bf16* y2 = nullptr,
-                    int64_t y2p = 0) {
+                    int64_t y2p = 0, int64_t ap = 0) {
   const bool v4 = width % 4 == 0 && aligned(x, 4 * sizeof(TX)) && aligned(y, 4 * sizeof(TY)) &&
                   aligned(w, 16) && (kMode == 0 || aligned(a, 4 * sizeof(TA))) &&
-                  (kMode != 1 || aligned(b, 4 * sizeof(TA))) && yp % 4 == 0 &&
+                  (kMode != 1 || aligned(b, 4 * sizeof(TA))) && yp % 4 == 0 && ap % 4 == 0 &&
                   (!y2 || (aligned(y2, 8) && y2p % 4 == 0));
   const int grid = grid_for(rows, kThreads / 32);
   auto X = static_cast<const TX*>(x);
@@ -177,10 +180,10 @@ int launch_row_norm(const void* x, const void* a, const void* b, const float* w,
   auto Y = static_cast<TY*>(y);
   if (v4)
     row_norm_kernel<kMode, TX, TA, TY, true><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo,
-                                                                      yp, y2, y2p);
+                                                                      yp, y2, y2p, ap);
   else
     row_norm_kernel<kMode, TX, TA, TY, false><<<grid, kThreads, 0, s>>>(X, A, B, w, mask, Y, rows, width, eps, xo,
-                                                                       yp, y2, y2p);
+                                                                       yp, y2, y2p, ap);
   return launch_status();
 }
 
@@ -789,6 +792,30 @@ int tf_evidence_norm_out_fwd(const void* x, int x_dtype, const void* value, cons
   if (vg_dtype == TF_F32)
     return tf::launch_row_norm<1, bf16, float, bf16>(x, value, gate, w, mask, y, rows, width, eps, s);
   return tf::launch_row_norm<1, bf16, bf16, bf16>(x, value, gate, w, mask, y, rows, width, eps, s);
+}
+
+int tf_evidence_norm_pitched_fwd(const void* x, int x_dtype, const void* value, const void* gate, int vg_dtype,
+                                 int64_t vg_pitch, const float* w, const uint8_t* mask, void* y, int y_dtype,
+                                 int64_t rows, int width, float eps, void* stream) {
+  if (rows < 0 || width <= 0 || !valid_dtype(x_dtype) || !valid_dtype(vg_dtype) || !valid_dtype(y_dtype))
+    return TF_ERR_ARG;
+  if (vg_pitch < width) return TF_ERR_ARG;
+  if (rows == 0) return TF_OK;
+  if (!x || !value || !gate || !w || !mask || !y) return TF_ERR_ARG;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using tf::bf16;
+  const int64_t p = vg_pitch;
+#define TF_EVIDENCE(TX, TA, TY) \
+  tf::launch_row_norm<1, TX, TA, TY>(x, value, gate, w, mask, y, rows, width, eps, s, nullptr, 0, nullptr, 0, p)
+  if (y_dtype == TF_F32) {
+    if (x_dtype == TF_F32) return vg_dtype == TF_F32 ? TF_EVIDENCE(float, float, float) : TF_EVIDENCE(float, bf16, float);
+    return vg_dtype == TF_F32 ? TF_EVIDENCE(bf16, float, float) : TF_EVIDENCE(bf16, bf16, float);
+  }
+  if (x_dtype == TF_F32) return vg_dtype == TF_F32 ? TF_EVIDENCE(float, float, bf16) : TF_EVIDENCE(float, bf16, bf16);
+  return vg_dtype == TF_F32 ? TF_EVIDENCE(bf16, float, bf16) : TF_EVIDENCE(bf16, bf16, bf16);
+#undef TF_EVIDENCE
 }
 
 int tf_evidence_norm_fwd(const void* x, int x_dtype, const void* value, const void* gate,

@@ -48,6 +48,8 @@ SIGNATURES = {
     "tf_gated_concat_fwd": [_p, _i, _p, _i, _p, _q, _i, _p],
     "tf_gated_branches_fwd": [_p, _p, _p, _i, _p, _p, _i, _p, _q, _i, _p],
     "tf_gate_branches_fwd": [_p, _q, _p, _q, _p, _p, _p, _p, _q, _i, _p],
+    "tf_pooled_attention_fwd": [_p, _p, _p, _p, _p, _i, _i, _i, _i, _p],
+    "tf_evidence_norm_pitched_fwd": [_p, _i, _p, _p, _i, _q, _p, _p, _p, _i, _q, _i, _f, _p],
     "tf_query_read_state_floats": [_i, _i],
     "tf_query_read_fwd": [_p, _p, _q, _p, _i, _p, _q, _p, _i, _i, _p],
     "tf_rms_pitched_fwd": [_p, _i, _p, _p, _i, _q, _p, _q, _q, _i, _f, _p],

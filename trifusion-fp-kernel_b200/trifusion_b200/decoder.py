@@ -20,6 +20,19 @@ def sin_position(time, dim, device):
     return torch.stack((angle.sin(), angle.cos()), -1).flatten(-2)
 
 
+_POSITIONS = {}
+
+
+def _position_table(time, dim, device, dtype):
+    """``sin_position(time, dim)`` in ``dtype``, computed once per (time, device, dtype):
+    a constant table, so steady-state forwards launch nothing for it."""
+    key = (time, dim, str(device), dtype)
+    table = _POSITIONS.get(key)
+    if table is None:
+        table = _POSITIONS[key] = sin_position(time, dim, device).to(dtype)
+    return table
+
+
 class QueryRead(nn.Module):
     """10 learned queries × 8 heads of width 32 attend over a sequence; the
     outputs are averaged in groups of 4/4/2 (``decoder.py:18-33``)."""
@@ -79,8 +92,14 @@ class Decoder(nn.Module):
         fine_mask = time_mask(fine_lengths, tf_)
         native = self.native_kernels and x.is_cuda
         deep_q = self.deep_read(self.query, x, grids.mask, grids.lengths if native else None)
-        fp = (fine + sin_position(tf_, 64, fine.device)[None, :, None, :].to(fine.dtype)
-              + self.band.to(fine.dtype)[None, None, :, :])
+        if native:
+            from .kernels.buffers import _param_bf16
+
+            band = _param_bf16(self.band, (8, 64)) if fine.dtype == torch.bfloat16 else self.band.to(fine.dtype)
+            fp = fine + _position_table(tf_, 64, fine.device, fine.dtype)[None, :, None, :] + band[None, None]
+        else:
+            fp = (fine + sin_position(tf_, 64, fine.device)[None, :, None, :].to(fine.dtype)
+                  + self.band.to(fine.dtype)[None, None, :, :])
         if native:  # key t * 8 + band is valid when t < fine_lengths
             fine_q = self.fine_read(self.query, fp.flatten(1, 2), None, fine_lengths, keys_per_length=8)
         else:

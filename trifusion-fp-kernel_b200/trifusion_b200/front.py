@@ -44,6 +44,16 @@ class CNNStage(nn.Module):
                 and x.dtype == torch.float32 and torch.is_autocast_enabled("cuda")
                 and torch.get_autocast_dtype("cuda") == torch.bfloat16)
 
+    def _skip_rows(self, x):
+        """The strided 1x1 skip convolution of channels-last ``x`` as one GEMM over the
+        subsampled positions: ``skip(x)[b, :, t, f] = W x[b, :, s t, 2 f]``, returned
+        channels-last. (For these shapes cuDNN's heuristics pick kernels several
+        times slower than the GEMM plus the gather of the subsampled rows.)"""
+        rows = x.permute(0, 2, 3, 1)[:, ::self.stride, ::2, :]  # [B, T', F', C], a strided view
+        b, tp, fp, c = rows.shape
+        w = self.skip.weight.reshape(self.skip.weight.shape[0], c)
+        return F.linear(rows.reshape(-1, c), w).view(b, tp, fp, -1).permute(0, 3, 1, 2)
+
     def forward(self, x, lengths):
         lengths = (lengths + self.stride - 1) // self.stride
         if self.backend != "reference" and x.is_cuda:
@@ -60,7 +70,10 @@ class CNNStage(nn.Module):
             x = x.contiguous(memory_format=torch.channels_last)
             h = front_norm(self.conv1(x), lengths, self.norm1, silu=True)
             h = front_norm(self.conv2(h), lengths, self.norm2)
-            return front_residual(h, self.skip(x), lengths)
+            # BF16 activations (the autocast path): the skip as a gather + GEMM. FP32 ones keep
+            # cuDNN's convolution, whose TF32 setting the GEMM would not share.
+            skip = self._skip_rows(x) if x.dtype == torch.bfloat16 else self.skip(x)
+            return front_residual(h, skip, lengths)
         h = self.conv1(x)
         valid = time_mask(lengths, h.shape[2])[:, None, :, None]
         # A zero row stays zero through the bias-free norm and SiLU, so masking

@@ -25,6 +25,37 @@ def _param_bf16(param, shape):
     return hit[1]
 
 
+_STACKED = {}
+
+
+def stacked_linear(layers, dtype, multiple=1):
+    """The weights (and biases) of Linear ``layers`` that share an input, stacked into one
+    ``[n * pitch, in]`` matrix (and ``[n * pitch]`` bias, or None) of ``dtype``: layer i's
+    rows start at ``i * pitch``, its width rounded up to ``multiple`` with zero rows, so
+    one GEMM computes all the layers and its output rows have aligned slices. Cached
+    until a parameter changes (version counter or storage). Returns (weight, bias, pitch)."""
+    params = [p for layer in layers for p in (layer.weight, layer.bias) if p is not None]
+    key = (tuple(id(p) for p in params), dtype, multiple)
+    stamp = tuple((p._version, p.data_ptr(), p.device) for p in params)
+    hit = _STACKED.get(key)
+    if hit is None or hit[0] != stamp:
+        width, dim = layers[0].weight.shape
+        if any(tuple(layer.weight.shape) != (width, dim) for layer in layers):
+            raise ValueError("stacked_linear: the layers must have one shape")
+        pitch = (width + multiple - 1) // multiple * multiple
+        dev = layers[0].weight.device
+        w = torch.zeros(len(layers) * pitch, dim, dtype=dtype, device=dev)
+        has_bias = layers[0].bias is not None
+        b = torch.zeros(len(layers) * pitch, dtype=dtype, device=dev) if has_bias else None
+        for i, layer in enumerate(layers):
+            w[i * pitch:i * pitch + width] = layer.weight.detach().to(dtype)
+            if has_bias:
+                b[i * pitch:i * pitch + width] = layer.bias.detach().to(dtype)
+        hit = (stamp, (w, b, pitch))
+        _STACKED[key] = hit
+    return hit[1]
+
+
 def _mask_bytes(mask):
     """The mask as one byte per row, without a conversion pass for bool masks."""
     m = mask.contiguous()

@@ -118,20 +118,28 @@ def rms_silu(x, weight, eps=1e-5):
 def evidence_norm(x, value, gate, weight, mask, eps=1e-5, out_dtype=torch.float32):
     """RMSNorm of ``x + value * 2 sigmoid(gate)`` on rows where ``mask`` is set
     (zero rows elsewhere); FP32 output (reference ``native.py:73-74``), or BF16 (the
-    FP32 result rounded once) with ``out_dtype``."""
-    x, value, gate = x.contiguous(), value.contiguous(), gate.contiguous()
+    FP32 result rounded once) with ``out_dtype``. ``value`` and ``gate`` may be views
+    whose rows share one pitch (the halves of a stacked projection row): they are
+    read in place."""
+    x = x.contiguous()
     if value.dtype != gate.dtype:
-        gate = gate.to(value.dtype)
+        value, gate = value, gate.to(value.dtype)
     dev = _lib.require_cuda("evidence_norm", x, value, gate, weight, mask)
     rows, d = _rows(x)
     if value.shape != x.shape or gate.shape != x.shape or mask.numel() != rows:
         raise ValueError("evidence_norm: value/gate must match x and mask must have one entry per row")
+    try:
+        pitch = _row_pitch(value, d, "evidence_norm")
+        if _row_pitch(gate, d, "evidence_norm") != pitch:
+            raise ValueError("evidence_norm: value and gate rows differ in pitch")
+    except ValueError:
+        value, gate, pitch = value.contiguous(), gate.contiguous(), d
     w = _weight(weight, d, "evidence_norm")
     m = mask.contiguous()
     m = m.view(torch.uint8) if m.dtype == torch.bool else m.to(torch.uint8)
     y = torch.empty(x.shape, device=dev, dtype=out_dtype)
-    _lib.launch("tf_evidence_norm_out_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "evidence_norm"),
-                value.data_ptr(), gate.data_ptr(), _lib.dtype_code(value, "evidence_norm"),
+    _lib.launch("tf_evidence_norm_pitched_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "evidence_norm"),
+                value.data_ptr(), gate.data_ptr(), _lib.dtype_code(value, "evidence_norm"), pitch,
                 w.data_ptr(), m.data_ptr(), y.data_ptr(), _lib.dtype_code(y, "evidence_norm"), rows, d,
                 float(eps))
     return y
@@ -172,6 +180,27 @@ def masked_mean(x, lengths):
     y = torch.empty((b, d), device=dev, dtype=torch.float32)
     _lib.launch("tf_masked_mean_fwd", dev, x.data_ptr(), _lib.dtype_code(x, "masked_mean"),
                 lengths.data_ptr(), y.data_ptr(), b, t, d)
+    return y
+
+
+def pooled_attention(qkv, cos, sin, lengths, heads):
+    """A block's attention over its pooled rows (reference ``model.py:127-133`` after
+    the qkv projection): ``qkv`` BF16 ``[B, LT, 3 * heads * 64]``, q/k rotated by the
+    ``[>= LT, 32]`` cos/sin table and rounded to BF16, FP32 masked softmax attention
+    with key j valid when ``j < lengths[b]``. Returns the BF16 ``[B, LT, heads * 64]``
+    rows the out projection reads."""
+    dev = _lib.require_cuda("pooled_attention", qkv, cos, sin, lengths)
+    b, t, width = qkv.shape
+    if qkv.dtype != torch.bfloat16 or width != 3 * heads * 64:
+        raise ValueError("pooled_attention: qkv must be BF16 [B, LT, 3 * heads * 64]")
+    if cos.shape[0] < t or cos.shape[-1] != 32 or sin.shape != cos.shape:
+        raise ValueError("pooled_attention: the rotary table must be [>= LT, 32]")
+    qkv = qkv.contiguous()
+    cos, sin = cos.float().contiguous(), sin.float().contiguous()
+    lengths = lengths.to(torch.int64).contiguous()
+    y = torch.empty((b, t, heads * 64), device=dev, dtype=torch.bfloat16)
+    _lib.launch("tf_pooled_attention_fwd", dev, qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), lengths.data_ptr(),
+                y.data_ptr(), b, t, heads, 64)
     return y
 
 

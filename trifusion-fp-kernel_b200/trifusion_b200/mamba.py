@@ -21,38 +21,18 @@ from torch import nn
 from .kernels import RMSNorm
 
 
-_STACKED = {}
-
-
-def _stacked_in_proj(mods, dtype):
-    """The ``in_proj`` weights of ``mods`` as one ``[len(mods) * pitch, dim]`` matrix of
-    ``dtype``, each ``[width, dim]`` weight followed by zero rows up to ``pitch`` (width
-    rounded up to a multiple of 8), so every projection row starts on a 16-byte
-    boundary. Cached until a weight changes (version counter or storage)."""
-    ws = [m.in_proj.weight for m in mods]
-    key = (tuple(id(w) for w in ws), dtype)
-    stamp = tuple((w._version, w.data_ptr(), w.device) for w in ws)
-    hit = _STACKED.get(key)
-    if hit is None or hit[0] != stamp:
-        width, dim = ws[0].shape
-        pitch = (width + 7) // 8 * 8
-        stacked = torch.zeros(len(ws) * pitch, dim, dtype=dtype, device=ws[0].device)
-        for i, w in enumerate(ws):
-            stacked[i * pitch:i * pitch + width] = w.detach().to(dtype)
-        hit = (stamp, stacked, pitch)
-        _STACKED[key] = hit
-    return hit[1], hit[2]
-
-
 def projections(mods, u):
-    """``[m.in_proj(u) for m in mods]`` as ONE GEMM over the stacked, padded weights:
-    views of a ``[..., len(mods) * pitch]`` output whose rows are 16-byte aligned
+    """``[m.in_proj(u) for m in mods]`` as ONE GEMM over the stacked weights, each padded
+    with zero rows to a multiple of 8: views of a ``[..., len(mods) * pitch]`` output whose
+    rows are 16-byte aligned
     (the in_proj width, 1860 at dim 384, is not a multiple of 8; cuBLAS then falls
     back to kernels without TMA). The operands are what ``in_proj`` would use: under
     autocast the weights in the autocast type, otherwise in their own type."""
+    from .kernels.buffers import stacked_linear
+
     dev = u.device.type
     dtype = torch.get_autocast_dtype(dev) if torch.is_autocast_enabled(dev) else mods[0].in_proj.weight.dtype
-    w, pitch = _stacked_in_proj(mods, dtype)
+    w, _, pitch = stacked_linear([m.in_proj for m in mods], dtype, multiple=8)
     width = mods[0].in_proj.weight.shape[0]
     p = F.linear(u, w)
     return [p[..., i * pitch:i * pitch + width] for i in range(len(mods))]

@@ -150,6 +150,13 @@ class GlobalAttention(nn.Module):
         b, t = p.shape[:2]
         qkv = self.qkv(p)
         mask = grids.low_mask[:, None, None, :]
+        if (self.backend != "reference" and self.buffer_fusion and qkv.is_cuda and qkv.dtype == torch.bfloat16
+                and self.head_dim == 64):
+            # One kernel: rotary q/k, FP32 masked attention, rows in the out projection's layout.
+            from .kernels.native import pooled_attention
+
+            y = pooled_attention(qkv, grids.rope_cos, grids.rope_sin, grids.low_lengths, self.heads)
+            return grids.interpolate(self.out(y))
         if self.backend != "reference" and self.buffer_fusion and qkv.is_cuda and qkv.dtype == torch.bfloat16:
             # One kernel: rotary q/k and the FP32 attention operands.
             from .kernels.buffers import RotaryQKV
@@ -234,8 +241,17 @@ class TriFusionBlock(nn.Module):
 
             # u feeds only the Mamba in_proj GEMMs: under BF16 autocast it is written in BF16
             # (the FP32 result rounded once, as autocast would) instead of being cast twice.
-            u = native.evidence_norm(x, self.e_value(z), self.e_gate(z), self.u_norm.weight, mask,
-                                     self.u_norm.eps,
+            if _bf16_autocast(x):
+                from .kernels.buffers import stacked_linear
+
+                # e_value and e_gate share z: one GEMM over both weights; the norm reads the
+                # two halves of its output rows in place.
+                w_ev, b_ev, _ = stacked_linear([self.e_value, self.e_gate], torch.bfloat16)
+                ev = F.linear(z, w_ev, b_ev)
+                value, gate = ev[..., :d], ev[..., d:]
+            else:
+                value, gate = self.e_value(z), self.e_gate(z)
+            u = native.evidence_norm(x, value, gate, self.u_norm.weight, mask, self.u_norm.eps,
                                      out_dtype=torch.bfloat16 if _bf16_autocast(x) else torch.float32)
             # Both directions in one launch; the recurrence zeroes rows past each length
             # itself (out_proj has no bias) and runs the backward direction reversed.

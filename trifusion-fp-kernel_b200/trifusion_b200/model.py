@@ -216,8 +216,17 @@ class TriFusionBlock(nn.Module):
 
         if opt and not input_masked:
             x = _mask_rows(x, mask, True)
-        h = keep_zero(self.pre(x))
-        local, attended = self.local(h, mask, lengths), self.attention(h, grids)
+        if opt and x.is_cuda and _bf16_autocast(x) and x.dtype == torch.float32 and x.shape[-1] % 4 == 0:
+            from .kernels import native
+
+            # The pre-norm writes the FP32 rows (pooled by the attention branch) and their
+            # BF16 copy (the local branch's up projection input, autocast's cast) in one pass.
+            h, h16 = torch.empty_like(x), torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+            native.rms_into(x, self.pre.weight, self.pre.eps, h, h16)
+            local, attended = self.local(h16, mask, lengths), self.attention(h, grids)
+        else:
+            h = keep_zero(self.pre(x))
+            local, attended = self.local(h, mask, lengths), self.attention(h, grids)
         d = local.shape[-1]
         # BF16 branch outputs on the GPU: the cn/an norms write their parts of e_down's
         # input row and of the gate's BF16 input row in place of the two concatenations

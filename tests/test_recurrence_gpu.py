@@ -193,3 +193,36 @@ def test_agrees_with_reference_bf16_arithmetic(batch, time, heads):
     rel = (out - ref).norm() / ref.norm()
     assert rel < 0.006, float(rel)
     torch.testing.assert_close(out, ref, atol=0.04, rtol=0.02)
+
+
+def test_captured_graph_survives_workspace_growth():
+    """A CUDA graph captured with the cached recurrence workspace still replays correctly
+    after a larger call has outgrown that workspace and the allocator has released its
+    cache: the outgrown buffer stays allocated (an engine serving many batch shapes
+    captures its graphs in increasing size)."""
+    from trifusion_b200 import _lib
+
+    small = recurrence_inputs(2, 130, 4, kind="reftest", device=DEV)
+    ref = fused_mamba(*small)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fused_mamba(*small)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y = fused_mamba(*small)
+    before = _lib._workspaces[torch.cuda.current_device()]
+    lib = _lib.lib()
+    t = 4096
+    while lib.tf_recurrence_workspace_size(4, t, 12) <= before.numel():
+        t *= 2
+    big = recurrence_inputs(4, t, 12, kind="baseline", device=DEV)
+    fused_mamba(*big)
+    assert _lib._workspaces[torch.cuda.current_device()].data_ptr() != before.data_ptr()
+    del before, big
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)

@@ -528,4 +528,3 @@ def test_evidence_norm_reads_stacked_halves_in_place():
         sv, sg = ev_v(z), ev_g(z)
     torch.testing.assert_close(ev[..., :d].float(), sv.float(), atol=1e-2, rtol=2 ** -7)
     torch.testing.assert_close(ev[..., d:].float(), sg.float(), atol=1e-2, rtol=2 ** -7)
-

@@ -156,6 +156,9 @@ def launch(fn, device, *args):
 
 
 _workspaces = {}
+# Outgrown workspaces are kept, never freed: a CUDA graph captured while one of them was
+# current has its address baked into its recurrence launches.
+_retired_workspaces = []
 
 
 def workspace(device, nbytes):
@@ -165,12 +168,17 @@ def workspace(device, nbytes):
     zeroed only when (re)allocated. Launches sharing it must not overlap in
     time, which holds for calls issued from one stream, or serialised across
     streams, as the reference requires of its callers (docs/api.md:47-48).
+    When a call needs more, a new buffer of at least twice the size replaces it
+    for later calls, and the old one stays allocated for the graphs that use it.
     """
     import torch
 
     idx = device.index if device.index is not None else torch.cuda.current_device()
     buf = _workspaces.get(idx)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        size = max(nbytes, 1 << 20, 2 * buf.numel() if buf is not None else 0)
+        if buf is not None:
+            _retired_workspaces.append(buf)
+        buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
         _workspaces[idx] = buf
     return buf

@@ -10,6 +10,9 @@ from .. import _lib
 
 
 _BF16_PARAMS = {}
+# Superseded cached copies stay allocated: a CUDA graph captured before the parameter
+# changed still reads them (it must be recaptured to see the new values).
+_RETIRED = []
 
 
 def _param_bf16(param, shape):
@@ -20,6 +23,8 @@ def _param_bf16(param, shape):
     stamp = (param._version, param.data_ptr(), param.device)
     hit = _BF16_PARAMS.get(key)
     if hit is None or hit[0] != stamp:
+        if hit is not None:
+            _RETIRED.append(hit[1])
         hit = (stamp, param.detach().to(torch.bfloat16).reshape(shape).contiguous())
         _BF16_PARAMS[key] = hit
     return hit[1]
@@ -39,6 +44,8 @@ def stacked_linear(layers, dtype, multiple=1):
     stamp = tuple((p._version, p.data_ptr(), p.device) for p in params)
     hit = _STACKED.get(key)
     if hit is None or hit[0] != stamp:
+        if hit is not None:
+            _RETIRED.append(hit[1])
         width, dim = layers[0].weight.shape
         if any(tuple(layer.weight.shape) != (width, dim) for layer in layers):
             raise ValueError("stacked_linear: the layers must have one shape")

@@ -48,7 +48,9 @@ WORKLOADS = {
     # whole student forward through InferenceEngine(graphs=True)
     "cfg3": dict(kind="model", batch=16, samples=64000, lengths=("uniform", 32000, 64000)),
     # box-level sweep: 1024 clips, length buckets, LPT partition over the GPUs
-    "cfg4": dict(kind="box", clips=1024, max_batch=32, padded_seconds=120),
+    # Up to 32 clips per batch and 480 padded audio-seconds per batch: a B200-sized budget
+    # (the reference's planner takes it as a setting; its L4 default is 64 s on 24 GB).
+    "cfg4": dict(kind="box", clips=1024, max_batch=32, padded_seconds=480),
 }
 AUDIO_METRIC_UNIT = "audio-sec/s"
 # Default timed steps: each bounded to well under a minute of GPU time.
@@ -680,7 +682,7 @@ def run_box(args, wl):
         "config": {"workload": args.workload, "student": STUDENT, "clips": len(records),
                    "audio_seconds": total_audio_s, "batches": len(plan),
                    "batches_on_rank0": len(mine), "graph_shapes_on_rank0": len(shapes),
-                   "max_batch": wl["max_batch"],
+                   "max_batch": wl["max_batch"], "padded_seconds_per_batch": wl["padded_seconds"],
                    "step": "all batches through InferenceEngine(graphs=True) + one logits all-gather",
                    "l2": "inputs larger than L2 (the sweep streams all batches)",
                    "parallelism": f"data-parallel x{world}, LPT partition by padded audio-seconds"},

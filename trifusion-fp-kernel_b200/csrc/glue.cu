@@ -99,8 +99,9 @@ __global__ void __launch_bounds__(kThreads) interpolate_kernel(const bf16* __res
 //   y[b, i, 64 h + d] = sum_{j < low_len[b]} softmax_j(q_i . k_j / 8) v[b, j, h, d],
 // FP32 throughout, rounded once to BF16 in the [B, LT, H*64] row layout the out
 // projection reads. One CTA per (64-row query tile, head, batch): warp w owns query
-// rows 8w..8w+7 of the tile; keys come in tiles of 32 (lane l scores key l) with an
-// online softmax; keys past the length are never loaded (their weight is exactly 0).
+// rows 8w..8w+7 of the tile and treats them together (lane l scores key l against all
+// 8); keys come in tiles of 32 with an online softmax; keys past the length are never
+// loaded (their weight is exactly 0).
 // ---------------------------------------------------------------------------
 constexpr int kAttnD = 64;
 constexpr int kAttnRows = 64;  // query rows per CTA
@@ -111,7 +112,7 @@ __global__ void __launch_bounds__(256) pooled_attention_kernel(const bf16* __res
                                                                const float* __restrict__ sinv,
                                                                const int64_t* __restrict__ lengths,
                                                                bf16* __restrict__ y, int LT, int H) {
-  __shared__ float qs[kAttnRows][kAttnD];
+  __shared__ __align__(16) float qs[kAttnRows][kAttnD];
   __shared__ float ks[kAttnKeys][kAttnD + 1];
   __shared__ float vs[kAttnKeys][kAttnD];
   const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -136,6 +137,10 @@ __global__ void __launch_bounds__(256) pooled_attention_kernel(const bf16* __res
     qs[r][2 * pr] = q.x;
     qs[r][2 * pr + 1] = q.y;
   }
+  // Warp w owns rows 8w..8w+7 of the tile; a warp whose rows all lie past LT only
+  // helps stage the key tiles.
+  const int row0 = warp * 8;
+  const bool active = tile * kAttnRows + row0 < LT;
   float m[8], l[8], o0[8], o1[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) { m[r] = -INFINITY; l[r] = 0.f; o0[r] = 0.f; o1[r] = 0.f; }
@@ -154,31 +159,64 @@ __global__ void __launch_bounds__(256) pooled_attention_kernel(const bf16* __res
       vs[j][2 * pr + 1] = v.y;
     }
     __syncthreads();
+    if (!active) continue;  // warp-uniform; the barriers above are still reached
     const bool valid = k0 + lane < len;
+    // Scores of key `lane` against the warp's 8 rows: 8 independent FMA chains, one
+    // read of the key's column per step (q rows are broadcast reads).
+    float s[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) s[r] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < kAttnD; d += 4) {
+      const float k0v = ks[lane][d], k1v = ks[lane][d + 1], k2v = ks[lane][d + 2], k3v = ks[lane][d + 3];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float4 q = *reinterpret_cast<const float4*>(&qs[row0 + r][d]);
+        s[r] = fmaf(q.x, k0v, s[r]);
+        s[r] = fmaf(q.y, k1v, s[r]);
+        s[r] = fmaf(q.z, k2v, s[r]);
+        s[r] = fmaf(q.w, k3v, s[r]);
+      }
+    }
+    float mt[8], p[8], ps[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-      const int qr = warp * 8 + r;
-      float s = 0.f;
-#pragma unroll 16
-      for (int d = 0; d < kAttnD; ++d) s = fmaf(qs[qr][d], ks[lane][d], s);
-      s = valid ? s * 0.125f : -INFINITY;
-      float mt = s;
+      s[r] = valid ? s[r] * 0.125f : -INFINITY;
+      mt[r] = s[r];
+    }
 #pragma unroll
-      for (int w = 16; w > 0; w >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, w));
-      const float mn = fmaxf(m[r], mt);  // finite: this tile holds at least one valid key
+    for (int w = 16; w > 0; w >>= 1) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], w));
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float mn = fmaxf(m[r], mt[r]);  // finite: this tile holds at least one valid key
       const float scale = m[r] == -INFINITY ? 0.f : expf(m[r] - mn);
-      const float p = valid ? expf(s - mn) : 0.f;
-      l[r] = l[r] * scale + warp_sum(p);
-      float a0 = o0[r] * scale, a1 = o1[r] * scale;
-#pragma unroll 8
-      for (int j = 0; j < kAttnKeys; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, p, j);
-        a0 = fmaf(pj, vs[j][lane], a0);
-        a1 = fmaf(pj, vs[j][lane + 32], a1);
-      }
-      o0[r] = a0;
-      o1[r] = a1;
+      p[r] = valid ? expf(s[r] - mn) : 0.f;
+      ps[r] = p[r];
       m[r] = mn;
+      l[r] *= scale;
+      o0[r] *= scale;
+      o1[r] *= scale;
+    }
+#pragma unroll
+    for (int w = 16; w > 0; w >>= 1) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) ps[r] += __shfl_xor_sync(0xffffffffu, ps[r], w);
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) l[r] += ps[r];
+    // Weighted values: each v row is read once for all 8 rows.
+#pragma unroll 4
+    for (int j = 0; j < kAttnKeys; ++j) {
+      const float v0 = vs[j][lane], v1 = vs[j][lane + 32];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float pj = __shfl_sync(0xffffffffu, p[r], j);
+        o0[r] = fmaf(pj, v0, o0[r]);
+        o1[r] = fmaf(pj, v1, o1[r]);
+      }
     }
   }
 #pragma unroll

@@ -622,6 +622,7 @@ __global__ void __launch_bounds__(kThreads) gate_branches_kernel(const bf16* __r
   for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
     const bf16* sr = s + row * sp;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll 3
     for (int c = lane * 4; c < width; c += 128) {
       const float4 v = load4(sr + c);
       const float4 w0 = load4(w + c), w1 = load4(w + width + c), w2 = load4(w + 2 * width + c);
@@ -641,6 +642,7 @@ __global__ void __launch_bounds__(kThreads) gate_branches_kernel(const bf16* __r
     const float s0 = 2.f * sigmoid_ieee(g0), s1 = 2.f * sigmoid_ieee(g1), s2 = 2.f * sigmoid_ieee(g2);
     float* yr = y + row * width;
     const float* xr = x1 + row * p1;
+#pragma unroll 3
     for (int c = lane * 4; c < width; c += 128) {
       const int j = c / d;  // d % 4 == 0: a 4-vector never straddles two branches
       const float4 v = j == 1 ? load4(xr + (c - d)) : load4(sr + c);

@@ -157,3 +157,38 @@ def test_reversed_direction_contiguous_inputs():
         flipped[name] = reverse_rows(args[name].transpose(1, 2), lengths).transpose(1, 2).contiguous()
     fwd = fused_recurrence_multi([dict(flipped, q_norm=prm["q_norm"], k_norm=prm["k_norm"])], lengths=lengths)[0]
     assert torch.equal(rev, reverse_rows(fwd, lengths))
+
+
+def test_pair_rows_side_by_side_and_paired_mean():
+    """Both directions written into one [B, T, 2 * 768] row buffer through the output
+    strides equal the separate outputs bit for bit, and the one-GEMM mean of the two
+    out projections is within BF16 rounding of the mean of the two projections."""
+    from types import SimpleNamespace
+
+    from trifusion_b200.mamba import Mamba3Inference, bidirectional_pair, bidirectional_rows, paired_mean
+
+    torch.manual_seed(11)
+    cfg = SimpleNamespace(dim=384, state_dim=128, backend="l4")
+    fwd, bwd = Mamba3Inference(cfg).cuda(), Mamba3Inference(cfg).cuda()
+    for m in (fwd, bwd):
+        m.fused_recurrence = True
+    u = (0.5 * torch.randn(3, 150, 384, device="cuda")).to(torch.bfloat16)
+    lengths = torch.tensor([150, 77, 9], device="cuda")
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        y = bidirectional_rows(fwd, bwd, u, lengths)
+        from trifusion_b200.mamba import projections
+        from trifusion_b200.mamba_fused import fused_recurrence_multi
+
+        pf, pb = projections([fwd, bwd], u)
+        yf, yb = fused_recurrence_multi([fwd._direction(pf, 3, 150), bwd._direction(pb, 3, 150, reverse=True)],
+                                        lengths=lengths, eps=fwd.C_norm.eps)
+        avg = paired_mean(fwd, bwd, y)
+        mf, mb = bidirectional_pair(fwd, bwd, u, lengths)
+    assert torch.equal(y[..., :768], yf.reshape(3, 150, 768))
+    assert torch.equal(y[..., 768:], yb.reshape(3, 150, 768))
+    ref = (mf.float() + mb.float()) * 0.5
+    torch.testing.assert_close(avg.float(), ref, atol=2e-2, rtol=2 ** -6)
+    with pytest.raises(ValueError):
+        d = fwd._direction(pf, 3, 150)
+        d["out"] = torch.empty(3, 150, 12, 32, dtype=torch.bfloat16, device="cuda")
+        fused_recurrence_multi([d], lengths=lengths)

@@ -38,6 +38,46 @@ def projections(mods, u):
     return [p[..., i * pitch:i * pitch + width] for i in range(len(mods))]
 
 
+_PAIRED = {}
+_RETIRED = []  # superseded weights stay allocated for graphs captured before the change
+
+
+def paired_mean(fwd, bwd, y):
+    """``(fwd.out_proj(y_f) + bwd.out_proj(y_b)) / 2`` for ``y = [y_f | y_b]`` (rows of
+    ``2 * d_inner``) as ONE GEMM over K = 2 * d_inner with the two weights side by side
+    and halved (exact in binary floating point): the mean is rounded once, in the
+    GEMM's output type, instead of each projection being rounded before the average."""
+    dev = y.device.type
+    dtype = torch.get_autocast_dtype(dev) if torch.is_autocast_enabled(dev) else fwd.out_proj.weight.dtype
+    wf, wb = fwd.out_proj.weight, bwd.out_proj.weight
+    key = (id(wf), id(wb), dtype)
+    stamp = tuple((w._version, w.data_ptr(), w.device) for w in (wf, wb))
+    hit = _PAIRED.get(key)
+    if hit is None or hit[0] != stamp:
+        if hit is not None:
+            _RETIRED.append(hit[1])
+        hit = (stamp, (0.5 * torch.cat((wf.detach().float(), wb.detach().float()), 1)).to(dtype))
+        _PAIRED[key] = hit
+    return F.linear(y, hit[1])
+
+
+def bidirectional_rows(fwd, bwd, u, lengths):
+    """Both directions of a block in one recurrence launch (as ``bidirectional_pair``),
+    written side by side into one BF16 ``[B, T, 2 * d_inner]`` row buffer, forward
+    half first (the launch takes output strides)."""
+    from .mamba_fused import fused_recurrence_multi
+
+    b, t, _ = u.shape
+    e = fwd.d_inner
+    pf, pb = projections([fwd, bwd], u) if u.is_cuda else (fwd.in_proj(u), bwd.in_proj(u))
+    y = torch.empty(b, t, 2 * e, dtype=torch.bfloat16, device=u.device)
+    df, db = fwd._direction(pf, b, t), bwd._direction(pb, b, t, reverse=True)
+    df["out"] = y[..., :e].view(b, t, fwd.nheads, fwd.headdim)
+    db["out"] = y[..., e:].view(b, t, bwd.nheads, bwd.headdim)
+    fused_recurrence_multi([df, db], lengths=lengths, eps=fwd.C_norm.eps)
+    return y
+
+
 class Mamba3Inference(nn.Module):
     def __init__(self, config):
         super().__init__()

@@ -172,6 +172,10 @@ def fused_recurrence_multi(directions, *, lengths=None, eps=1e-5):
         out = d_.get("out")
         if out is None:
             out = torch.empty_like(v, memory_format=torch.contiguous_format)
+        elif (tuple(out.shape) != tuple(v.shape) or out.dtype != torch.bfloat16 or out.device != v.device
+              or out.stride(-1) != 1):
+            raise ValueError("fused_recurrence_multi: out must be BF16 [B,T,H,64] on v's device with a "
+                             "contiguous last dimension")
         io = ios[i]
         io.q, io.k, io.v, io.z, io.angles = (x.data_ptr() for x in (q, k, v, z, angles))
         io.qb, io.kb, io.d = qb.data_ptr(), kb.data_ptr(), d.data_ptr()

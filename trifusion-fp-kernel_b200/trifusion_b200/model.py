@@ -205,9 +205,11 @@ class TriFusionBlock(nn.Module):
             for layer in (self.merge, self.down):
                 layer.weight.mul_(1 / math.sqrt(2 * c.depth))
 
-    def forward(self, x, grids, input_masked=False):
+    def forward(self, x, grids, input_masked=False, need_directions=True):
         """``input_masked``: the rows of ``x`` past each length are already zero (the
-        previous block's output on the optimized path), so the input mask is skipped."""
+        previous block's output on the optimized path), so the input mask is skipped.
+        ``need_directions=False``: the two Mamba directions' outputs are not returned
+        (None), so the optimized path may form only their mean."""
         mask, lengths = grids.mask, grids.lengths
         opt = self.backend != "reference"
 
@@ -265,15 +267,25 @@ class TriFusionBlock(nn.Module):
             # Both directions in one launch; the recurrence zeroes rows past each length
             # itself (out_proj has no bias) and runs the backward direction reversed.
             fwd, bwd = self.forward_mamba, self.backward_mamba
-            if fwd.fused_recurrence and bwd.fused_recurrence:
-                from .mamba import bidirectional_pair
+            if fwd.fused_recurrence and bwd.fused_recurrence and split and not need_directions:
+                from .mamba import bidirectional_rows, paired_mean
 
-                mf, mb = bidirectional_pair(fwd, bwd, u, lengths)
+                # Both directions' rows side by side, then ONE GEMM over both out_proj weights
+                # (halved) gives their mean, rounded once; the norm writes mn and its BF16 copy.
+                avg = paired_mean(fwd, bwd, bidirectional_rows(fwd, bwd, u, lengths))
+                mn = torch.empty(avg.shape, dtype=torch.float32, device=avg.device)
+                native.rms_into(avg, self.mn.weight, self.mn.eps, mn, s16[..., d:2 * d])
+                mf = mb = None
             else:
-                mf = fwd(u, lengths)
-                mb = reverse_valid(bwd(reverse_valid(u, lengths), lengths), lengths)
-            mn = native.mean_norm(mf, mb, self.mn.weight, self.mn.eps,
-                                  copy_to=s16[..., d:2 * d] if split else None)
+                if fwd.fused_recurrence and bwd.fused_recurrence:
+                    from .mamba import bidirectional_pair
+
+                    mf, mb = bidirectional_pair(fwd, bwd, u, lengths)
+                else:
+                    mf = fwd(u, lengths)
+                    mb = reverse_valid(bwd(reverse_valid(u, lengths), lengths), lengths)
+                mn = native.mean_norm(mf, mb, self.mn.weight, self.mn.eps,
+                                      copy_to=s16[..., d:2 * d] if split else None)
         else:
             evidence = self.e_value(z).float() * (2 * torch.sigmoid(self.e_gate(z).float()))
             u = _mask_rows(self.u_norm(x + evidence), mask, opt)
@@ -359,7 +371,9 @@ class TriFusion(nn.Module):
         mf = mb = None
         for i, block in enumerate(self.blocks):
             # Each optimized block's output is zero past the lengths: the next one needn't mask it.
-            x, mf, mb = block(x, grids, input_masked=optimized and i > 0)
+            # Only the last block's per-direction outputs reach the decoder.
+            x, mf, mb = block(x, grids, input_masked=optimized and i > 0,
+                              need_directions=i == len(self.blocks) - 1)
         return x, fine, grids, fine_lengths, mf, mb
 
     def forward(self, audio, lengths, channels):

@@ -85,3 +85,24 @@ def test_query_read_lengths_equal_the_expanded_mask_on_cpu():
         got = qr(query, x, None, lengths, keys_per_length=8)
     for r, g in zip(ref, got):
         assert torch.equal(r, g)
+
+
+def test_weight_caches_match_only_the_same_live_parameter():
+    """A cache entry hits only for the very parameter object it was made from: another
+    tensor with the same address and version counter (here a view, as a new model's
+    parameter can be after the old one is freed) is a miss, and so is a freed one."""
+    from trifusion_b200.kernels import buffers as B
+
+    p = torch.nn.Parameter(torch.randn(6, 4))
+    stamp = B._stamp((p,))
+    assert B._stamp_matches(stamp, (p,))
+    alias = p.view(6, 4)  # same storage, same version counter, another object
+    assert alias.data_ptr() == p.data_ptr() and alias._version == p._version
+    assert not B._stamp_matches(stamp, (alias,))
+    with torch.no_grad():
+        p.mul_(2.0)
+    assert not B._stamp_matches(stamp, (p,))  # version moved
+    q = torch.nn.Parameter(torch.randn(6, 4))
+    first = B._param_bf16(q, (6, 4))
+    assert B._param_bf16(q, (6, 4)) is first
+    torch.testing.assert_close(first.float(), q.detach(), atol=1e-2, rtol=1e-2)

@@ -4,6 +4,8 @@
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from .. import _lib
@@ -15,17 +17,29 @@ _BF16_PARAMS = {}
 _RETIRED = []
 
 
+def _stamp(params):
+    """Identity and state of ``params`` for a cache entry: weak references (a freed
+    parameter whose id and address are reused never matches) plus each version
+    counter and storage."""
+    return tuple((weakref.ref(p), p._version, p.data_ptr(), p.device) for p in params)
+
+
+def _stamp_matches(stamp, params):
+    return len(stamp) == len(params) and all(
+        ref() is p and (v, ptr, dev) == (p._version, p.data_ptr(), p.device)
+        for (ref, v, ptr, dev), p in zip(stamp, params))
+
+
 def _param_bf16(param, shape):
     """A contiguous BF16 copy of ``param`` reshaped to ``shape``, cached until the
     parameter changes (its version counter or storage), so steady-state calls launch
     no conversion kernel."""
     key = (id(param), shape)
-    stamp = (param._version, param.data_ptr(), param.device)
     hit = _BF16_PARAMS.get(key)
-    if hit is None or hit[0] != stamp:
+    if hit is None or not _stamp_matches(hit[0], (param,)):
         if hit is not None:
             _RETIRED.append(hit[1])
-        hit = (stamp, param.detach().to(torch.bfloat16).reshape(shape).contiguous())
+        hit = (_stamp((param,)), param.detach().to(torch.bfloat16).reshape(shape).contiguous())
         _BF16_PARAMS[key] = hit
     return hit[1]
 
@@ -41,9 +55,8 @@ def stacked_linear(layers, dtype, multiple=1):
     until a parameter changes (version counter or storage). Returns (weight, bias, pitch)."""
     params = [p for layer in layers for p in (layer.weight, layer.bias) if p is not None]
     key = (tuple(id(p) for p in params), dtype, multiple)
-    stamp = tuple((p._version, p.data_ptr(), p.device) for p in params)
     hit = _STACKED.get(key)
-    if hit is None or hit[0] != stamp:
+    if hit is None or not _stamp_matches(hit[0], params):
         if hit is not None:
             _RETIRED.append(hit[1])
         width, dim = layers[0].weight.shape
@@ -58,7 +71,7 @@ def stacked_linear(layers, dtype, multiple=1):
             w[i * pitch:i * pitch + width] = layer.weight.detach().to(dtype)
             if has_bias:
                 b[i * pitch:i * pitch + width] = layer.bias.detach().to(dtype)
-        hit = (stamp, (w, b, pitch))
+        hit = (_stamp(params), (w, b, pitch))
         _STACKED[key] = hit
     return hit[1]
 

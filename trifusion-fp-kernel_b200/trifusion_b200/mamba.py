@@ -49,14 +49,15 @@ def paired_mean(fwd, bwd, y):
     GEMM's output type, instead of each projection being rounded before the average."""
     dev = y.device.type
     dtype = torch.get_autocast_dtype(dev) if torch.is_autocast_enabled(dev) else fwd.out_proj.weight.dtype
+    from .kernels.buffers import _stamp, _stamp_matches
+
     wf, wb = fwd.out_proj.weight, bwd.out_proj.weight
     key = (id(wf), id(wb), dtype)
-    stamp = tuple((w._version, w.data_ptr(), w.device) for w in (wf, wb))
     hit = _PAIRED.get(key)
-    if hit is None or hit[0] != stamp:
+    if hit is None or not _stamp_matches(hit[0], (wf, wb)):
         if hit is not None:
             _RETIRED.append(hit[1])
-        hit = (stamp, (0.5 * torch.cat((wf.detach().float(), wb.detach().float()), 1)).to(dtype))
+        hit = (_stamp((wf, wb)), (0.5 * torch.cat((wf.detach().float(), wb.detach().float()), 1)).to(dtype))
         _PAIRED[key] = hit
     return F.linear(y, hit[1])
 

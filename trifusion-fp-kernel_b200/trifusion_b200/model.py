@@ -257,9 +257,9 @@ class TriFusionBlock(nn.Module):
 
                 # e_value and e_gate share z: one GEMM over both weights; the norm reads the
                 # two halves of its output rows in place.
-                w_ev, b_ev, _ = stacked_linear([self.e_value, self.e_gate], torch.bfloat16)
+                w_ev, b_ev, pitch = stacked_linear([self.e_value, self.e_gate], torch.bfloat16)
                 ev = F.linear(z, w_ev, b_ev)
-                value, gate = ev[..., :d], ev[..., d:]
+                value, gate = ev[..., :d], ev[..., pitch:pitch + d]
             else:
                 value, gate = self.e_value(z), self.e_gate(z)
             u = native.evidence_norm(x, value, gate, self.u_norm.weight, mask, self.u_norm.eps,

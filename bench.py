@@ -53,6 +53,9 @@ WORKLOADS = {
     "cfg4": dict(kind="box", clips=1024, max_batch=32, padded_seconds=480),
 }
 AUDIO_METRIC_UNIT = "audio-sec/s"
+# Reserved-memory bound of the benchmark engines: one graph per batch shape of up to 480
+# padded audio-seconds needs more than the reference's 19.5 GiB default (sized for a 24 GB L4).
+BENCH_RESERVED_GIB = 64.0
 # Default timed steps: each bounded to well under a minute of GPU time.
 DEFAULT_STEPS = {"cfg1": 20000, "cfg2": 20000, "cfg3": 200, "cfg4": 3}
 
@@ -103,6 +106,25 @@ def algorithmic_bytes(b, t, h, lengths, hq=1, n=128, p=64, r=32, trap_bytes=4):
             + rows * r * 2                  # raw angles (broadcast over heads)
             + b * t * h * p * 2             # out (all rows)
             + h * (2 * n + 1) * 4 + 2 * n * 4 + b * 8)  # qb, kb, d, norm weights, lengths
+
+
+def input_sets(base, b, t, h):
+    """(bytes of one input set incl. its output buffer, number of sets cycled so that
+    every timed step reads its inputs from HBM: > 3x the L2)."""
+    full_set_bytes = sum(x.numel() * x.element_size() for i, x in enumerate(base) if i != 8) + \
+        b * t * 32 * 2 + b * t * h * 64 * 2  # + shared angles + the output buffer
+    return full_set_bytes, max(2, math.ceil(3 * L2_BYTES / full_set_bytes))
+
+
+def recurrence_config(workload, wl, base, lengths, world):
+    """The ``config`` of a recurrence bench line; both arms print the same dict."""
+    b, t, h = wl["batch"], wl["time"], wl["heads"]
+    full_set_bytes, nsets = input_sets(base, b, t, h)
+    return {"workload": workload, "B": b, "T": t, "H": h, "Hq": 1, "N": 128, "P": 64,
+            "R": 32, "lengths": [int(x) for x in lengths],
+            "step": "RMSNorm(q,k) + fused recurrence + SiLU(z) gate + length mask, one launch",
+            "l2": f"inputs cycled over {nsets} sets ({nsets * full_set_bytes / 2**20:.0f} MiB > L2)",
+            "parallelism": f"replicas x{world} (one batch per GPU)"}
 
 
 class ClockSampler:
@@ -214,8 +236,10 @@ def run_reference(args, wl):
     from trifusion_b200.synthetic import recurrence_inputs, norm_weight
     torch.set_num_threads(cores)
     b, t, h = wl["batch"], wl["time"], wl["heads"]
-    inputs = [a.float().numpy() for a in recurrence_inputs(b, t, h, kind="baseline")]
+    base = recurrence_inputs(b, t, h, kind="baseline")
+    inputs = [a.float().numpy() for a in base]
     lengths = make_lengths(wl["lengths"], b).numpy()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     qw, kw = norm_weight(128, 1).numpy(), norm_weight(128, 2).numpy()
     from oracle import mamba_oracle as O
 
@@ -225,7 +249,7 @@ def run_reference(args, wl):
         a[1] = O.rms(a[1], kw)
         return O.mask_rows(O.fused_mamba(*a, dtype=np.float32), lengths)
 
-    for _ in range(max(args.warmup, 0) and 1):
+    for _ in range(max(args.warmup, 0)):
         step()
     steps = max(1, min(args.steps, 20))
     t0 = time.perf_counter()
@@ -235,11 +259,10 @@ def run_reference(args, wl):
     value = b * t * steps / el
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": steps, "warmup": 1, "ms_per_step": el / steps * 1e3,
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": el / steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": args.workload, "B": b, "T": t, "H": h, "Hq": 1, "N": 128, "P": 64,
-                   "R": 32, "step": "rms(q,k) -> fused recurrence -> length mask"},
+        "config": recurrence_config(args.workload, wl, base, lengths, world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "torch_threads": _torch_threads(), "kind": "port",
                          "sample": f"{steps} full {args.workload} batches (B={b}, T={t}, H={h}), numpy FP32"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -303,9 +326,7 @@ def run_recurrence(args, wl):
     qw_cpu, kw_cpu = norm_weight(128, 1), norm_weight(128, 2)
     qw, kw = qw_cpu.to(dev), kw_cpu.to(dev)
     step_bytes = algorithmic_bytes(b, t, h, lengths_cpu.tolist())
-    full_set_bytes = sum(x.numel() * x.element_size() for i, x in enumerate(base) if i != 8) + \
-        b * t * 32 * 2 + b * t * h * 64 * 2  # + shared angles + the output buffer
-    nsets = max(2, math.ceil(3 * L2_BYTES / full_set_bytes))
+    full_set_bytes, nsets = input_sets(base, b, t, h)
     sets = []
     for s in range(nsets):
         dev_args = [x.to(dev) if i != 8 else None for i, x in enumerate(base)]
@@ -323,11 +344,20 @@ def run_recurrence(args, wl):
         for i in range(max(args.warmup, 0)):
             step(i)
         torch.cuda.synchronize(dev)
+        # Exactly K launches, all as graph replays: a graph over every input set,
+        # replayed K // S times, then a graph over the first K % S sets, once.
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             for i in range(nsets):
                 step(i)
         rest = args.steps % nsets
+        tail = None
+        if rest:
+            tail = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(tail, stream=stream):
+                for i in range(rest):
+                    step(i)
+            tail.replay()
         # load phase so clock samples reflect a busy GPU
         sampler = ClockSampler(local)
         sampler.start()
@@ -344,8 +374,8 @@ def run_recurrence(args, wl):
         ev0.record(stream)
         for _ in range(args.steps // nsets):
             graph.replay()
-        for i in range(rest):
-            step(i)
+        if tail is not None:
+            tail.replay()
         ev1.record(stream)
         torch.cuda.synchronize(dev)
         tw1 = time.time()
@@ -432,7 +462,7 @@ def run_recurrence(args, wl):
 
     if world > 1:
         dist.barrier()
-        del graph, warm_graph
+        del graph, tail, warm_graph
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -443,15 +473,12 @@ def run_recurrence(args, wl):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.workload, "B": b, "T": t, "H": h, "Hq": 1, "N": 128, "P": 64,
-                   "R": 32, "lengths": lengths_cpu.tolist(),
-                   "step": "RMSNorm(q,k) + fused recurrence + SiLU(z) gate + length mask, one launch",
-                   "l2": f"inputs cycled over {nsets} sets ({nsets * full_set_bytes / 2**20:.0f} MiB > L2)",
-                   "parallelism": f"replicas x{world} (one batch per GPU)"},
+        "config": recurrence_config(args.workload, wl, base, lengths_cpu.tolist(), world),
         "hbm_gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
                      "tensor_pipe_active_pct_ncu": tensor_pct,
+                     "kernel_source_sha16": kernel_source_hash(),
                      "l2_warm": {"ms_per_step": warm_ms_per_step,
                                  "value": world * b * t / (warm_ms_per_step / 1e3)},
                      "peak_source": peak_kind,
@@ -506,7 +533,7 @@ def run_model(args, wl):
             eager(*inputs)
         torch.cuda.synchronize(dev)
         return
-    engine = InferenceEngine(model, graphs=True, max_graphs=1)
+    engine = InferenceEngine(model, graphs=True, max_graphs=1, max_reserved_gib=BENCH_RESERVED_GIB)
     flush = _l2_flush_buffer(dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 1)):
@@ -616,7 +643,8 @@ def run_box(args, wl):
     shapes = {tuple(h[0].shape) for h in host}
     with tempfile.TemporaryDirectory() as tmp:
         model = _student(dev, tmp)
-    engine = InferenceEngine(model, graphs=True, max_graphs=max(len(shapes), 1))
+    engine = InferenceEngine(model, graphs=True, max_graphs=max(len(shapes), 1),
+                             max_reserved_gib=BENCH_RESERVED_GIB)
     total_audio_s = sum(r.samples for r in records) / 16000
     stream = torch.cuda.current_stream(dev)
 
@@ -743,14 +771,30 @@ def run_reference_model(args, wl):
     print(json.dumps(line), flush=True)
 
 
+KERNEL_SOURCES = ("recurrence_persistent.cu", "recurrence.cuh", "sm100.cuh", "tf_common.cuh")
+
+
+def kernel_source_hash():
+    """First 16 hex digits of the SHA-256 over the recurrence kernel's source files."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for name in KERNEL_SOURCES:
+        h.update((ROOT / "trifusion-fp-kernel_b200" / "csrc" / name).read_bytes())
+    return h.hexdigest()[:16]
+
+
 def measured_traffic(workload, column=2):
-    """A figure of the committed ncu summary (column 2: DRAM bytes per launch; 3: tensor-pipe active %)."""
+    """A figure of the committed ncu summary (column 2: DRAM bytes per launch; 3: tensor-pipe
+    active %), or None when it is absent or was captured on other kernel sources (column 4
+    holds the source hash of the capture)."""
     path = ROOT / "profiles" / "traffic.txt"
     if not path.exists():
         return None
+    current = kernel_source_hash()
     for row in path.read_text().splitlines():
         f = row.split()
-        if len(f) > column and f[0] == workload:
+        if len(f) > 4 and f[0] == workload and f[4] == current:
             try:
                 return float(f[column])
             except ValueError:

@@ -90,10 +90,12 @@ class InferenceEngine:
     """Eager or CUDA-graph inference (reference ``runtime.py:70-138``).
 
     ``max_reserved_gib`` bounds the caching allocator's reservation after a
-    capture; the default leaves most of a B200's 180 GB to other work.
+    capture (a capture that leaves more reserved is dropped and its shape runs
+    eagerly); the default is the reference's 19.5 GiB. Callers that batch many
+    seconds of audio per call on a 180 GB B200 pass a larger bound.
     """
 
-    def __init__(self, model, graphs=False, max_graphs=2, max_reserved_gib=64.0):
+    def __init__(self, model, graphs=False, max_graphs=2, max_reserved_gib=19.5):
         self.model = model
         self.graphs = graphs
         self.max_graphs = max_graphs

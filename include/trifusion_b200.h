@@ -114,7 +114,11 @@ int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v,
  * workspace is a 64 MiB array inside the library, held on every GPU that loads
  * it until exit; problems needing more (tf_recurrence_workspace_size) return
  * TF_ERR_SIZE without launching. The first call on a device sets up that
- * device's array address and must come before any stream capture. Every call
+ * device's array address and must come before any stream capture; with lazy
+ * module loading the array is reserved then, so make that call at start-up,
+ * before a memory pool takes the device's memory (if the array cannot be had
+ * the call returns TF_ERR_DEVICE and tf_last_cuda_error names why). Arguments
+ * are validated before the array is touched. Every call
  * clears the array's header and chunk flags on `stream` before the launch;
  * calls that overlap on the GPU share the array and race, so serialise them.
  * Same arguments and results as tf_mamba_recurrence_fwd otherwise.

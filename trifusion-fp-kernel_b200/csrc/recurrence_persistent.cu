@@ -50,8 +50,12 @@
 // split into FP16 hi + lo halves; sums accumulate in FP32. qk (the D-skip dot
 // product, mamba_fused.py:124) is the score diagonal, since rotating q and k by
 // the same angle preserves their dot product; (D + qk) v rides on P's diagonal.
+#include <cstdio>
+
+#include "../../include/trifusion_b200.h"
 #include "recurrence.cuh"
 #include "sm100.cuh"
+#include "tf_host.cuh"
 
 namespace tf {
 namespace {
@@ -1337,7 +1341,11 @@ int read_device_error(int reset) {
 //     TF_ERR_SIZE before anything is launched.
 //   - The first call on a device looks up the array's device address there
 //     (cudaGetSymbolAddress, with that device current) and caches it; make that
-//     first call before any stream capture.
+//     first call before any stream capture. With CUDA's lazy module loading the
+//     array is reserved when this file's module first loads on the device, which
+//     can be that first call: make it at start-up, before a memory pool takes the
+//     device's memory. If the array cannot be had, the call returns
+//     TF_ERR_DEVICE and tf_last_cuda_error names the cause.
 //   - All calls on a device share the one array. Each call first clears what
 //     the kernel needs at zero (the workspace header and every chunk flag), so
 //     a call never depends on what an earlier call left behind, but calls that
@@ -1352,34 +1360,51 @@ __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes
 void* g_static_ptr[kMaxDevices] = {nullptr};
 
 // Device address of g_static_workspace on the current device (set up once).
+// TF_OK, or TF_ERR_DEVICE with the cause recorded.
 int static_workspace(void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    snprintf(g_last_error, sizeof g_last_error, "no usable current CUDA device");
+    return TF_ERR_DEVICE;
+  }
   if (g_static_ptr[dev] == nullptr) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_static_workspace) != cudaSuccess || ptr == nullptr) return -1;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_workspace);
+    if (e != cudaSuccess || ptr == nullptr) {
+      // With lazy module loading this is where the module (and the array) is first
+      // loaded on the device; it fails when no device memory is left for it.
+      snprintf(g_last_error, sizeof g_last_error, "static workspace unavailable on device %d: %s", dev,
+               cudaGetErrorString(e));
+      (void)cudaGetLastError();
+      return TF_ERR_DEVICE;
+    }
     g_static_ptr[dev] = ptr;
   }
   *out = g_static_ptr[dev];
-  return 0;
+  return TF_OK;
 }
 
 }  // namespace
 
 // Clears the static workspace's header and chunk flags on `stream`, then
-// returns its address and capacity; nonzero when the set-up failed.
+// returns its address and capacity. TF_OK, or an error status with the cause
+// recorded.
 int prepare_static_workspace(int B, int T, int H, cudaStream_t stream, void** ws, size_t* bytes) {
   void* ptr = nullptr;
-  if (static_workspace(&ptr) != 0) return -1;
+  const int st = static_workspace(&ptr);
+  if (st != TF_OK) return st;
   const size_t units = static_cast<size_t>((T + kChunk - 1) / kChunk) * B * H;
   unsigned char* base = static_cast<unsigned char*>(ptr);
-  if (cudaMemsetAsync(base, 0, kWsHeader, stream) != cudaSuccess) return -1;
-  if (units > 0 && cudaMemset2DAsync(base + kWsHeader + kUnitFlag, kUnitBytes, 0, sizeof(uint32_t), units,
-                                     stream) != cudaSuccess)
-    return -1;
+  cudaError_t e = cudaMemsetAsync(base, 0, kWsHeader, stream);
+  if (e == cudaSuccess && units > 0)
+    e = cudaMemset2DAsync(base + kWsHeader + kUnitFlag, kUnitBytes, 0, sizeof(uint32_t), units, stream);
+  if (e != cudaSuccess) {
+    snprintf(g_last_error, sizeof g_last_error, "%s", cudaGetErrorString(e));
+    return TF_ERR_LAUNCH;
+  }
   *ws = ptr;
   *bytes = kStaticWorkspaceBytes;
-  return 0;
+  return TF_OK;
 }
 
 size_t static_workspace_capacity() { return kStaticWorkspaceBytes; }

@@ -55,19 +55,25 @@ int launch_status() {
   return TF_ERR_LAUNCH;
 }
 
-int recurrence_entry(const void* q, const void* k, const void* v, const float* adt,
-                     const float* dt, const void* trap, int trap_dtype, const float* qb,
-                     const float* kb, const void* angles, const float* d, const void* z,
-                     void* out, const int64_t* strides, int batch, int seqlen, int heads,
-                     int groups, const float* qw, const float* kw, float eps,
-                     const int64_t* lengths, void* workspace, size_t workspace_bytes, void* stream) {
+// Builds and validates the parameters of a one-direction launch. Returns TF_OK
+// (with `empty` set when there is nothing to launch) or an error status; touches
+// no device state besides the per-device attribute cache.
+int recurrence_params(const void* q, const void* k, const void* v, const float* adt, const float* dt,
+                      const void* trap, int trap_dtype, const float* qb, const float* kb, const void* angles,
+                      const float* d, const void* z, void* out, const int64_t* strides, int batch, int seqlen,
+                      int heads, int groups, const float* qw, const float* kw, float eps,
+                      const int64_t* lengths, RecurrenceParams& p, bool& empty) {
+  empty = false;
   if (!strides || batch < 0 || seqlen < 0 || heads < 0 || groups <= 0) return TF_ERR_ARG;
   if (trap_dtype != TF_F32 && trap_dtype != TF_BF16) return TF_ERR_ARG;
   if (heads % groups != 0) return TF_ERR_ARG;
-  if (batch == 0 || seqlen == 0 || heads == 0) return TF_OK;  // empty launch grid
+  if (batch == 0 || seqlen == 0 || heads == 0) {  // empty launch grid
+    empty = true;
+    return TF_OK;
+  }
   if (!q || !k || !v || !adt || !dt || !trap || !qb || !kb || !angles || !d || !z || !out)
     return TF_ERR_ARG;
-  RecurrenceParams p{};
+  p = RecurrenceParams{};
   p.q = static_cast<const bf16*>(q);
   p.k = static_cast<const bf16*>(k);
   p.v = static_cast<const bf16*>(v);
@@ -102,21 +108,37 @@ int recurrence_entry(const void* q, const void* k, const void* v, const float* a
   p.T = seqlen;
   p.H = heads;
   p.Hq = groups;
-  int st = check_device();
-  if (st != TF_OK) return st;
+  return check_device();
+}
+
+// Launches validated one-direction parameters on `workspace`.
+int recurrence_launch(const RecurrenceParams& p, void* workspace, size_t workspace_bytes, void* stream) {
   if (!workspace) return TF_ERR_ARG;
-  if (workspace_bytes < recurrence_workspace_bytes(batch, seqlen, heads)) return TF_ERR_SIZE;
-  const cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H)) return TF_ERR_SIZE;
   RecurrenceLaunch launch{};
   launch.dir[0] = p;
   launch.dir[1] = p;
   launch.ndir = 1;
-  st = launch_recurrence_persistent(launch, workspace, workspace_bytes, cs);
+  const int st = launch_recurrence_persistent(launch, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
   if (st != 0) {
     const int ls = launch_status();
     return ls != TF_OK ? ls : TF_ERR_LAUNCH;
   }
   return launch_status();
+}
+
+int recurrence_entry(const void* q, const void* k, const void* v, const float* adt,
+                     const float* dt, const void* trap, int trap_dtype, const float* qb,
+                     const float* kb, const void* angles, const float* d, const void* z,
+                     void* out, const int64_t* strides, int batch, int seqlen, int heads,
+                     int groups, const float* qw, const float* kw, float eps,
+                     const int64_t* lengths, void* workspace, size_t workspace_bytes, void* stream) {
+  RecurrenceParams p;
+  bool empty = false;
+  const int st = recurrence_params(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out, strides, batch,
+                                   seqlen, heads, groups, qw, kw, eps, lengths, p, empty);
+  if (st != TF_OK || empty) return st;
+  return recurrence_launch(p, workspace, workspace_bytes, stream);
 }
 
 // One direction's parameters from the public argument record; validation as in
@@ -248,22 +270,24 @@ int tf_mamba_recurrence_fwd_static(const void* q, const void* k, const void* v, 
                                    const int64_t* strides, int batch, int seqlen, int heads,
                                    int groups, const float* q_norm_w, const float* k_norm_w,
                                    float eps, const int64_t* lengths, void* stream) {
-  if (batch < 0 || seqlen < 0 || heads < 0) return TF_ERR_ARG;
-  if (batch == 0 || seqlen == 0 || heads == 0) return TF_OK;
+  // Everything is validated before the shared array is touched: a rejected call
+  // leaves its contents as they were.
+  tf::RecurrenceParams p;
+  bool empty = false;
+  int st = tf::recurrence_params(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out, strides, batch,
+                                 seqlen, heads, groups, q_norm_w, k_norm_w, eps, lengths, p, empty);
+  if (st != TF_OK || empty) return st;
   if (tf::recurrence_workspace_bytes(batch, seqlen, heads) > tf::static_workspace_capacity()) {
     snprintf(tf::g_last_error, sizeof tf::g_last_error,
              "problem needs %zu workspace bytes; the static workspace holds %zu",
              tf::recurrence_workspace_bytes(batch, seqlen, heads), tf::static_workspace_capacity());
     return TF_ERR_SIZE;
   }
-  const int st = tf::check_device();
-  if (st != TF_OK) return st;
   void* ws = nullptr;
   size_t bytes = 0;
-  if (tf::prepare_static_workspace(batch, seqlen, heads, static_cast<cudaStream_t>(stream), &ws, &bytes) != 0)
-    return tf::launch_status() != TF_OK ? TF_ERR_LAUNCH : TF_ERR_DEVICE;
-  return tf::recurrence_entry(q, k, v, adt, dt, trap, trap_dtype, qb, kb, angles, d, z, out, strides, batch,
-                              seqlen, heads, groups, q_norm_w, k_norm_w, eps, lengths, ws, bytes, stream);
+  st = tf::prepare_static_workspace(batch, seqlen, heads, static_cast<cudaStream_t>(stream), &ws, &bytes);
+  if (st != TF_OK) return st;
+  return tf::recurrence_launch(p, ws, bytes, stream);
 }
 
 int tf_mamba_recurrence_fwd(const void* q, const void* k, const void* v, const float* adt,

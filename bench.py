@@ -636,7 +636,11 @@ def run_box(args, wl):
     configure_runtime()
     records = clip_set(wl["clips"], seed=0)
     plan = plan_batches(records, padded_seconds=wl["padded_seconds"], max_batch=wl["max_batch"])
-    mine = lpt_partition([batch_cost(lim, rows) for lim, rows in plan], world)[rank]
+    parts = lpt_partition([batch_cost(lim, rows) for lim, rows in plan], world)
+    mine = parts[rank]
+    # Every rank computes the same partition, so the largest rank's clip count bounds
+    # the gather: one all-gather of logits at the end.
+    capacity = max(sum(len(plan[i][1]) for i in p) for p in parts)
     host = [tuple(x.pin_memory() for x in batch_audio(plan[i][0], plan[i][1], seed=0)) for i in mine]
     indices = torch.tensor([r.index for i in mine for r in plan[i][1]], dtype=torch.int64, device=dev)
     dev_in = [tuple(x.to(dev) for x in h) for h in host]
@@ -652,7 +656,7 @@ def run_box(args, wl):
         outs = [engine(*x) for x in inputs]
         local_logits = torch.cat(outs) if outs else torch.zeros(0, 5, device=dev)
         if world > 1:
-            return gather_logits(indices, local_logits)
+            return gather_logits(indices, local_logits, capacity=capacity)
         return indices, local_logits
 
     for _ in range(max(args.warmup, 1)):

@@ -43,14 +43,35 @@ def test_stacked_linear_pads_caches_and_retires():
     torch.testing.assert_close(y[:, :13], a(x).detach())
     torch.testing.assert_close(y[:, 16:29], b(x).detach())
     assert B.stacked_linear([a, b], torch.float32, multiple=8)[0] is w  # cached
-    retired = len(B._RETIRED)
+    key = next(k for k, e in B._STACKED._entries.items() if e[1][0] is w)
     with torch.no_grad():
         a.weight.add_(1.0)  # version counter moves: a new stacked copy, the old one kept
     w2, _, _ = B.stacked_linear([a, b], torch.float32, multiple=8)
-    assert w2 is not w and len(B._RETIRED) == retired + 1
+    assert w2 is not w and B._STACKED._entries[key][2][-1][0] is w
     assert torch.equal(w2[:13], a.weight.detach())
     with pytest.raises(ValueError):
         B.stacked_linear([a, torch.nn.Linear(16, 12)], torch.float32)
+
+
+def test_param_caches_drop_entries_of_freed_parameters():
+    """Loading and freeing layers leaves no cached copies behind: an entry (with the
+    copies it superseded) goes when one of its parameters is garbage-collected."""
+    import gc
+
+    from trifusion_b200.kernels import buffers as B
+
+    before = len(B._STACKED), len(B._BF16_PARAMS)
+    for _ in range(5):
+        a, b = torch.nn.Linear(16, 13), torch.nn.Linear(16, 13)
+        B.stacked_linear([a, b], torch.float32, multiple=8)
+        with torch.no_grad():
+            a.weight.add_(1.0)
+        B.stacked_linear([a, b], torch.float32, multiple=8)
+        B._param_bf16(a.weight, (13, 16))
+        assert len(B._STACKED) == before[0] + 1 and len(B._BF16_PARAMS) == before[1] + 1
+        del a, b
+        gc.collect()
+        assert (len(B._STACKED), len(B._BF16_PARAMS)) == before
 
 
 def test_paired_mean_is_the_mean_of_both_projections():

@@ -66,6 +66,10 @@ def _gather_worker(rank, world, port, out):
         idx = torch.tensor([10 * i + j for i in mine for j in range(2)], dtype=torch.int64)
         logits = idx.double().unsqueeze(1).repeat(1, 5).float() + torch.arange(5).float()
         all_idx, all_logits = gather_logits(idx, logits)
+        # One collective round when every rank knows a bound on the others' rows.
+        cap = max(2 * len(p) for p in lpt_partition(costs, world))
+        one_idx, one_logits = gather_logits(idx, logits, capacity=cap)
+        assert torch.equal(one_idx, all_idx) and torch.equal(one_logits, all_logits)
         out[rank] = (all_idx.tolist(), all_logits.tolist())
     finally:
         dist.destroy_process_group()

@@ -11,12 +11,6 @@ import torch
 from .. import _lib
 
 
-_BF16_PARAMS = {}
-# Superseded cached copies stay allocated: a CUDA graph captured before the parameter
-# changed still reads them (it must be recaptured to see the new values).
-_RETIRED = []
-
-
 def _stamp(params):
     """Identity and state of ``params`` for a cache entry: weak references (a freed
     parameter whose id and address are reused never matches) plus each version
@@ -30,21 +24,56 @@ def _stamp_matches(stamp, params):
         for (ref, v, ptr, dev), p in zip(stamp, params))
 
 
+class ParamCache:
+    """Tensors derived from parameters (casts, stacks), kept while the parameters
+    stay the same live objects with the same version counters and storage.
+
+    When a parameter changes, the entry is rebuilt and the superseded value stays
+    allocated beside the new one for as long as the parameters live: a CUDA graph
+    captured before the change still reads it (and must be recaptured to see the
+    new values). When any of the parameters is garbage-collected, its entries and
+    their superseded values are dropped, so loading and freeing models in one
+    process does not accumulate device memory.
+    """
+
+    def __init__(self):
+        self._entries = {}  # key -> (stamp, value, superseded values, token)
+
+    def get(self, key, params, build):
+        params = tuple(params)
+        hit = self._entries.get(key)
+        if hit is not None and _stamp_matches(hit[0], params):
+            return hit[1]
+        superseded = []
+        if hit is not None and all(ref() is p for (ref, *_), p in zip(hit[0], params)):
+            superseded = hit[2] + [hit[1]]  # same live parameters, new contents
+        token = object()
+        self._entries[key] = (_stamp(params), build(), superseded, token)
+        for prm in params:
+            weakref.finalize(prm, self._drop, key, token)
+        return self._entries[key][1]
+
+    def _drop(self, key, token):
+        hit = self._entries.get(key)
+        if hit is not None and hit[3] is token:
+            del self._entries[key]
+
+    def __len__(self):
+        return len(self._entries)
+
+
+_BF16_PARAMS = ParamCache()
+
+
 def _param_bf16(param, shape):
     """A contiguous BF16 copy of ``param`` reshaped to ``shape``, cached until the
     parameter changes (its version counter or storage), so steady-state calls launch
     no conversion kernel."""
-    key = (id(param), shape)
-    hit = _BF16_PARAMS.get(key)
-    if hit is None or not _stamp_matches(hit[0], (param,)):
-        if hit is not None:
-            _RETIRED.append(hit[1])
-        hit = (_stamp((param,)), param.detach().to(torch.bfloat16).reshape(shape).contiguous())
-        _BF16_PARAMS[key] = hit
-    return hit[1]
+    return _BF16_PARAMS.get((id(param), shape), (param,),
+                            lambda: param.detach().to(torch.bfloat16).reshape(shape).contiguous())
 
 
-_STACKED = {}
+_STACKED = ParamCache()
 
 
 def stacked_linear(layers, dtype, multiple=1):
@@ -55,10 +84,8 @@ def stacked_linear(layers, dtype, multiple=1):
     until a parameter changes (version counter or storage). Returns (weight, bias, pitch)."""
     params = [p for layer in layers for p in (layer.weight, layer.bias) if p is not None]
     key = (tuple(id(p) for p in params), dtype, multiple)
-    hit = _STACKED.get(key)
-    if hit is None or not _stamp_matches(hit[0], params):
-        if hit is not None:
-            _RETIRED.append(hit[1])
+
+    def build():
         width, dim = layers[0].weight.shape
         if any(tuple(layer.weight.shape) != (width, dim) for layer in layers):
             raise ValueError("stacked_linear: the layers must have one shape")
@@ -71,9 +98,9 @@ def stacked_linear(layers, dtype, multiple=1):
             w[i * pitch:i * pitch + width] = layer.weight.detach().to(dtype)
             if has_bias:
                 b[i * pitch:i * pitch + width] = layer.bias.detach().to(dtype)
-        hit = (_stamp(params), (w, b, pitch))
-        _STACKED[key] = hit
-    return hit[1]
+        return w, b, pitch
+
+    return _STACKED.get(key, params, build)
 
 
 def _mask_bytes(mask):

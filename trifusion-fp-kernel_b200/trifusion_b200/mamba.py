@@ -38,10 +38,6 @@ def projections(mods, u):
     return [p[..., i * pitch:i * pitch + width] for i in range(len(mods))]
 
 
-_PAIRED = {}
-_RETIRED = []  # superseded weights stay allocated for graphs captured before the change
-
-
 def paired_mean(fwd, bwd, y):
     """``(fwd.out_proj(y_f) + bwd.out_proj(y_b)) / 2`` for ``y = [y_f | y_b]`` (rows of
     ``2 * d_inner``) as ONE GEMM over K = 2 * d_inner with the two weights side by side
@@ -49,17 +45,12 @@ def paired_mean(fwd, bwd, y):
     GEMM's output type, instead of each projection being rounded before the average."""
     dev = y.device.type
     dtype = torch.get_autocast_dtype(dev) if torch.is_autocast_enabled(dev) else fwd.out_proj.weight.dtype
-    from .kernels.buffers import _stamp, _stamp_matches
+    from .kernels.buffers import _STACKED
 
     wf, wb = fwd.out_proj.weight, bwd.out_proj.weight
-    key = (id(wf), id(wb), dtype)
-    hit = _PAIRED.get(key)
-    if hit is None or not _stamp_matches(hit[0], (wf, wb)):
-        if hit is not None:
-            _RETIRED.append(hit[1])
-        hit = (_stamp((wf, wb)), (0.5 * torch.cat((wf.detach().float(), wb.detach().float()), 1)).to(dtype))
-        _PAIRED[key] = hit
-    return F.linear(y, hit[1])
+    w = _STACKED.get(("paired_mean", id(wf), id(wb), dtype), (wf, wb),
+                     lambda: (0.5 * torch.cat((wf.detach().float(), wb.detach().float()), 1)).to(dtype))
+    return F.linear(y, w)
 
 
 def bidirectional_rows(fwd, bwd, u, lengths):

@@ -39,29 +39,43 @@ def lpt_partition(costs, world):
     return [sorted(items) for items in owned]
 
 
-def gather_logits(indices, logits, group=None):
+def gather_logits(indices, logits, group=None, capacity=None):
     """All-gather each rank's ``(indices [n_r] int64, logits [n_r, 5])`` and
     return them concatenated in clip-index order, on every rank.
 
-    One collective round: the per-rank counts, then the padded payload
-    (indices and logits packed in one float64 tensor).
+    With ``capacity`` (an upper bound on every rank's ``n_r``, e.g. from the
+    deterministic partition every rank computes) this is one all-gather: each
+    rank sends ``capacity + 1`` rows of float64, the first holding its count.
+    Without it, two: the per-rank counts, then the payload padded to the largest.
+    Indices travel as float64, exact below 2**53.
     """
     import torch
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     dev = logits.device
-    n = torch.tensor([indices.numel()], device=dev, dtype=torch.int64)
-    counts = [torch.zeros_like(n) for _ in range(world)]
-    dist.all_gather(counts, n, group=group)
-    top = int(max(int(c.item()) for c in counts))
     width = logits.shape[1] if logits.dim() == 2 else 5
-    pack = torch.zeros(top, 1 + width, device=dev, dtype=torch.float64)
-    if indices.numel():
-        pack[: indices.numel(), 0] = indices.to(dev, torch.float64)
-        pack[: indices.numel(), 1:] = logits.to(torch.float64)
+    n_local = indices.numel()
+    if capacity is None:
+        n = torch.tensor([n_local], device=dev, dtype=torch.int64)
+        counts = [torch.zeros_like(n) for _ in range(world)]
+        dist.all_gather(counts, n, group=group)
+        counts = [int(c.item()) for c in counts]
+        top, head = max(counts), 0
+    else:
+        if n_local > capacity:
+            raise ValueError(f"gather_logits: {n_local} rows exceed the capacity {capacity}")
+        counts, top, head = None, int(capacity), 1
+    pack = torch.zeros(head + top, 1 + width, device=dev, dtype=torch.float64)
+    if head:
+        pack[0, 0] = n_local
+    if n_local:
+        pack[head:head + n_local, 0] = indices.to(dev, torch.float64)
+        pack[head:head + n_local, 1:] = logits.to(torch.float64)
     parts = [torch.empty_like(pack) for _ in range(world)]
     dist.all_gather(parts, pack, group=group)
-    rows = torch.cat([p[: int(c.item())] for p, c in zip(parts, counts)])
+    if counts is None:
+        counts = [int(p[0, 0].item()) for p in parts]
+    rows = torch.cat([p[head:head + c] for p, c in zip(parts, counts)])
     order = rows[:, 0].argsort()
     return rows[order, 0].long(), rows[order, 1:].to(logits.dtype)

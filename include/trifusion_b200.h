@@ -53,10 +53,28 @@ int tf_version(void);
 /* Last CUDA error string recorded by this thread (static storage). */
 const char* tf_last_cuda_error(void);
 
-/* Device-side error word of the current device: non-zero after a kernel's
- * bounded wait on the tensor core gave up (the kernel then returns instead of
- * hanging). Synchronous; `reset` != 0 clears it. */
+/* Device-side error word of the current device: non-zero after one of a
+ * recurrence kernel's bounded waits gave up (on the tensor core, on the other
+ * warps of its CTA, or on another CTA's chunk flag); the kernel then finishes
+ * instead of hanging, and the outputs of that launch are invalid. Synchronous;
+ * `reset` != 0 clears it (and the host-mapped word below). */
 int tf_device_error(int reset);
+
+/* Sets up a pinned, device-mapped host word that the kernels also set when a
+ * wait gives up, so the host can poll it without synchronising
+ * (tf_device_error_pending). Call once, before any stream capture; allocates
+ * host memory only. Launches made before it report to the device word only. */
+int tf_error_watch_init(void);
+
+/* The host-mapped error word: non-zero once a launch has given up a wait
+ * (asynchronous: it shows after that launch has run). 0 when not set up. */
+int tf_device_error_pending(void);
+
+/* Limit, in nanoseconds, of a recurrence kernel's waits on other CTAs' chunk
+ * flags in later launches (0 restores the default of 2 s). A diagnostic
+ * control: a launch whose wait runs out records the error above and completes
+ * with invalid outputs. Waits inside a CTA keep their fixed 2 s limit. */
+int tf_set_flag_wait_ns(long long ns);
 
 /* Bytes of workspace the recurrence needs for [batch, seqlen, heads]
  * (0 for an empty problem). */

@@ -41,6 +41,11 @@ struct RecurrenceParams {
   // Set by the launcher: angle rows are 8-byte aligned with contiguous pairs
   // (staged by cp.async with the other rows).
   int ang_vec;
+  // Set by the launcher: how long a wait on another CTA's chunk flag may last
+  // before the kernel gives up (records an error and carries on), and the
+  // host-mapped error word it then also sets (null when none is set up).
+  unsigned long long flag_wait_ns;
+  int* err_host;
 };
 
 // One launch may run up to two directions over the same (B, T, H) shape; their
@@ -58,6 +63,10 @@ int launch_recurrence_persistent(const RecurrenceLaunch& launch, void* workspace
                                  cudaStream_t stream);
 // Device error word set when a kernel's bounded wait gave up (synchronous read).
 int read_device_error(int reset);
+// Host-mapped copy of the error word (readable without a synchronisation), the
+// flag-wait limit applied to later launches, and their set-up (tf_api.cu).
+int* host_error_word();
+unsigned long long flag_wait_limit_ns();
 // The library's own workspace array (see recurrence_persistent.cu): capacity,
 // and per-call preparation (device-address set-up on first use, clearing).
 size_t static_workspace_capacity();

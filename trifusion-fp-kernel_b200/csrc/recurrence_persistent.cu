@@ -370,7 +370,9 @@ __device__ __forceinline__ unsigned char* unit_ws(unsigned char* ws, int u) {
   return ws + kWsHeader + static_cast<size_t>(u) * kUnitBytes;
 }
 // Spin (bounded in time) until a unit's flag reaches `want` in this launch's epoch.
-__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, uint32_t want, uint32_t& seen) {
+// `limit_ns` is the launch's flag-wait limit (2 s unless the caller lowered it).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, uint32_t want, uint32_t& seen,
+                                          uint64_t limit_ns) {
   seen = ld_acquire_u32(flag);
   if (static_cast<int>(seen - epoch) >= static_cast<int>(want)) return true;
   const uint64_t t0 = global_timer_ns();
@@ -378,7 +380,7 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, 
     __nanosleep(64);
     seen = ld_acquire_u32(flag);
     if (static_cast<int>(seen - epoch) >= static_cast<int>(want)) return true;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -1025,7 +1027,8 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
             for (; y >= 0; --y) {
               uint32_t seen = 0;
               const int ub = unit_index(shp, y, dir, b, h);
-              ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, ub) + kUnitFlag), epoch, kFlagAgg, seen);
+              ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, ub) + kUnitFlag), epoch, kFlagAgg, seen,
+                              p0.flag_wait_ns);
               if (static_cast<int>(seen - epoch) >= static_cast<int>(kFlagIncl)) break;
             }
             mi.lookback_start = y;  // -1: none
@@ -1052,7 +1055,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           for (int x = lane; x < c; x += 32) {
             uint32_t seen = 0;
             ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, unit_index(shp, x, dir, b, h)) + kUnitFlag),
-                            epoch, kFlagAgg, seen);
+                            epoch, kFlagAgg, seen, p0.flag_wait_ns);
           }
           __syncwarp();
         }
@@ -1187,7 +1190,13 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
   }
 
   // ---- teardown: free TMEM; the last CTA advances the epoch -----------------------
-  if (!ok) atomicExch(&g_device_error, 1);
+  if (!ok) {
+    atomicExch(&g_device_error, 1);
+    if (p0.err_host) {  // a plain store: host memory over PCIe need not support atomics
+      *reinterpret_cast<volatile int*>(p0.err_host) = 1;
+      __threadfence_system();
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1295,7 +1304,11 @@ int launch_recurrence_persistent(const RecurrenceLaunch& launch_in, void* worksp
                                  cudaStream_t stream) {
   if (launch_in.ndir < 1 || launch_in.ndir > 2) return 1;
   RecurrenceLaunch L = launch_in;
-  for (int i = 0; i < L.ndir; ++i) L.dir[i].ang_vec = angles_vectorizable(L.dir[i]);
+  for (int i = 0; i < L.ndir; ++i) {
+    L.dir[i].ang_vec = angles_vectorizable(L.dir[i]);
+    L.dir[i].flag_wait_ns = flag_wait_limit_ns();
+    L.dir[i].err_host = host_error_word();
+  }
   const RecurrenceParams& p = L.dir[0];
   if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H, L.ndir)) return 1;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
@@ -1318,6 +1331,7 @@ int read_device_error(int reset) {
   if (reset) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (int* w = host_error_word()) *reinterpret_cast<volatile int*>(w) = 0;
   }
   return v;
 }

@@ -1,9 +1,11 @@
 // C ABI of trifusion_b200: argument validation, status codes and launches.
 // Declarations and the reference interface each entry point replaces are in
 // include/trifusion_b200.h.
+#include <atomic>
 #include <cstddef>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/trifusion_b200.h"
 #include "recurrence.cuh"
@@ -47,6 +49,14 @@ int sm_count() {
   }
   return g_sm_count[dev];
 }
+
+// Host-mapped error word (pinned, written by kernels whose bounded wait gave up)
+// and the flag-wait limit of later launches.
+std::atomic<int*> g_host_error{nullptr};
+std::atomic<unsigned long long> g_flag_wait_ns{2000000000ull};
+
+int* host_error_word() { return g_host_error.load(std::memory_order_relaxed); }
+unsigned long long flag_wait_limit_ns() { return g_flag_wait_ns.load(std::memory_order_relaxed); }
 
 int launch_status() {
   cudaError_t e = cudaGetLastError();
@@ -247,6 +257,34 @@ int tf_version(void) { return 100; }
 const char* tf_last_cuda_error(void) { return tf::g_last_error; }
 
 int tf_device_error(int reset) { return tf::read_device_error(reset); }
+
+int tf_error_watch_init(void) {
+  static std::mutex m;
+  std::lock_guard<std::mutex> lock(m);
+  if (tf::g_host_error.load()) return TF_OK;
+  int* w = nullptr;
+  const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&w), sizeof(int),
+                                      cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) {
+    snprintf(tf::g_last_error, sizeof tf::g_last_error, "%s", cudaGetErrorString(e));
+    (void)cudaGetLastError();
+    return TF_ERR_DEVICE;
+  }
+  *reinterpret_cast<volatile int*>(w) = 0;
+  tf::g_host_error.store(w);
+  return TF_OK;
+}
+
+int tf_device_error_pending(void) {
+  const int* w = tf::g_host_error.load();
+  return w ? *reinterpret_cast<const volatile int*>(w) : 0;
+}
+
+int tf_set_flag_wait_ns(long long ns) {
+  if (ns < 0) return TF_ERR_ARG;
+  tf::g_flag_wait_ns.store(ns == 0 ? 2000000000ull : static_cast<unsigned long long>(ns));
+  return TF_OK;
+}
 
 size_t tf_recurrence_workspace_size(int batch, int seqlen, int heads) {
   if (batch <= 0 || seqlen <= 0 || heads <= 0) return 0;

@@ -16,6 +16,7 @@ _EXPORTS = {
     "InferenceEngine": (".runtime", "InferenceEngine"),
     "fused_mamba": (".mamba_fused", "fused_mamba"),
     "fused_recurrence": (".mamba_fused", "fused_recurrence"),
+    "check_device_error": ("._lib", "check_device_error"),
 }
 
 

@@ -28,6 +28,9 @@ SIGNATURES = {
     "tf_version": [],
     "tf_last_cuda_error": [],
     "tf_device_error": [_i],
+    "tf_error_watch_init": [],
+    "tf_device_error_pending": [],
+    "tf_set_flag_wait_ns": [ctypes.c_longlong],
     "tf_recurrence_workspace_size": [_i, _i, _i],
     "tf_fused_mamba_fwd": [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p,
                            _i, _i, _i, _i, _p, _z, _p],
@@ -122,6 +125,38 @@ def check(status):
     raise RuntimeError(f"trifusion_b200: {text}" + (f" ({detail})" if detail else ""))
 
 
+DEVICE_ERROR_MESSAGE = ("trifusion_b200: a recurrence kernel gave up one of its bounded waits "
+                        "(outputs of that launch are invalid)")
+_watch = {"ready": False}
+
+
+def error_watch():
+    """Set up (once, outside stream capture) the host-mapped word that the kernels
+    set when a bounded wait gives up, so later calls can see it without a sync."""
+    if _watch["ready"]:
+        return
+    import torch
+
+    if torch.cuda.is_current_stream_capturing():
+        return
+    _watch["ready"] = lib().tf_error_watch_init() == TF_OK
+
+
+def check_device_error():
+    """Raise ``RuntimeError`` if an earlier launch recorded a device-side timeout
+    (read from the host-mapped word: no synchronisation). The word is cleared, so
+    the error is raised once."""
+    if _watch["ready"] and lib().tf_device_error_pending():
+        lib().tf_device_error(1)
+        raise RuntimeError(DEVICE_ERROR_MESSAGE)
+
+
+def set_flag_wait_ns(ns):
+    """Limit of the kernels' waits on other CTAs' chunk flags in later launches, in
+    nanoseconds (0: the default 2 s). A diagnostic control for tests."""
+    check(lib().tf_set_flag_wait_ns(int(ns)))
+
+
 def int64_array(values):
     values = list(values)
     return (ctypes.c_int64 * len(values))(*values)
@@ -173,6 +208,7 @@ def workspace(device, nbytes):
     """
     import torch
 
+    error_watch()
     idx = device.index if device.index is not None else torch.cuda.current_device()
     buf = _workspaces.get(idx)
     if buf is None or buf.numel() < nbytes:

@@ -69,6 +69,7 @@ def fused_mamba(q, k, v, adt, dt, trap, qb, kb, angles, d, z, warps=8):
     del warps
     (q, k, v, adt, dt, trap, qb, kb, angles, d, z), (b, t, h, hq) = _prep(
         q, k, v, adt, dt, trap, qb, kb, angles, d, z)
+    _lib.check_device_error()
     out = torch.empty_like(v, memory_format=torch.contiguous_format)
     stream = torch.cuda.current_stream(v.device).cuda_stream
     with torch.cuda.device(v.device):
@@ -96,6 +97,7 @@ def fused_recurrence(q, k, v, adt, dt, trap, qb, kb, angles, d, z, *, q_norm=Non
     """
     (q, k, v, adt, dt, trap, qb, kb, angles, d, z), (b, t, h, hq) = _prep(
         q, k, v, adt, dt, trap, qb, kb, angles, d, z)
+    _lib.check_device_error()
     if out is None:
         out = torch.empty_like(v, memory_format=torch.contiguous_format)
     qw = None if q_norm is None else q_norm.float().contiguous()
@@ -152,6 +154,7 @@ def fused_recurrence_multi(directions, *, lengths=None, eps=1e-5):
     """
     if not 1 <= len(directions) <= 2:
         raise ValueError("fused_recurrence_multi: one or two directions")
+    _lib.check_device_error()
     ios = (_lib.RecurrenceIO * len(directions))()
     keep, outs, shape = [], [], None
     for i, d_ in enumerate(directions):

@@ -17,6 +17,7 @@ from dataclasses import fields
 
 import torch
 
+from . import _lib
 from .model import ModelConfig, TriFusion
 
 B200_CAPABILITY = (10, 0)
@@ -152,6 +153,8 @@ class InferenceEngine:
 
     @torch.inference_mode()
     def __call__(self, audio, lengths, channels):
+        # A device-side timeout of an earlier call surfaces here (host-mapped word, no sync).
+        _lib.check_device_error()
         key = (tuple(audio.shape), audio.dtype)
         if not self.graphs or key in self.disabled_shapes:
             return self.eager(audio, lengths, channels)

@@ -71,19 +71,19 @@ constexpr int kMmaThread = 192;        // producer thread that issues MMA 1
 constexpr int kLookbackChunks = 8;     // rows with more chunks publish outgoing states
 
 // ---- shared memory --------------------------------------------------------------
-// Per slot (bytes from the slot base, 1024-aligned). The k tile and the vs hi/lo
-// tiles are read only by MMA 1; the epilogue starts after MMA 1 has completed, so
-// its P hi/lo tiles reuse the k tile and its S^T tile reuses the vs tiles.
+// Per slot (bytes from the slot base, 1024-aligned). The k and vs tiles are read
+// only by MMA 1; the epilogue starts after MMA 1 has completed, so its P hi/lo
+// tiles reuse the k tile. The S^T tile reuses the vs and v16 tiles once MMA 2
+// (the last reader of v16) has completed.
 constexpr uint32_t kSlotQ = 0;        // q16  K-major  [2 K-blocks][64 rows][128 B]
-constexpr uint32_t kSlotK = 16384;    // k16  K-major  [2 K-blocks][64 rows][128 B]
-constexpr uint32_t kSlotPH = 16384;   // P hi K-major [64 rows][128 B]   (over k16, after MMA 1)
-constexpr uint32_t kSlotPL = 24576;   // P lo                            (over k16, after MMA 1)
-constexpr uint32_t kSlotVH = 32768;   // vs hi MN-major
-constexpr uint32_t kSlotVL = 40960;   // vs lo MN-major
-constexpr uint32_t kSlotS = 32768;    // S^T MN-major [128 rows][128 B]  (over vs hi/lo, after MMA 1)
-constexpr uint32_t kSlotV = 49152;    // v16  MN-major [64 rows][128 B]
-constexpr uint32_t kSlotZ = 57344;    // z in / out staging, BF16 [64 rows][128 B]
-constexpr uint32_t kSlotBytes = 65536;
+constexpr uint32_t kSlotK = 16384;    // k~   K-major  [2 K-blocks][64 rows][128 B]
+constexpr uint32_t kSlotPH = 16384;   // P hi K-major [64 rows][128 B]   (over k~, after MMA 1)
+constexpr uint32_t kSlotPL = 24576;   // P lo                            (over k~, after MMA 1)
+constexpr uint32_t kSlotVS = 32768;   // vs   MN-major [64 rows][128 B]
+constexpr uint32_t kSlotV = 40960;    // v16  MN-major [64 rows][128 B]
+constexpr uint32_t kSlotS = 32768;    // S^T MN-major [128 rows][128 B]  (over vs and v16, after MMA 2)
+constexpr uint32_t kSlotZ = 49152;    // z in / out staging, BF16 [64 rows][128 B]
+constexpr uint32_t kSlotBytes = 57344;
 // Staging of the next unit's raw rows, filled by cp.async while the current unit
 // is prepared. Each producer thread copies and later reads back only its own
 // 16-byte chunks ([chunk][thread] order: a warp's accesses are contiguous); the
@@ -101,15 +101,17 @@ struct SlotHeader {
   int b, h, c, nv;
   int dir, teff;        // direction of the unit, valid length of its row
   float cs[kChunk];     // decay cumsum (log2 units)
-  float gamma[kChunk];
+  float g[kChunk];      // gamma_i / scale_i (0 where scale_i is 0): the D-skip term on P's diagonal
   float qe[kChunk];     // q16 row exponents
-  float ke[kChunk];     // k16 row exponents
-  float kcoef[kChunk];  // scale_j * 2^-ke_j
+  float rl[kChunk];     // log2 of P's row factor: cs_i - mu - qe_i
+  float cl[kChunk];     // log2 of P's column factor: n_j - ke_j (an integer)
+  float cf[kChunk];     // 2^cl_j (units that are not wide)
   float pe[kChunk];     // P row exponents (epilogue)
   float pmax[2][kChunk];  // per column half (epilogue)
   float theta[kRotary];
   float gtot;
   float sinv;           // 2^-(state tile exponent) (epilogue)
+  int wide;             // decay range over 180 binades: P's factors are combined per element
 };
 struct Misc {
   SlotHeader hdr[2];
@@ -117,6 +119,7 @@ struct Misc {
   float dtc[kChunk];
   float seg[8][kRotary];
   float wsum[2];
+  float csmax[2], csmin[2];  // decay cumsum range (warps 0-1)
   float ered[8];        // epilogue reductions
   int ticket;
   int next_ticket;
@@ -512,11 +515,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
         umma_f16(tm + kColD, desc_sw128(sbs + kSlotK + kk * 2048u, 8192, 1024),
-                 desc_sw128(sbs + kSlotVH + kk * 2048u, 8192, 1024), kIdState, kk > 0);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        umma_f16(tm + kColD, desc_sw128(sbs + kSlotK + kk * 2048u, 8192, 1024),
-                 desc_sw128(sbs + kSlotVL + kk * 2048u, 8192, 1024), kIdState, 1);
+                 desc_sw128(sbs + kSlotVS + kk * 2048u, 8192, 1024), kIdState, kk > 0);
       umma_commit(&mi.mma1[s]);
       mbar_arrive(&mi.ready[s]);
     };
@@ -684,14 +683,32 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         }
         if (lane == 31) mi.wsum[warp] = x;
         mi.dtc[tid] = c_dt;
-        hd.gamma[tid] = gm;
-        mi.scale[tid] = c_dn * (1.f - sigmoidf_fast(c_tn)) + gm;
+        const float scl = c_dn * (1.f - sigmoidf_fast(c_tn)) + gm;
+        mi.scale[tid] = scl;
+        hd.g[tid] = scl > 0.f ? gm * rcp_approx(scl) : 0.f;
         hd.cs[tid] = x;
       }
       if (tid == kClaimThread) mi.next_ticket = my_next;
       bar_sync_n(kBarProducer, kProducerThreads);  // also: every thread has read its staged rows
       stage_unit(mi.next_ticket);
-      if (tid >= 32 && tid < kChunk) hd.cs[tid] += mi.wsum[0];
+      if (tid < kChunk) {
+        // Final cumsum, and its range over the chunk (warps 0-1).
+        float cv = hd.cs[tid];
+        if (tid >= 32) {
+          cv += mi.wsum[0];
+          hd.cs[tid] = cv;
+        }
+        float hi = cv, lo = cv;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+          lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        }
+        if (lane == 0) {
+          mi.csmax[warp] = hi;
+          mi.csmin[warp] = lo;
+        }
+      }
       // ---- local angle phases: lane = pair r, warp = 8-step segment ------------
       float* phase = reinterpret_cast<float*>(smem + kOffPhase);
       {
@@ -722,7 +739,16 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       }
       bar_sync_n(kBarProducer, kProducerThreads);
       const float total = hd.cs[kChunk - 1];
-      // ---- rows -> FP16 operand tiles (q, k, v, vs hi/lo) and the z tile -------
+      // Decay reference of the unit: mu near the middle of the cumsum's range, with
+      // E = total - mu an integer, so that the decay-weighted values vs below are
+      // exact power-of-two multiples of v.
+      const float cmax = fmaxf(mi.csmax[0], mi.csmax[1]), cmin = fminf(mi.csmin[0], mi.csmin[1]);
+      const float Ef = rintf(total - 0.5f * (cmax + cmin));
+      const float mu = total - Ef;
+      // Over 180 binades of decay in one chunk: P's row and column factors would leave
+      // FP32's range, so the epilogue combines them per element.
+      const bool wide = cmax - cmin > 180.f;
+      // ---- rows -> FP16 operand tiles (q16, k~, vs, v16) and the z tile ------------
       {
         const float* qbh = p.qb + h * kState;
         const float* kbh = p.kb + h * kState;
@@ -755,56 +781,65 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         for (int e = 0; e < 16; ++e) vmax = fmaxf(vmax, fabsf(vf[e]));
         vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
         vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-        const float sc = mi.scale[t];
-        const float sw = row_ok ? sc * ex2_approx(total - hd.cs[t]) : 0.f;
-        // Split 2^ka between k16 = kr 2^ka (also the score operand) and
-        // vs = v scale w 2^-ka near the geometric mean of their magnitudes, but
-        // keep the k16 row maximum >= 2^-6 so the scores keep FP16's full
-        // precision; a vs row pushed below that carries a negligible state
-        // contribution. Both stay below 2^15.
-        const int kl = ilog2_or(kmax, 1000), vl = ilog2_or(vmax * sw, 1000);
-        int ka = 0;
+        // Key j's weight scale_j 2^(mu - cs_j) goes into the k row as scale_j 2^(d_j),
+        // with d_j = mu - cs_j - n_j, n_j an integer that is 0 unless |mu - cs_j| > 100
+        // (wide units); 2^(E + n_j) goes into vs. Then the state contribution is
+        //   k~_j^T vs_j = kr_j scale_j 2^(total - cs_j) v_j
+        // and the scores q16_i . k~_j carry 2^(qe_i + ke_j + d_j) besides the decay.
+        const float tj = mu - hd.cs[t];
+        const float nj = tj > 100.f ? floorf(tj - 100.f) : (tj < -100.f ? -floorf(-tj - 100.f) : 0.f);
+        const float kf0 = row_ok ? mi.scale[t] * ex2_approx(tj - nj) : 0.f;
+        // Split the remaining power of two between k~ = kr kf0 2^ke and vs = v 2^(E+n_j-ke)
+        // near the geometric mean of their magnitudes, but keep the k~ row maximum >= 2^-6
+        // so the scores keep FP16's full precision; a vs row pushed below that carries a
+        // negligible state contribution. Both stay below 2^15.
+        const int kl = ilog2_or(kmax * kf0, 1000);
+        const int vl = vmax > 0.f ? ilog2_or(vmax, 0) + static_cast<int>(Ef + nj) : 1000;
+        int ke = 0;
         if (kl != 1000) {
-          ka = vl != 1000 ? ((vl - kl) >> 1) : 14 - kl;
-          ka = max(ka, -6 - kl);
-          if (vl != 1000) ka = max(ka, vl - 14);
-          ka = min(ka, 14 - kl);
-          ka = ka < -60 ? -60 : (ka > 60 ? 60 : ka);
+          ke = vl != 1000 ? ((vl - kl) >> 1) : 14 - kl;
+          ke = max(ke, -6 - kl);
+          if (vl != 1000) ke = max(ke, vl - 14);
+          ke = min(ke, 14 - kl);
+          ke = ke < -120 ? -120 : (ke > 120 ? 120 : ke);
         }
         {
-          const float ks = exp2i(ka);
+          const float kf = kf0 * exp2i(ke);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int e0 = 32 * i + 8 * s4;
             st_shared_v4(sb + kSlotK + (e0 >> 6) * 8192u + sw128_offset(t, e0 & 63),
-                         pack_f16x2(x[8 * i] * ks, x[8 * i + 1] * ks), pack_f16x2(x[8 * i + 2] * ks, x[8 * i + 3] * ks),
-                         pack_f16x2(x[8 * i + 4] * ks, x[8 * i + 5] * ks),
-                         pack_f16x2(x[8 * i + 6] * ks, x[8 * i + 7] * ks));
+                         pack_f16x2(x[8 * i] * kf, x[8 * i + 1] * kf), pack_f16x2(x[8 * i + 2] * kf, x[8 * i + 3] * kf),
+                         pack_f16x2(x[8 * i + 4] * kf, x[8 * i + 5] * kf),
+                         pack_f16x2(x[8 * i + 6] * kf, x[8 * i + 7] * kf));
           }
-          const float vsc = sw * exp2i(-ka);
+          // vs = v 2^(E + n_j - ke): an exact power-of-two multiple of the BF16 v while it
+          // stays in FP16's normal range (zero below 2^-126 and for rows past the length).
+          const int ev = static_cast<int>(Ef + nj) - ke;
+          const float vsc = (row_ok && ev >= -126) ? exp2i(ev > 127 ? 127 : ev) : 0.f;
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const uint32_t off = sw128_offset(t, 32 * i + 8 * s4);
-            uint32_t hv[4], hh[4], hl[4];
+            uint32_t hv[4], hs[4];
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-              const float a0 = vf[8 * i + 2 * m], a1 = vf[8 * i + 2 * m + 1];
+              const float a0 = row_ok ? vf[8 * i + 2 * m] : 0.f, a1 = row_ok ? vf[8 * i + 2 * m + 1] : 0.f;
               hv[m] = pack_f16x2(a0, a1);
-              const float w0 = a0 * vsc, w1 = a1 * vsc;
-              hh[m] = pack_f16x2(w0, w1);
-              const float2 back = unpack_f16x2(hh[m]);
-              hl[m] = pack_f16x2(w0 - back.x, w1 - back.y);
+              hs[m] = pack_f16x2(a0 * vsc, a1 * vsc);
             }
             st_shared_v4(sb + kSlotV + off, hv[0], hv[1], hv[2], hv[3]);
-            st_shared_v4(sb + kSlotVH + off, hh[0], hh[1], hh[2], hh[3]);
-            st_shared_v4(sb + kSlotVL + off, hl[0], hl[1], hl[2], hl[3]);
+            st_shared_v4(sb + kSlotVS + off, hs[0], hs[1], hs[2], hs[3]);
             st_shared_v4(sb + kSlotZ + off, zraw[i].x, zraw[i].y, zraw[i].z, zraw[i].w);
           }
         }
         if (s4 == 0) {
+          // P_ij = D_ij 2^(cl_j) 2^(rl_i) for j < i, with D the score accumulator.
+          const float cl = nj - static_cast<float>(ke);
           hd.qe[t] = static_cast<float>(qe);
-          hd.ke[t] = static_cast<float>(ka);
-          hd.kcoef[t] = sc * exp2i(-ka);
+          const float rl = hd.cs[t] - mu - static_cast<float>(qe);
+          hd.rl[t] = wide ? rl : fminf(fmaxf(rl, -126.f), 126.f);  // (bounded unless q rows are extreme)
+          hd.cl[t] = cl;
+          hd.cf[t] = exp2i(cl < -126.f ? -126 : (cl > 127.f ? 127 : static_cast<int>(cl)));
         }
       }
       if (tid == 0) {
@@ -816,6 +851,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         hd.dir = dir;
         hd.teff = T_eff;
         hd.gtot = ex2_approx(total);
+        hd.wide = wide ? 1 : 0;
       }
       fence_async_smem();
       tc_fence_before();
@@ -884,83 +920,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         if (et < kRotary) reinterpret_cast<float*>(uws + kUnitTheta)[et] = hd.theta[et];
         if (et == 0) reinterpret_cast<float*>(uws + kUnitTheta)[kRotary] = hd.gtot;
       }
-      // ---- decayed scores P (+ the D-skip diagonal) -> FP16 hi/lo tiles ---------
-      {
-        float sc[16];
-        tmem_ld_16x256_x4(tmem_addr(tm, 32 * q4, kColS + 32 * chalf), sc);
-        tmem_wait_ld();
-        const float d = p.d[h];
-        const float rq0 = hd.cs[i0] - hd.qe[i0], rq1 = hd.cs[i1] - hd.qe[i1];
-        const float dg0 = exp2i(-static_cast<int>(hd.qe[i0]) - static_cast<int>(hd.ke[i0])) * hd.gamma[i0];
-        const float dg1 = exp2i(-static_cast<int>(hd.qe[i1]) - static_cast<int>(hd.ke[i1])) * hd.gamma[i1];
-        float m0 = 0.f, m1 = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int j = 32 * chalf + 8 * kk + 2 * c4 + e;
-            const float kc = hd.kcoef[j], csj = hd.cs[j];
-            float v0 = sc[4 * kk + e], v1 = sc[4 * kk + 2 + e];
-            v0 = j < i0 ? v0 * kc * ex2_approx(rq0 - csj) : (j == i0 ? d + v0 * dg0 : 0.f);
-            v1 = j < i1 ? v1 * kc * ex2_approx(rq1 - csj) : (j == i1 ? d + v1 * dg1 : 0.f);
-            sc[4 * kk + e] = v0;
-            sc[4 * kk + 2 + e] = v1;
-            m0 = fmaxf(m0, fabsf(v0));
-            m1 = fmaxf(m1, fabsf(v1));
-          }
-        }
-        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
-        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
-        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
-        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
-        if (c4 == 0) {
-          hd.pmax[chalf][i0] = m0;
-          hd.pmax[chalf][i1] = m1;
-        }
-        bar_sync_n(kBarPair + q4, 64);  // the two warps sharing this TMEM quarter
-        m0 = fmaxf(hd.pmax[0][i0], hd.pmax[1][i0]);
-        m1 = fmaxf(hd.pmax[0][i1], hd.pmax[1][i1]);
-        const int pe0 = pow2_scale_exponent(m0), pe1 = pow2_scale_exponent(m1);
-        if (chalf == 0 && c4 == 0) {
-          hd.pe[i0] = static_cast<float>(pe0);
-          hd.pe[i1] = static_cast<float>(pe1);
-        }
-        const float ps0 = exp2i(pe0), ps1 = exp2i(pe1);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int j = 32 * chalf + 8 * kk + 2 * c4;
-          const float a0 = sc[4 * kk] * ps0, a1 = sc[4 * kk + 1] * ps0;
-          const float b0 = sc[4 * kk + 2] * ps1, b1 = sc[4 * kk + 3] * ps1;
-          const uint32_t h0 = pack_f16x2(a0, a1), h1 = pack_f16x2(b0, b1);
-          const float2 f0 = unpack_f16x2(h0), f1 = unpack_f16x2(h1);
-          st_shared_u32(sb + kSlotPH + sw128_offset(i0, j), h0);
-          st_shared_u32(sb + kSlotPH + sw128_offset(i1, j), h1);
-          st_shared_u32(sb + kSlotPL + sw128_offset(i0, j), pack_f16x2(a0 - f0.x, a1 - f0.y));
-          st_shared_u32(sb + kSlotPL + sw128_offset(i1, j), pack_f16x2(b0 - f1.x, b1 - f1.y));
-        }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      bar_sync_n(kBarEpilogue, kEpilogueThreads);
-      if (et == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tm + kColPV, desc_sw128(sb + kSlotPH + kk * 32u, 0, 1024),
-                   desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tm + kColPV, desc_sw128(sb + kSlotPL + kk * 32u, 0, 1024),
-                   desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, 1);
-        umma_commit(&mi.mma2[slot]);
-      }
-      // Publish dS (a thread of warp 15, in parallel with warp 8's MMA issue). Every
-      // epilogue thread's export stores precede the barrier above, and a release after
-      // a CTA barrier is cumulative over them, so one thread's gpu-scope release
-      // orders the whole export before the flag.
-      if (et == kEpilogueThreads - 32 && !last())
-        st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
-      // ---- fold the predecessors' state contributions (row n, 32-column half) ---
+      // ---- helpers of the state fold (row n, this thread's 32-column half) ----------
       // One step: st = R(-theta) (g st + dS), dS from a published unit.
       auto fold_step = [&](float (&st)[32], const uint4 (&w)[4], float f, float gx, float th) {
 #pragma unroll
@@ -1015,10 +975,12 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         gx = __ldcg(reinterpret_cast<const float*>(xws + kUnitTheta) + kRotary);
         th = __ldcg(reinterpret_cast<const float*>(xws + kUnitTheta) + ((n >> 1) & 31u));
       };
-      if (c > 0) {
-        float st[32];
+      // The state entering chunk c (c > 0): predecessors' contributions folded from the
+      // nearest published outgoing state (look-back rows) or from chunk 0.
+      float st[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) st[j] = 0.f;
+      for (int j = 0; j < 32; ++j) st[j] = 0.f;
+      auto fold_predecessors = [&]() {
         int start = 0;
         if (lookback) {
           // Nearest predecessor with a published outgoing state (one thread decides).
@@ -1049,8 +1011,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
             }
             start = y + 1;
           }
-        }
-        if (!lookback) {
+        } else {
           // Short rows: lane l of every warp waits for predecessor l's dS flag.
           for (int x = lane; x < c; x += 32) {
             uint32_t seen = 0;
@@ -1075,15 +1036,19 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
             ta = tb;
           }
         }
-        // FP16 S^T tile with one power-of-two exponent: this thread's part of the maximum.
-        float m = 0.f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(st[j]));
-        m = warp_max(m);
-        if (lane == 0) mi.ered[warp - 8] = m;
-        // Outgoing state S(c+1) = R(-theta_c) (2^total_c S(c) + dS_c) for look-back, published
-        // before the S tile is built: successors along the row wait for it.
-        if (lookback && !last()) {
+      };
+      if (lookback) {
+        // Rows of many chunks: the chain of outgoing states along the row sets the
+        // launch's time, so this unit's link in it (dS flag, fold, outgoing state)
+        // comes before its own output work. Every epilogue thread's export stores
+        // precede this barrier, and a release after a CTA barrier is cumulative over
+        // them, so one thread's gpu-scope release orders the whole export before the flag.
+        bar_sync_n(kBarEpilogue, kEpilogueThreads);
+        if (et == kEpilogueThreads - 32 && !last())
+          st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
+        if (c > 0) fold_predecessors();
+        if (!last()) {
+          // Outgoing state S(c+1) = R(-theta_c) (2^total_c S(c) + dS_c).
           float so[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) so[j] = st[j];
@@ -1095,10 +1060,117 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(so[4 * q], so[4 * q + 1], so[4 * q + 2], so[4 * q + 3]);
+          bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the release below is cumulative over these stores
+          if (et == 0) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
         }
-        bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the maxima, and the outgoing-state stores
-        if (lookback && !last() && et == 0)  // cumulative over every thread's stores before the barrier
-          st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
+      }
+      // ---- decayed scores P (+ the D-skip diagonal) -> FP16 hi/lo tiles ---------
+      // P_ij = D_ij 2^(cl_j) 2^(rl_i) for j < i (D the score accumulator: the decay is
+      // split between the k~ rows and these factors), d + P_ii g_i on the diagonal.
+      {
+        // Warps whose 16 rows (< 32) all lie above their 32 columns (>= 32) hold zeros.
+        const bool upper = q4 < 2 && chalf == 1;
+        float sc[16];
+        float m0 = 0.f, m1 = 0.f;
+        if (!upper) {
+          tmem_ld_16x256_x4(tmem_addr(tm, 32 * q4, kColS + 32 * chalf), sc);
+          tmem_wait_ld();
+          const float d = p.d[h];
+          const float g0 = hd.g[i0], g1 = hd.g[i1];
+          const float rl0 = hd.rl[i0], rl1 = hd.rl[i1];
+          const bool wide_u = hd.wide != 0;
+          const float r0 = ex2_approx(rl0), r1 = ex2_approx(rl1);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int j = 32 * chalf + 8 * kk + 2 * c4 + e;
+              float v0 = sc[4 * kk + e], v1 = sc[4 * kk + 2 + e];
+              if (!wide_u) {
+                const float cf = hd.cf[j];
+                v0 = (v0 * cf) * r0;
+                v1 = (v1 * cf) * r1;
+              } else {
+                const float cl = hd.cl[j];
+                v0 *= ex2_approx(rl0 + cl);
+                v1 *= ex2_approx(rl1 + cl);
+              }
+              v0 = j < i0 ? v0 : (j == i0 ? fmaf(v0, g0, d) : 0.f);
+              v1 = j < i1 ? v1 : (j == i1 ? fmaf(v1, g1, d) : 0.f);
+              sc[4 * kk + e] = v0;
+              sc[4 * kk + 2 + e] = v1;
+              m0 = fmaxf(m0, fabsf(v0));
+              m1 = fmaxf(m1, fabsf(v1));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) sc[e] = 0.f;
+        }
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+        if (c4 == 0) {
+          hd.pmax[chalf][i0] = m0;
+          hd.pmax[chalf][i1] = m1;
+        }
+        bar_sync_n(kBarPair + q4, 64);  // the two warps sharing this TMEM quarter
+        m0 = fmaxf(hd.pmax[0][i0], hd.pmax[1][i0]);
+        m1 = fmaxf(hd.pmax[0][i1], hd.pmax[1][i1]);
+        const int pe0 = pow2_scale_exponent(m0), pe1 = pow2_scale_exponent(m1);
+        if (chalf == 0 && c4 == 0) {
+          hd.pe[i0] = static_cast<float>(pe0);
+          hd.pe[i1] = static_cast<float>(pe1);
+        }
+        const float ps0 = exp2i(pe0), ps1 = exp2i(pe1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int j = 32 * chalf + 8 * kk + 2 * c4;
+          const float a0 = sc[4 * kk] * ps0, a1 = sc[4 * kk + 1] * ps0;
+          const float b0 = sc[4 * kk + 2] * ps1, b1 = sc[4 * kk + 3] * ps1;
+          const uint32_t h0 = pack_f16x2(a0, a1), h1 = pack_f16x2(b0, b1);
+          const float2 f0 = unpack_f16x2(h0), f1 = unpack_f16x2(h1);
+          st_shared_u32(sb + kSlotPH + sw128_offset(i0, j), h0);
+          st_shared_u32(sb + kSlotPH + sw128_offset(i1, j), h1);
+          st_shared_u32(sb + kSlotPL + sw128_offset(i0, j), pack_f16x2(a0 - f0.x, a1 - f0.y));
+          st_shared_u32(sb + kSlotPL + sw128_offset(i1, j), pack_f16x2(b0 - f1.x, b1 - f1.y));
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      bar_sync_n(kBarEpilogue, kEpilogueThreads);
+      if (et == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tm + kColPV, desc_sw128(sb + kSlotPH + kk * 32u, 0, 1024),
+                   desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tm + kColPV, desc_sw128(sb + kSlotPL + kk * 32u, 0, 1024),
+                   desc_sw128(sb + kSlotV + kk * 2048u, 8192, 1024), kIdPV, 1);
+        umma_commit(&mi.mma2[slot]);
+      }
+      if (!lookback) {
+        // Publish dS (a thread of warp 15, in parallel with warp 8's MMA issue). Every
+        // epilogue thread's export stores precede the barrier above, and a release
+        // after a CTA barrier is cumulative over them, so one thread's gpu-scope
+        // release orders the whole export before the flag.
+        if (et == kEpilogueThreads - 32 && !last())
+          st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagAgg);
+        if (c > 0) fold_predecessors();
+      }
+      if (c > 0) {
+        // FP16 S^T tile with one power-of-two exponent: this thread's part of the maximum.
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(st[j]));
+        m = warp_max(m);
+        if (lane == 0) mi.ered[warp - 8] = m;
+        // The S^T tile overwrites vs and v16: MMA 2, the last reader of v16, must be done.
+        ok &= mbar_wait(&mi.mma2[slot], ph);
+        bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the maxima
 #pragma unroll
         for (int w8 = 0; w8 < 8; ++w8) m = fmaxf(m, mi.ered[w8]);
         const int se = pow2_scale_exponent(m);
@@ -1124,22 +1196,6 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         }
       } else {
         if (et == 0) mbar_arrive(&mi.mma3[slot]);  // no inter-chunk MMA; keep the phase in step
-        if (lookback && !last()) {
-          // Chunk 0: its outgoing state is R(-theta_0) dS_0.
-          float st[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) st[j] = 0.f;
-          uint4 w[4];
-          float f;
-          own_ds(w, f);
-          fold_step(st, w, f, 1.f, hd.theta[(n >> 1) & 31u]);
-          float* incl = reinterpret_cast<float*>(uws + kUnitIncl) + n * 64 + 32 * chalf;
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(incl + 4 * q) = make_float4(st[4 * q], st[4 * q + 1], st[4 * q + 2], st[4 * q + 3]);
-          bar_sync_n(kBarEpilogue, kEpilogueThreads);  // the release below is cumulative over these stores
-          if (et == 0) st_release_u32(reinterpret_cast<uint32_t*>(uws + kUnitFlag), epoch + kFlagIncl);
-        }
       }
       // ---- output: combine, gate, stage in the z tile, coalesced stores ----------
       ok &= mbar_wait(&mi.mma2[slot], ph);

@@ -1,7 +1,6 @@
 // Thin wrappers over the sm_100a PTX used by the tensor-core kernels:
 // mbarriers, 5th-generation tensor-core MMA (tcgen05) with tensor-memory
-// accumulators, tensor-memory loads, UMMA shared-memory descriptors, and
-// cluster (distributed shared memory) access.
+// accumulators, tensor-memory loads and UMMA shared-memory descriptors.
 #pragma once
 
 #include "tf_common.cuh"
@@ -135,44 +134,6 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // chunk index XORed with (row % 8).
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
   return (row >> 3) * 1024u + (row & 7u) * 128u + ((((col >> 3) ^ row) & 7u) << 4) + (col & 7u) * 2u;
-}
-
-// ---- clusters ----------------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_shared(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-// Remote shared-memory loads. No "memory" clobber: ordering against the
-// producer's writes comes from the cluster barrier (itself a compiler fence),
-// and leaving these unordered lets independent loads be issued back to back.
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared::cluster.v4.b32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
 }
 
 }  // namespace sm100

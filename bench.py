@@ -15,6 +15,11 @@ replays, each step on the next of S input sets whose total size exceeds the
 stream; the max over ranks is reported. Under torchrun every rank runs its own
 batch (weak scaling; no collective on the data path).
 
+The default line also carries ``box``: the box-level sweep of the metric's
+audio-seconds/s (1024 synthetic clips through ``InferenceEngine(graphs=True)``,
+batches partitioned over the ranks, one logits all-gather; strong scaling), so a
+run at N = 1, 2, 4, 8 GPUs measures both halves of the metric (``--no-box`` skips it).
+
 ``--impl reference`` times the reference's arithmetic on the host CPU (the
 oracle port under ``oracle/``, all host threads) on the same workload.
 """
@@ -58,6 +63,8 @@ AUDIO_METRIC_UNIT = "audio-sec/s"
 BENCH_RESERVED_GIB = 64.0
 # Default timed steps: each bounded to well under a minute of GPU time.
 DEFAULT_STEPS = {"cfg1": 20000, "cfg2": 20000, "cfg3": 200, "cfg4": 3}
+# Sweeps timed by the box sub-record of the default line.
+BOX_STEPS = 3
 
 
 def parse():
@@ -71,6 +78,8 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-box", action="store_true",
+                    help="cfg1: skip the box-level audio-seconds/s sweep (cfg4) recorded under 'box'")
     ap.add_argument("--profile-eager", type=int, default=0, metavar="K",
                     help="model workloads: run K untimed eager forwards and exit (for ncu launch lists)")
     args = ap.parse_args()
@@ -460,9 +469,14 @@ def run_recurrence(args, wl):
         cpu = {"value": b * t * n / el, "unit": "tokens/s", "cores": host_threads(), "torch_threads": _torch_threads(), "kind": "port",
                "sample": f"{n} full {args.workload} batches through the numpy oracle (FP32), {el:.1f} s"}
 
+    box = None
+    if args.workload == "cfg1" and not args.no_box:
+        # The box-level sweep of the metric's audio-seconds/s (cfg4), on the same ranks:
+        # strong scaling over the ranks, one logits all-gather.
+        del graph, tail, warm_graph
+        box = box_sweep(WORKLOADS["cfg4"], BOX_STEPS, 1, world, rank, local, dev)
     if world > 1:
         dist.barrier()
-        del graph, tail, warm_graph
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -490,6 +504,8 @@ def run_recurrence(args, wl):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if box is not None:
+        line["box"] = dict(workload="cfg4", scaling="strong", **box)
     print(json.dumps(line), flush=True)
 
 
@@ -615,14 +631,14 @@ def run_model(args, wl):
     print(json.dumps(line), flush=True)
 
 
-def run_box(args, wl):
-    """cfg4: 1024 clips bucketed by (channels, length) into batches of up to 32,
-    partitioned over the ranks longest-processing-time first; one step = every
-    rank runs all of its batches through its ``InferenceEngine(graphs=True)``
-    (one graph per batch shape, captured during warm-up) and the logits are
-    all-gathered once. ``value`` = total audio-seconds / step time (max over
-    ranks); inputs are device-resident for ``value`` and copied from pinned
-    host memory batch by batch for ``e2e``."""
+def box_sweep(wl, steps, warmup, world, rank, local, dev):
+    """The cfg4 box sweep on an initialised rank: 1024 clips bucketed by (channels,
+    length) into batches of up to 32, partitioned over the ranks longest-processing-time
+    first; one step = every rank runs all of its batches through its
+    ``InferenceEngine(graphs=True)`` (one graph per batch shape, captured during
+    warm-up) and the logits are all-gathered once. Returns the measurements (max over
+    ranks); inputs are device-resident for ``value`` and copied from pinned host memory
+    batch by batch for ``e2e``."""
     import tempfile
 
     import torch
@@ -632,7 +648,6 @@ def run_box(args, wl):
     from trifusion_b200.sharding import batch_cost, gather_logits, lpt_partition
     from trifusion_b200.synthetic import batch_audio, clip_set
 
-    world, rank, local, dev = setup_dist()
     configure_runtime()
     records = clip_set(wl["clips"], seed=0)
     plan = plan_batches(records, padded_seconds=wl["padded_seconds"], max_batch=wl["max_batch"])
@@ -659,7 +674,7 @@ def run_box(args, wl):
             return gather_logits(indices, local_logits, capacity=capacity)
         return indices, local_logits
 
-    for _ in range(max(args.warmup, 1)):
+    for _ in range(max(warmup, 1)):
         sweep(dev_in)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -668,7 +683,7 @@ def run_box(args, wl):
     sampler.start()
     tl0 = time.time()
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
+              for _ in range(steps)]
     for e0, e1 in events:
         e0.record(stream)
         idx, logits = sweep(dev_in)
@@ -677,7 +692,7 @@ def run_box(args, wl):
     tw1 = time.time()
     sampler.stop()
     ms = max_over_ranks(sum(a.elapsed_time(c) for a, c in events), world, dev)
-    ms_per_step = ms / max(args.steps, 1)
+    ms_per_step = ms / max(steps, 1)
     assert idx.numel() == len(records) and bool(torch.isfinite(logits).all())
 
     h2d = sum(x.numel() * x.element_size() for h in host for x in h)
@@ -701,27 +716,41 @@ def run_box(args, wl):
     e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     if world > 1:
         dist.barrier()
-        engine.clear()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    line = {
-        "metric": METRIC, "value": total_audio_s / (ms_per_step / 1e3), "unit": AUDIO_METRIC_UNIT,
-        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 1),
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (random-init student, 1024 PCM16-quantised noise clips)",
-        "config": {"workload": args.workload, "student": STUDENT, "clips": len(records),
-                   "audio_seconds": total_audio_s, "batches": len(plan),
-                   "batches_on_rank0": len(mine), "graph_shapes_on_rank0": len(shapes),
+    engine.clear()
+    return {
+        "value": total_audio_s / (ms_per_step / 1e3), "unit": AUDIO_METRIC_UNIT, "steps": steps,
+        "warmup": max(warmup, 1), "ms_per_step": ms_per_step,
+        "config": {"student": STUDENT, "clips": len(records), "audio_seconds": total_audio_s,
+                   "batches": len(plan), "batches_on_rank0": len(mine) if rank == 0 else None,
+                   "graph_shapes_on_rank0": len(shapes) if rank == 0 else None,
                    "max_batch": wl["max_batch"], "padded_seconds_per_batch": wl["padded_seconds"],
                    "step": "all batches through InferenceEngine(graphs=True) + one logits all-gather",
                    "l2": "inputs larger than L2 (the sweep streams all batches)",
                    "parallelism": f"data-parallel x{world}, LPT partition by padded audio-seconds"},
-        "roofline": None,
         "e2e": {"value": total_audio_s / (e_ms / 1e3), "unit": AUDIO_METRIC_UNIT,
                 "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": len(records) * 5 * 4},
         "clocks": sampler.summary(tl0, tw1),
+    }
+
+
+def run_box(args, wl):
+    """cfg4 as its own bench line (see ``box_sweep``)."""
+    import torch.distributed as dist
+
+    world, rank, local, dev = setup_dist()
+    res = box_sweep(wl, args.steps, args.warmup, world, rank, local, dev)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": AUDIO_METRIC_UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": res["warmup"],
+        "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init student, 1024 PCM16-quantised noise clips)",
+        "config": dict(workload=args.workload, **res["config"]),
+        "roofline": None, "e2e": res["e2e"], "clocks": res["clocks"],
     }
     print(json.dumps(line), flush=True)
 

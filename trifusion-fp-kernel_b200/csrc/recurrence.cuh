@@ -2,11 +2,19 @@
 // the C-ABI launcher).
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (a plain 128-byte descriptor; no driver-library linking)
+
 #include "tf_common.cuh"
 
 namespace tf {
 
-struct RecurrenceParams {
+struct alignas(64) RecurrenceParams {
+  // Set by the launcher when every row of q, k, v, z and the angles is 16-byte
+  // aligned with 16-byte strides: the producer stages a unit's rows with these
+  // tensor maps (TMA) instead of per-thread cp.async. Boxes of 64 time steps.
+  CUtensorMap tm_q, tm_k, tm_v, tm_z, tm_a;
+  int tma;
+
   const bf16* q;       // [B,T,Hq,128]
   const bf16* k;       // [B,T,Hq,128]
   const bf16* v;       // [B,T,H,64]

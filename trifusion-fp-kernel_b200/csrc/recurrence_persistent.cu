@@ -53,6 +53,8 @@
 #include <cstdio>
 
 #include "../../include/trifusion_b200.h"
+#include <cudaTypedefs.h>
+
 #include "recurrence.cuh"
 #include "sm100.cuh"
 #include "tf_host.cuh"
@@ -90,6 +92,10 @@ constexpr uint32_t kSlotBytes = 57344;
 // angle rows ([64][32] BF16) are read across threads after a barrier.
 constexpr uint32_t kOffStage = 2 * kSlotBytes;
 constexpr uint32_t kStQ = 0, kStK = 16384, kStV = 32768, kStZ = 40960, kStA = 49152, kStageBytes = 53248;
+// With TMA staging the same regions hold boxes of 64 time steps in time order:
+// q and k as two [64][128 B] 128B-swizzled boxes (columns 0-63, 64-127), v and z as
+// one each, the angles as [64][64 B]; all 53248 bytes arrive on one mbarrier.
+constexpr uint32_t kStageTmaBytes = 53248;
 // Producer scratch and barriers after the staging area.
 constexpr uint32_t kOffPhase = kOffStage + kStageBytes;  // FP32 [64][33]
 constexpr uint32_t kOffTeff = kOffPhase + 64 * 33 * 4;   // int [2][kTeffTable]: valid length of every row
@@ -128,6 +134,7 @@ struct Misc {
   uint32_t epoch;
   uint32_t tmem_base;
   uint64_t ready[2], freed[2], mma1[2], mma2[2], mma3[2];
+  uint64_t staged;  // TMA staging of the next unit's rows
 };
 constexpr uint32_t kSmemBytes = kOffMisc + sizeof(Misc) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory beyond the 227 KB a B200 CTA may use");
@@ -391,7 +398,9 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, 
 // kDirs: directions in the launch (1 or 2), a compile-time constant so that a
 // one-direction launch reads its parameters at fixed offsets. kExt: reversed
 // rows and in-launch controls are possible (otherwise compiled out).
-template <int kVec, int kDirs, bool kExt, bool kLook>
+// kTma: the unit's rows are staged by TMA boxes (16-byte rows whose tensor maps the
+// launcher could encode); otherwise by per-thread cp.async (or read directly).
+template <int kVec, int kDirs, bool kExt, bool kLook, bool kTma>
 __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, const RecurrenceParams& pd1,
                                                 unsigned char* ws) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -428,6 +437,17 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
     tmem_alloc(&mi.tmem_base, kTmemCols);
     tmem_relinquish();
   }
+  if (kTma && tid == kClaimThread) {
+#pragma unroll
+    for (int d = 0; d < kDirs; ++d) {
+      const RecurrenceParams& pp = d == 0 ? pd0 : pd1;
+      prefetch_tensormap(&pp.tm_q);
+      prefetch_tensormap(&pp.tm_k);
+      prefetch_tensormap(&pp.tm_v);
+      prefetch_tensormap(&pp.tm_z);
+      prefetch_tensormap(&pp.tm_a);
+    }
+  }
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&mi.ready[s], 1);
@@ -436,6 +456,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       mbar_init(&mi.mma2[s], 1);
       mbar_init(&mi.mma3[s], 1);
     }
+    mbar_init(&mi.staged, 1);
     fence_mbar_init();
     // The first unit's ticket, claimed now so its round trip overlaps the epoch
     // and length loads (the previous launch reset the counter before it ended).
@@ -457,6 +478,8 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
     constexpr bool kStage = kVec >= 8;     // rows aligned for 8/16-byte cp.async
     const uint32_t stage = base + kOffStage;
     // Stage unit un's q/k/v/z rows (this thread's chunks) and angle rows.
+    bool tma_pending = false;  // TMA boxes of a staged unit in flight on mi.staged
+    uint32_t tma_phase = 0;
     auto stage_unit = [&](int un) {
       if constexpr (kStage) {
         if (un >= shp.units) return;
@@ -468,6 +491,26 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         const int nvn = max(0, min(kChunk, te - nc * kChunk));
         if (nvn == 0) return;
         const bool rv = kExt && pn.reverse != 0;
+        if constexpr (kTma) {
+          // One thread issues the unit's boxes: 64 time steps starting at the chunk's
+          // first step, or (reversed rows) at len - 64 - c0, read in reverse below.
+          // Steps before 0 or past T read as zeros.
+          if (tid == kClaimThread) {
+            const int row0 = rv ? te - kChunk - nc * kChunk : nc * kChunk;
+            const int hq = nh / (pn.H / pn.Hq);
+            fence_async_smem();  // the previous unit's rows were read through the generic proxy
+            mbar_arrive_expect_tx(&mi.staged, kStageTmaBytes);
+            tma_load_4d(stage + kStQ, &pn.tm_q, &mi.staged, 0, hq, row0, nb);
+            tma_load_4d(stage + kStQ + 8192u, &pn.tm_q, &mi.staged, 64, hq, row0, nb);
+            tma_load_4d(stage + kStK, &pn.tm_k, &mi.staged, 0, hq, row0, nb);
+            tma_load_4d(stage + kStK + 8192u, &pn.tm_k, &mi.staged, 64, hq, row0, nb);
+            tma_load_4d(stage + kStV, &pn.tm_v, &mi.staged, 0, nh, row0, nb);
+            tma_load_4d(stage + kStZ, &pn.tm_z, &mi.staged, 0, nh, row0, nb);
+            tma_load_4d(stage + kStA, &pn.tm_a, &mi.staged, 0, pn.sa[2] == 0 ? 0 : nh, row0, nb);
+          }
+          tma_pending = true;
+          return;
+        }
         const bool valid = t < nvn;
         const int64_t x = static_cast<int64_t>(nc) * kChunk + t;
         const int64_t pos = valid ? (rv ? te - 1 - x : x) : 0;
@@ -542,6 +585,13 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
     stage_unit(mi.next_ticket);
     for (;;) {
       if constexpr (kStage) cp_async_wait_all();
+      if constexpr (kTma) {
+        if (tma_pending) {
+          ok &= mbar_spin(&mi.staged, tma_phase);
+          tma_phase ^= 1u;
+          tma_pending = false;
+        }
+      }
       bar_sync_n(kBarProducer, kProducerThreads);  // staged rows and the ticket are visible
       const int u = mi.next_ticket;
       bar_sync_n(kBarProducer, kProducerThreads);  // everyone has read the ticket
@@ -589,7 +639,30 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       auto src_row = [&](int64_t x) -> int64_t { return rev ? (T_eff - 1 - x) : x; };
       // ---- loads ------------------------------------------------------------------
       uint4 qraw[4], kraw[4], vraw[2], zraw[2];
-      if constexpr (kStage) {
+      constexpr bool tma_rows = kTma;
+      if constexpr (tma_rows) {
+        // Boxes in time order: local step t is box row t, or 63 - t for reversed rows.
+        const int r = rev ? kChunk - 1 - t : t;
+        const uint32_t off0 = r * 128u + (((s4 ^ r) & 7u) << 4), off1 = r * 128u + ((((4 + s4) ^ r) & 7u) << 4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t off = (i >> 1) * 8192u + ((i & 1) ? off1 : off0);
+          qraw[i] = ld_shared_v4(stage + kStQ + off);
+          kraw[i] = ld_shared_v4(stage + kStK + off);
+        }
+        vraw[0] = ld_shared_v4(stage + kStV + off0);
+        vraw[1] = ld_shared_v4(stage + kStV + off1);
+        zraw[0] = ld_shared_v4(stage + kStZ + off0);
+        zraw[1] = ld_shared_v4(stage + kStZ + off1);
+        if (nv < kChunk && !row_ok) {
+          // A row's last chunk: the boxes hold whatever lies past the length; use zeros
+          // (as the reference's masked loads do).
+          const uint4 zero = make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) qraw[i] = kraw[i] = zero;
+          vraw[0] = vraw[1] = zraw[0] = zraw[1] = zero;
+        }
+      } else if constexpr (kStage) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           qraw[i] = ld_shared_v4(stage + kStQ + i * 4096u + tid * 16u);
@@ -657,7 +730,13 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         }
       }
       float araw[8];
-      if (kStage && p.ang_vec) {
+      if (tma_rows) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int tt = warp * 8 + i, ra = rev ? kChunk - 1 - tt : tt;
+          araw[i] = tt < nv ? __uint_as_float(ld_shared_u16(stage + kStA + ra * 64u + lane * 2u) << 16) : 0.f;
+        }
+      } else if (kStage && p.ang_vec) {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           araw[i] = __uint_as_float(ld_shared_u16(stage + kStA + (warp * 8 + i) * 64u + lane * 2u) << 16);
@@ -1274,17 +1353,17 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
 
 // One direction: a single parameter block (the launch copies less). kLook: rows
 // of more than kLookbackChunks chunks (outgoing states and look-back compiled in).
-template <int kVec, bool kExt, bool kLook>
+template <int kVec, bool kExt, bool kLook, bool kTma>
 __global__ void __launch_bounds__(kThreads, 1) recurrence_persistent_kernel(const __grid_constant__ RecurrenceParams p,
                                                                               unsigned char* ws) {
-  recurrence_body<kVec, 1, kExt, kLook>(p, p, ws);
+  recurrence_body<kVec, 1, kExt, kLook, kTma>(p, p, ws);
 }
 // Both directions of a bidirectional pair in one launch.
-template <int kVec, bool kLook>
+template <int kVec, bool kLook, bool kTma>
 __global__ void __launch_bounds__(kThreads, 1) recurrence_pair_kernel(const __grid_constant__ RecurrenceParams p0,
                                                                         const __grid_constant__ RecurrenceParams p1,
                                                                         unsigned char* ws) {
-  recurrence_body<kVec, 2, true, kLook>(p0, p1, ws);
+  recurrence_body<kVec, 2, true, kLook, kTma>(p0, p1, ws);
 }
 
 int alignment_class_one(const RecurrenceParams& p) {
@@ -1325,24 +1404,79 @@ int angles_vectorizable(const RecurrenceParams& p) {
   return 1;
 }
 
+// ---- tensor maps for the TMA staging of a unit's rows --------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+int g_encode_state = 0;  // 0: not looked up, 1: available, 2: unavailable
+
+bool encode_available() {
+  if (g_encode_state == 0) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess && fn) {
+      g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      g_encode_state = 1;
+    } else {
+      (void)cudaGetLastError();
+      g_encode_state = 2;
+    }
+  }
+  return g_encode_state == 1;
+}
+
+// A [B, T, M, width] BF16 tensor (element strides s0 batch, s1 time, s2 middle;
+// innermost contiguous) as a 4-D map {width, M, T, B} with boxes of
+// {min(width, 64), 1, 64, 1}: 64 consecutive time steps of one (batch, middle)
+// row as [64][box width] in shared memory, 128-byte swizzled when the box is
+// 128 bytes wide. Middle stride 0 (heads sharing the angles) is described as a
+// middle dimension of extent 1.
+bool encode_rows(CUtensorMap* map, const bf16* base, int width, int T, int M, int B, int64_t s0, int64_t s1,
+                 int64_t s2) {
+  if (s2 == 0) M = 1;
+  const int64_t st2 = s2 == 0 ? width : s2;
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (st2 * 2) % 16 || (s1 * 2) % 16 || (s0 * 2) % 16) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(T),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st2 * 2), static_cast<cuuint64_t>(s1 * 2),
+                                 static_cast<cuuint64_t>(s0 * 2)};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(width > 64 ? 64 : width), 1, kChunk, 1};
+  const cuuint32_t elem[4] = {1, 1, 1, 1};
+  const bool sw = width >= 64;
+  return g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<bf16*>(base), dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor maps of one direction; false (the launch then stages with cp.async) when a
+// tensor's layout does not allow them.
+bool encode_direction(RecurrenceParams& p) {
+  if (!encode_available() || p.sa[3] != 1) return false;
+  return encode_rows(&p.tm_q, p.q, kState, p.T, p.Hq, p.B, p.sq[0], p.sq[1], p.sq[2]) &&
+         encode_rows(&p.tm_k, p.k, kState, p.T, p.Hq, p.B, p.sk[0], p.sk[1], p.sk[2]) &&
+         encode_rows(&p.tm_v, p.v, kHead, p.T, p.H, p.B, p.sv[0], p.sv[1], p.sv[2]) &&
+         encode_rows(&p.tm_z, p.z, kHead, p.T, p.H, p.B, p.sz[0], p.sz[1], p.sz[2]) &&
+         encode_rows(&p.tm_a, p.ang, kRotary, p.T, p.H, p.B, p.sa[0], p.sa[1], p.sa[2]);
+}
+
 int alignment_class(const RecurrenceLaunch& L) {
   int a = alignment_class_one(L.dir[0]);
   if (L.ndir > 1) a = a < alignment_class_one(L.dir[1]) ? a : alignment_class_one(L.dir[1]);
   return a;
 }
 
-template <int kVec, int kDirs, bool kExt>
+template <int kVec, int kDirs, bool kExt, bool kTma = false>
 int launch(const RecurrenceLaunch& L, unsigned char* ws, cudaStream_t stream) {
   const RecurrenceParams& p = L.dir[0];
   const int units = ((p.T + kChunk - 1) / kChunk) * p.B * p.H * L.ndir;
   const int grid = units < sm_count() ? units : sm_count();
   const bool look = (p.T + kChunk - 1) / kChunk > kLookbackChunks;
   if constexpr (kDirs == 2) {
-    auto kernel = look ? recurrence_pair_kernel<kVec, true> : recurrence_pair_kernel<kVec, false>;
+    auto kernel = look ? recurrence_pair_kernel<kVec, true, kTma> : recurrence_pair_kernel<kVec, false, kTma>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(L.dir[0], L.dir[1], ws);
   } else {
-    auto kernel = look ? recurrence_persistent_kernel<kVec, kExt, true> : recurrence_persistent_kernel<kVec, kExt, false>;
+    auto kernel = look ? recurrence_persistent_kernel<kVec, kExt, true, kTma>
+                       : recurrence_persistent_kernel<kVec, kExt, false, kTma>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(L.dir[0], ws);
   }
@@ -1369,8 +1503,19 @@ int launch_recurrence_persistent(const RecurrenceLaunch& launch_in, void* worksp
   if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H, L.ndir)) return 1;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   const int a = alignment_class(L);
+  // TMA staging for 16-byte rows of long rows (more than kLookbackChunks chunks), when
+  // every direction's tensors allow it: there it measured faster than per-thread
+  // cp.async (137.3 against 138.2 us at B=2, T=3600); for short rows cp.async is
+  // faster (41.8 against 43.7 us at B=16, T=200), where the first unit's rows are on
+  // the launch's critical path.
+  bool tma = a == 16 && (p.T + kChunk - 1) / kChunk > kLookbackChunks;
+  for (int i = 0; i < L.ndir && tma; ++i) tma = encode_direction(L.dir[i]);
+  for (int i = 0; i < L.ndir; ++i) L.dir[i].tma = tma ? 1 : 0;
   bool ext = false;
   for (int i = 0; i < L.ndir; ++i) ext = ext || L.dir[i].reverse || L.dir[i].raw_controls;
+  if (tma)
+    return L.ndir == 2 ? launch<16, 2, true, true>(L, ws, stream)
+                       : ext ? launch<16, 1, true, true>(L, ws, stream) : launch<16, 1, false, true>(L, ws, stream);
   if (L.ndir == 2)
     return a == 16 ? launch<16, 2, true>(L, ws, stream)
                    : a == 8 ? launch<8, 2, true>(L, ws, stream) : launch<2, 2, true>(L, ws, stream);

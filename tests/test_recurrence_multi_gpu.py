@@ -12,6 +12,7 @@
 import pytest
 import torch
 
+from oracle import mamba_oracle as O
 from parity import assert_recurrence_close, oracle_out
 
 pytestmark = pytest.mark.gpu
@@ -192,3 +193,41 @@ def test_pair_rows_side_by_side_and_paired_mean():
         d = fwd._direction(pf, 3, 150)
         d["out"] = torch.empty(3, 150, 12, 32, dtype=torch.bfloat16, device="cuda")
         fused_recurrence_multi([d], lengths=lengths)
+
+
+def _aligned_views(p, pitch, offset):
+    """The projection's values in a wider buffer: rows `pitch` elements apart, starting
+    `offset` elements in (pitch 1864, offset 0: 16-byte rows; 1868, 4: 8-byte rows)."""
+    b, t, w = p.shape
+    buf = torch.zeros(b, t, pitch, dtype=p.dtype, device=p.device)
+    buf[..., offset:offset + w] = p
+    return buf[..., offset:offset + w]
+
+
+@pytest.mark.parametrize("mode", ["forward", "reversed", "pair"])
+def test_tma_staging_equals_cp_async_staging(mode):
+    """Rows of more than 8 chunks with 16-byte rows are staged by TMA boxes; the same
+    values in 8-byte-aligned rows by per-thread cp.async. Same arithmetic: equal bits."""
+    b, t = 3, 700
+    lengths = torch.tensor([700, 451, 64], device=DEV)
+    p = projection(b, t, 21)
+    prm = params(22)
+    outs = []
+    for pitch, offset in ((1864, 0), (1868, 4)):
+        pv = _aligned_views(p, pitch, offset)
+        dirs = {"forward": [direction(pv, b, t, prm)], "reversed": [direction(pv, b, t, prm, reverse=True)],
+                "pair": [direction(pv, b, t, prm), direction(pv, b, t, prm, reverse=True)]}[mode]
+        outs.append(fused_recurrence_multi(dirs, lengths=lengths))
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
+
+
+def test_tma_staged_long_rows_against_oracle():
+    from trifusion_b200.synthetic import recurrence_inputs
+
+    b, t = 2, 1100
+    lengths = torch.tensor([1100, 777], device=DEV)
+    args = recurrence_inputs(b, t, 4, kind="baseline", seed=31, device=DEV)
+    out = fused_recurrence(*args, lengths=lengths)
+    ref = O.mask_rows(oracle_out(args), lengths.cpu().numpy())
+    assert_recurrence_close(out, ref, "TMA-staged long rows")

@@ -623,11 +623,15 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       // the controls are done.
       held += nv > 0;
       // (Claimed by warp 7, which has less other single-thread work than warp 0.)
-      if (tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
+      // Short rows claim at once; long rows once the slot is free (below): the later a
+      // unit is claimed, the fewer of its row's predecessors are still unpublished when
+      // its epilogue looks back (cfg2-like rows).
+      if (!kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
       if (nv == 0) {
         // Whole chunk past the length: no tensor work, no slot; its rows are
         // zeroed after the loop. (Every later chunk of this row is empty too,
         // so nobody reads its state.)
+        if (kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
         if (tid == kClaimThread) mi.next_ticket = my_next;
         bar_sync_n(kBarProducer, kProducerThreads);
         stage_unit(mi.next_ticket);
@@ -750,6 +754,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       }
       // The slot's previous unit must be fully retired before it is rewritten.
       if (k >= 2) ok &= mbar_wait(&mi.freed[slot], ((k >> 1) - 1) & 1);
+      if (kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
       const uint32_t sb = base + slot * kSlotBytes;
       // ---- controls and the decay cumsum ----------------------------------------
       if (tid < kChunk) {

@@ -623,9 +623,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       // the controls are done.
       held += nv > 0;
       // (Claimed by warp 7, which has less other single-thread work than warp 0.)
-      // Short rows claim at once; long rows once the slot is free (below): the later a
-      // unit is claimed, the fewer of its row's predecessors are still unpublished when
-      // its epilogue looks back (cfg2-like rows).
+      // Short rows claim at once; long rows once the unit's tiles are under way (below):
+      // the later a unit is claimed, the fewer of its row's predecessors are still
+      // unpublished when its epilogue looks back.
       if (!kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
       if (nv == 0) {
         // Whole chunk past the length: no tensor work, no slot; its rows are
@@ -754,7 +754,6 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       }
       // The slot's previous unit must be fully retired before it is rewritten.
       if (k >= 2) ok &= mbar_wait(&mi.freed[slot], ((k >> 1) - 1) & 1);
-      if (kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
       const uint32_t sb = base + slot * kSlotBytes;
       // ---- controls and the decay cumsum ----------------------------------------
       if (tid < kChunk) {
@@ -772,9 +771,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         hd.g[tid] = scl > 0.f ? gm * rcp_approx(scl) : 0.f;
         hd.cs[tid] = x;
       }
-      if (tid == kClaimThread) mi.next_ticket = my_next;
+      if (!kLook && tid == kClaimThread) mi.next_ticket = my_next;
       bar_sync_n(kBarProducer, kProducerThreads);  // also: every thread has read its staged rows
-      stage_unit(mi.next_ticket);
+      if constexpr (!kLook) stage_unit(mi.next_ticket);
       if (tid < kChunk) {
         // Final cumsum, and its range over the chunk (warps 0-1).
         float cv = hd.cs[tid];
@@ -822,6 +821,8 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         }
       }
       bar_sync_n(kBarProducer, kProducerThreads);
+      // Long rows: the next unit is claimed here and staged at the end of the iteration.
+      if (kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
       const float total = hd.cs[kChunk - 1];
       // Decay reference of the unit: mu near the middle of the cumsum's range, with
       // E = total - mu an integer, so that the decay-weighted values vs below are
@@ -937,9 +938,11 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         hd.gtot = ex2_approx(total);
         hd.wide = wide ? 1 : 0;
       }
+      if (kLook && tid == kClaimThread) mi.next_ticket = my_next;
       fence_async_smem();
       tc_fence_before();
       bar_sync_n(kBarProducer, kProducerThreads);
+      if constexpr (kLook) stage_unit(mi.next_ticket);
       pend = slot;  // MMA 1 is issued at the top of the next iteration
       ++k;
     }

@@ -54,6 +54,10 @@ struct alignas(64) RecurrenceParams {
   // host-mapped error word it then also sets (null when none is set up).
   unsigned long long flag_wait_ns;
   int* err_host;
+  // Set by the launcher: element extent (largest offset + 1) of each tensor the
+  // kernel reads or writes, and the workspace's unit count. A build with
+  // TF_DEBUG_BOUNDS checks every global access of the kernel against them.
+  int64_t ext_q, ext_k, ext_v, ext_z, ext_a, ext_out, ext_dt, ext_adt, ext_trap, ext_ar, ext_dr;
 };
 
 // One launch may run up to two directions over the same (B, T, H) shape; their

@@ -51,6 +51,7 @@
 // product, mamba_fused.py:124) is the score diagonal, since rotating q and k by
 // the same angle preserves their dot product; (D + qk) v rides on P's diagonal.
 #include <cstdio>
+#include <initializer_list>
 
 #include "../../include/trifusion_b200.h"
 #include <cudaTypedefs.h>
@@ -285,7 +286,28 @@ __device__ __forceinline__ float silu_tanh(float z) {
   return fmaf(hz, tanh_approx(hz), hz);  // z * sigmoid(z) = hz (1 + tanh(hz))
 }
 
-__device__ int g_device_error = 0;  // set when a bounded wait gives up
+__device__ int g_device_error = 0;  // 1: a bounded wait gave up; 2: an out-of-range access (bounds build)
+
+// [off, off + width) within a tensor of `ext` elements. Always true, except in a
+// build with TF_DEBUG_BOUNDS, where a range outside records error 2 and returns
+// false: the caller then reads zeros (or element 0) or skips the store.
+// An offset to use only when `ok` (bounds build: element 0 otherwise; other builds
+// use the offset as it is, where `ok` is always the caller's own row validity).
+#ifdef TF_DEBUG_BOUNDS
+#define TF_OFF(ok, off) ((ok) ? (off) : 0)
+#else
+#define TF_OFF(ok, off) (off)
+#endif
+__device__ __forceinline__ bool tf_in(int64_t off, int64_t width, int64_t ext) {
+#ifdef TF_DEBUG_BOUNDS
+  if (off >= 0 && off + width <= ext) return true;
+  atomicExch(&g_device_error, 2);
+  return false;
+#else
+  (void)off, (void)width, (void)ext;
+  return true;
+#endif
+}
 
 __device__ __forceinline__ float2 pair(const float* x) { return make_float2(x[0], x[1]); }
 __device__ __forceinline__ void set_pair(float* x, float2 v) {
@@ -415,12 +437,14 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
   const RecurrenceParams& p0 = pd0;
   const int nck = (p0.T + kChunk - 1) / kChunk;
   const Shape shp{p0.B, p0.H, nck, nck * kDirs * p0.B * p0.H, kDirs};
+  // A unit's workspace record (unit 0's, with error 2 recorded, if u is out of range).
+  auto uws_of = [&](int u) { return unit_ws(ws, TF_OFF(tf_in(u, 1, shp.units), u)); };
   constexpr bool lookback = kLook;  // rows longer than kLookbackChunks chunks (chosen by the launcher)
   // Valid length of every row (per direction), read once per CTA.
   int* teff_tab = reinterpret_cast<int*>(smem + kOffTeff);
   auto row_length = [&](const RecurrenceParams& pr, int bb) -> int {
     if (!pr.lengths) return pr.T;
-    const int64_t len = pr.lengths[bb];
+    const int64_t len = tf_in(bb, 1, pr.B) ? pr.lengths[bb] : 0;
     return static_cast<int>(len < 0 ? 0 : (len > pr.T ? pr.T : len));
   };
   if (p0.B <= kTeffTable) {
@@ -515,26 +539,33 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         const int64_t x = static_cast<int64_t>(nc) * kChunk + t;
         const int64_t pos = valid ? (rv ? te - 1 - x : x) : 0;
         const int hq = nh / (pn.H / pn.Hq);
-        const bf16* qrow = pn.q + nb * pn.sq[0] + pos * pn.sq[1] + hq * pn.sq[2];
-        const bf16* krow = pn.k + nb * pn.sk[0] + pos * pn.sk[1] + hq * pn.sk[2];
-        const bf16* vrow = pn.v + nb * pn.sv[0] + pos * pn.sv[1] + nh * pn.sv[2];
-        const bf16* zrow = pn.z + nb * pn.sz[0] + pos * pn.sz[1] + nh * pn.sz[2];
+        const int64_t qo = nb * pn.sq[0] + pos * pn.sq[1] + hq * pn.sq[2];
+        const int64_t ko = nb * pn.sk[0] + pos * pn.sk[1] + hq * pn.sk[2];
+        const int64_t vo = nb * pn.sv[0] + pos * pn.sv[1] + nh * pn.sv[2];
+        const int64_t zo = nb * pn.sz[0] + pos * pn.sz[1] + nh * pn.sz[2];
+        const bool qv = valid && tf_in(qo, kState, pn.ext_q), kv = valid && tf_in(ko, kState, pn.ext_k);
+        const bool vv = valid && tf_in(vo, kHead, pn.ext_v), zv = valid && tf_in(zo, kHead, pn.ext_z);
+        const bf16* qrow = pn.q + TF_OFF(qv, qo);
+        const bf16* krow = pn.k + TF_OFF(kv, ko);
+        const bf16* vrow = pn.v + TF_OFF(vv, vo);
+        const bf16* zrow = pn.z + TF_OFF(zv, zo);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          stage16<kVec>(stage + kStQ + i * 4096u + tid * 16u, qrow + 32 * i + 8 * s4, valid);
-          stage16<kVec>(stage + kStK + i * 4096u + tid * 16u, krow + 32 * i + 8 * s4, valid);
+          stage16<kVec>(stage + kStQ + i * 4096u + tid * 16u, qrow + 32 * i + 8 * s4, qv);
+          stage16<kVec>(stage + kStK + i * 4096u + tid * 16u, krow + 32 * i + 8 * s4, kv);
         }
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          stage16<kVec>(stage + kStV + i * 4096u + tid * 16u, vrow + 32 * i + 8 * s4, valid);
-          stage16<kVec>(stage + kStZ + i * 4096u + tid * 16u, zrow + 32 * i + 8 * s4, valid);
+          stage16<kVec>(stage + kStV + i * 4096u + tid * 16u, vrow + 32 * i + 8 * s4, vv);
+          stage16<kVec>(stage + kStZ + i * 4096u + tid * 16u, zrow + 32 * i + 8 * s4, zv);
         }
         if (pn.ang_vec) {  // row tid/4, pairs 8*(tid%4) .. +7
           const int ra = tid >> 2;
-          const bool av = ra < nvn;
           const int64_t xa = static_cast<int64_t>(nc) * kChunk + ra;
-          const int64_t apos = av ? (rv ? te - 1 - xa : xa) : 0;
-          const bf16* arow = pn.ang + nb * pn.sa[0] + apos * pn.sa[1] + nh * pn.sa[2] + 8 * s4;
+          const int64_t apos = ra < nvn ? (rv ? te - 1 - xa : xa) : 0;
+          const int64_t ao = nb * pn.sa[0] + apos * pn.sa[1] + nh * pn.sa[2] + 8 * s4;
+          const bool av = ra < nvn && tf_in(ao, 8, pn.ext_a);
+          const bf16* arow = pn.ang + TF_OFF(av, ao);
           cp_async8(stage + kStA + ra * 64u + s4 * 16u, arow, av ? 8u : 0u);
           cp_async8(stage + kStA + ra * 64u + s4 * 16u + 8u, arow + 4, av ? 8u : 0u);
         }
@@ -679,21 +710,27 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         }
       } else {
         const int64_t pos = row_ok ? src_row(c0 + t) : 0;
-        const bf16* qrow = p.q + b * p.sq[0] + pos * p.sq[1] + (h / (p.H / p.Hq)) * p.sq[2];
-        const bf16* krow = p.k + b * p.sk[0] + pos * p.sk[1] + (h / (p.H / p.Hq)) * p.sk[2];
-        const bf16* vrow = p.v + b * p.sv[0] + pos * p.sv[1] + h * p.sv[2];
-        const bf16* zrow = p.z + b * p.sz[0] + pos * p.sz[1] + h * p.sz[2];
+        const int64_t qo = b * p.sq[0] + pos * p.sq[1] + (h / (p.H / p.Hq)) * p.sq[2];
+        const int64_t ko = b * p.sk[0] + pos * p.sk[1] + (h / (p.H / p.Hq)) * p.sk[2];
+        const int64_t vo = b * p.sv[0] + pos * p.sv[1] + h * p.sv[2];
+        const int64_t zo = b * p.sz[0] + pos * p.sz[1] + h * p.sz[2];
+        const bool qv = row_ok && tf_in(qo, kState, p.ext_q), kv = row_ok && tf_in(ko, kState, p.ext_k);
+        const bool vv = row_ok && tf_in(vo, kHead, p.ext_v), zv = row_ok && tf_in(zo, kHead, p.ext_z);
+        const bf16* qrow = p.q + TF_OFF(qv, qo);
+        const bf16* krow = p.k + TF_OFF(kv, ko);
+        const bf16* vrow = p.v + TF_OFF(vv, vo);
+        const bf16* zrow = p.z + TF_OFF(zv, zo);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int e = 32 * i + 8 * s4;
-          qraw[i] = row_ok ? load16<kVec>(qrow + e) : make_uint4(0, 0, 0, 0);
-          kraw[i] = row_ok ? load16<kVec>(krow + e) : make_uint4(0, 0, 0, 0);
+          qraw[i] = qv ? load16<kVec>(qrow + e) : make_uint4(0, 0, 0, 0);
+          kraw[i] = kv ? load16<kVec>(krow + e) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const int e = 32 * i + 8 * s4;
-          vraw[i] = row_ok ? load16<kVec>(vrow + e) : make_uint4(0, 0, 0, 0);
-          zraw[i] = row_ok ? load16<kVec>(zrow + e) : make_uint4(0, 0, 0, 0);
+          vraw[i] = vv ? load16<kVec>(vrow + e) : make_uint4(0, 0, 0, 0);
+          zraw[i] = zv ? load16<kVec>(zrow + e) : make_uint4(0, 0, 0, 0);
         }
       }
       float c_dt = 0.f, c_dn = 0.f, c_tr = 0.f, c_tn = 0.f, c_adt = 0.f;
@@ -703,33 +740,41 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         const char* trbase =
             static_cast<const char*>(p.trap) + (b * p.str[0] + h * p.str[1]) * (p.trap_bf16 ? 2 : 4);
         const int64_t tt = c0 + tid;
+        // Element offsets within each tensor (checked in a bounds build).
+        const int64_t o_dt = b * p.sdt[0] + h * p.sdt[1], o_adt = b * p.sadt[0] + h * p.sadt[1];
+        const int64_t o_tr = b * p.str[0] + h * p.str[1];
+        auto trap_at = [&](int64_t x) { return tf_in(o_tr + x, 1, p.ext_trap) ? load_trap(p, trbase, x) : 0.f; };
         if (kExt && p.raw_controls) {
           // dt = softplus(ddt + dt_bias), adt = A dt from the projection views.
+          const int64_t o_a = b * p.sar[0] + h * p.sar[2], o_d = b * p.sdr[0] + h * p.sdr[2];
           const bf16* abase = p.a_raw + b * p.sar[0] + h * p.sar[2];
           const bf16* dbase = p.ddt_raw + b * p.sdr[0] + h * p.sdr[2];
-          const float bias = p.dt_bias[h];
+          auto a_at = [&](int64_t x) { return tf_in(o_a + x, 1, p.ext_ar) ? bf2f(abase[x]) : 0.f; };
+          auto d_at = [&](int64_t x) { return tf_in(o_d + x, 1, p.ext_dr) ? bf2f(dbase[x]) : 0.f; };
+          const float bias = tf_in(h, 1, p.H) ? p.dt_bias[h] : 0.f;
           if (tid < nv) {
             const int64_t sr = src_row(tt);
-            c_dt = softplus_dt(bf2f(dbase[sr * p.sdr[1]]) + bias);
-            c_adt = a_control(bf2f(abase[sr * p.sar[1]]), p.a_floor) * c_dt;
-            c_tr = load_trap(p, trbase, sr * p.str[2]);
+            c_dt = softplus_dt(d_at(sr * p.sdr[1]) + bias);
+            c_adt = a_control(a_at(sr * p.sar[1]), p.a_floor) * c_dt;
+            c_tr = trap_at(sr * p.str[2]);
           }
           if (tt + 1 < T_eff) {
             const int64_t sn = src_row(tt + 1);
-            c_dn = softplus_dt(bf2f(dbase[sn * p.sdr[1]]) + bias);
-            c_tn = load_trap(p, trbase, sn * p.str[2]);
+            c_dn = softplus_dt(d_at(sn * p.sdr[1]) + bias);
+            c_tn = trap_at(sn * p.str[2]);
           }
         } else {
+          auto dt_at = [&](int64_t x) { return tf_in(o_dt + x, 1, p.ext_dt) ? dtbase[x] : 0.f; };
           if (tid < nv) {
             const int64_t sr = src_row(tt);
-            c_dt = dtbase[sr * p.sdt[2]];
-            c_tr = load_trap(p, trbase, sr * p.str[2]);
-            c_adt = adtbase[sr * p.sadt[2]];
+            c_dt = dt_at(sr * p.sdt[2]);
+            c_tr = trap_at(sr * p.str[2]);
+            c_adt = tf_in(o_adt + sr * p.sadt[2], 1, p.ext_adt) ? adtbase[sr * p.sadt[2]] : 0.f;
           }
           if (tt + 1 < T_eff) {
             const int64_t sn = src_row(tt + 1);
-            c_dn = dtbase[sn * p.sdt[2]];
-            c_tn = load_trap(p, trbase, sn * p.str[2]);
+            c_dn = dt_at(sn * p.sdt[2]);
+            c_tn = trap_at(sn * p.str[2]);
           }
         }
       }
@@ -749,7 +794,8 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int tt = warp * 8 + i;
-          araw[i] = tt < nv ? bf2f(abase[src_row(c0 + tt) * p.sa[1] + lane * p.sa[3]]) : 0.f;
+          const int64_t ax = src_row(c0 + tt) * p.sa[1] + lane * p.sa[3];
+          araw[i] = (tt < nv && tf_in(b * p.sa[0] + h * p.sa[2] + ax, 1, p.ext_a)) ? bf2f(abase[ax]) : 0.f;
         }
       }
       // The slot's previous unit must be fully retired before it is rewritten.
@@ -835,8 +881,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       const bool wide = cmax - cmin > 180.f;
       // ---- rows -> FP16 operand tiles (q16, k~, vs, v16) and the z tile ------------
       {
-        const float* qbh = p.qb + h * kState;
-        const float* kbh = p.kb + h * kState;
+        const int hb = TF_OFF(tf_in(static_cast<int64_t>(h) * kState, kState, static_cast<int64_t>(p.H) * kState), h);
+        const float* qbh = p.qb + hb * kState;
+        const float* kbh = p.kb + hb * kState;
         float cn[8], sn[8];  // this thread's 8 rotating pairs: 4s..4s+3, 16+4s..16+4s+3
 #pragma unroll
         for (int m = 0; m < 8; ++m)
@@ -955,7 +1002,9 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       const RecurrenceParams& pz = (kDirs == 1 || zd == 0) ? pd0 : pd1;
       const int z0 = zc * kChunk;
       if (z0 < teff_of(zd, zb, pz) || z0 + t >= pz.T) continue;
-      bf16* orow = pz.out + zb * pz.so[0] + static_cast<int64_t>(z0 + t) * pz.so[1] + zh * pz.so[2];
+      const int64_t oz = zb * pz.so[0] + static_cast<int64_t>(z0 + t) * pz.so[1] + zh * pz.so[2];
+      if (!tf_in(oz, kHead, pz.ext_out)) continue;
+      bf16* orow = pz.out + oz;
 #pragma unroll
       for (int i = 0; i < 2; ++i) store16<kVec>(orow + 32 * i + 8 * s4, make_uint4(0, 0, 0, 0));
     }
@@ -978,7 +1027,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       const RecurrenceParams& p = (kDirs == 1 || dir == 0) ? pd0 : pd1;
       const uint32_t sb = base + slot * kSlotBytes;
       const uint32_t tm = tmem0 + slot * kSlotCols;
-      unsigned char* uws = unit_ws(ws, u);
+      unsigned char* uws = uws_of(u);
       ok &= mbar_wait(&mi.mma1[slot], ph);
       tc_fence_after();
       // The row's last chunk has no successor: nothing reads its dS, flag or state.
@@ -1054,7 +1103,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       };
       // Loads of a predecessor whose dS is known to be published.
       auto fetch = [&](int x, uint4 (&w)[4], float& f, float& gx, float& th) {
-        const unsigned char* xws = unit_ws(ws, unit_index(shp, x, dir, b, h));
+        const unsigned char* xws = uws_of(unit_index(shp, x, dir, b, h));
         const __half* agg = reinterpret_cast<const __half*>(xws + kUnitAgg) + n * 64 + 32 * chalf;
 #pragma unroll
         for (int q = 0; q < 4; ++q) w[q] = ld_cg_v4(agg + 8 * q);
@@ -1076,7 +1125,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
             for (; y >= 0; --y) {
               uint32_t seen = 0;
               const int ub = unit_index(shp, y, dir, b, h);
-              ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, ub) + kUnitFlag), epoch, kFlagAgg, seen,
+              ok &= wait_flag(reinterpret_cast<const uint32_t*>(uws_of(ub) + kUnitFlag), epoch, kFlagAgg, seen,
                               p0.flag_wait_ns);
               if (static_cast<int>(seen - epoch) >= static_cast<int>(kFlagIncl)) break;
             }
@@ -1085,7 +1134,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           bar_sync_n(kBarEpilogue, kEpilogueThreads);
           const int y = mi.lookback_start;
           if (y >= 0) {
-            const unsigned char* yws = unit_ws(ws, unit_index(shp, y, dir, b, h));
+            const unsigned char* yws = uws_of(unit_index(shp, y, dir, b, h));
             (void)ld_acquire_u32(reinterpret_cast<const uint32_t*>(yws + kUnitFlag));
             const float* incl = reinterpret_cast<const float*>(yws + kUnitIncl) + n * 64 + 32 * chalf;
 #pragma unroll
@@ -1102,7 +1151,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
           // Short rows: lane l of every warp waits for predecessor l's dS flag.
           for (int x = lane; x < c; x += 32) {
             uint32_t seen = 0;
-            ok &= wait_flag(reinterpret_cast<const uint32_t*>(unit_ws(ws, unit_index(shp, x, dir, b, h)) + kUnitFlag),
+            ok &= wait_flag(reinterpret_cast<const uint32_t*>(uws_of(unit_index(shp, x, dir, b, h)) + kUnitFlag),
                             epoch, kFlagAgg, seen, p0.flag_wait_ns);
           }
           __syncwarp();
@@ -1162,7 +1211,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         if (!upper) {
           tmem_ld_16x256_x4(tmem_addr(tm, 32 * q4, kColS + 32 * chalf), sc);
           tmem_wait_ld();
-          const float d = p.d[h];
+          const float d = tf_in(h, 1, p.H) ? p.d[h] : 0.f;
           const float g0 = hd.g[i0], g1 = hd.g[i1];
           const float rl0 = hd.rl[i0], rl1 = hd.rl[i1];
           const bool wide_u = hd.wide != 0;
@@ -1318,12 +1367,15 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
         if (c0 + r < p.T) {
           // Valid rows of a reversed row go back to time len-1-x; padding stays put.
           const int64_t row = (kExt && p.reverse && r < nv) ? static_cast<int64_t>(hd.teff - 1 - (c0 + r)) : c0 + r;
-          bf16* orow = p.out + b * p.so[0] + row * p.so[1] + h * p.so[2];
+          const int64_t oo = b * p.so[0] + row * p.so[1] + h * p.so[2];
+          if (tf_in(oo, kHead, p.ext_out)) {  // (a bounds build skips an out-of-range row)
+            bf16* orow = p.out + oo;
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int e = 8 * (2 * (et & 3) + q);
-            const uint4 val = r < nv ? ld_shared_v4(sb + kSlotZ + sw128_offset(r, e)) : make_uint4(0, 0, 0, 0);
-            store16<kVec>(orow + e, val);
+            for (int q = 0; q < 2; ++q) {
+              const int e = 8 * (2 * (et & 3) + q);
+              const uint4 val = r < nv ? ld_shared_v4(sb + kSlotZ + sw128_offset(r, e)) : make_uint4(0, 0, 0, 0);
+              store16<kVec>(orow + e, val);
+            }
           }
         }
       }
@@ -1466,6 +1518,30 @@ bool encode_direction(RecurrenceParams& p) {
          encode_rows(&p.tm_a, p.ang, kRotary, p.T, p.H, p.B, p.sa[0], p.sa[1], p.sa[2]);
 }
 
+// Largest element offset + 1 of a tensor with these extents and (non-negative) strides.
+int64_t extent(std::initializer_list<int64_t> dims, const int64_t* strides) {
+  int64_t last = 0, i = 0;
+  for (int64_t d : dims) {
+    if (d <= 0) return 0;
+    last += (d - 1) * strides[i++];
+  }
+  return last + 1;
+}
+
+void set_extents(RecurrenceParams& p) {
+  p.ext_q = extent({p.B, p.T, p.Hq, kState}, p.sq);
+  p.ext_k = extent({p.B, p.T, p.Hq, kState}, p.sk);
+  p.ext_v = extent({p.B, p.T, p.H, kHead}, p.sv);
+  p.ext_z = extent({p.B, p.T, p.H, kHead}, p.sz);
+  p.ext_out = extent({p.B, p.T, p.H, kHead}, p.so);
+  p.ext_a = extent({p.B, p.T, p.H, kRotary}, p.sa);
+  p.ext_dt = extent({p.B, p.H, p.T}, p.sdt);
+  p.ext_adt = extent({p.B, p.H, p.T}, p.sadt);
+  p.ext_trap = extent({p.B, p.H, p.T}, p.str);
+  p.ext_ar = p.raw_controls ? extent({p.B, p.T, p.H}, p.sar) : 0;
+  p.ext_dr = p.raw_controls ? extent({p.B, p.T, p.H}, p.sdr) : 0;
+}
+
 int alignment_class(const RecurrenceLaunch& L) {
   int a = alignment_class_one(L.dir[0]);
   if (L.ndir > 1) a = a < alignment_class_one(L.dir[1]) ? a : alignment_class_one(L.dir[1]);
@@ -1506,6 +1582,7 @@ int launch_recurrence_persistent(const RecurrenceLaunch& launch_in, void* worksp
     L.dir[i].ang_vec = angles_vectorizable(L.dir[i]);
     L.dir[i].flag_wait_ns = flag_wait_limit_ns();
     L.dir[i].err_host = host_error_word();
+    set_extents(L.dir[i]);
   }
   const RecurrenceParams& p = L.dir[0];
   if (workspace_bytes < recurrence_workspace_bytes(p.B, p.T, p.H, L.ndir)) return 1;

@@ -10,7 +10,11 @@ from __future__ import annotations
 import ctypes
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_native" / "libtrifusion_b200.so"
+import os
+
+# TRIFUSION_B200_BOUNDS=1 loads the bounds-checked debug build (build.py --debug-bounds).
+LIB_PATH = Path(__file__).resolve().parent / "_native" / (
+    "libtrifusion_b200_bounds.so" if os.environ.get("TRIFUSION_B200_BOUNDS") == "1" else "libtrifusion_b200.so")
 
 TF_OK, TF_ERR_SHAPE, TF_ERR_ARG, TF_ERR_LAYOUT, TF_ERR_DEVICE, TF_ERR_LAUNCH, TF_ERR_SIZE = range(7)
 TF_F32, TF_BF16 = 0, 1

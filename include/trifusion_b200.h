@@ -297,6 +297,43 @@ int tf_query_read_fwd(const void* q, const void* kv, int64_t kv_pitch, const int
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,
                       int64_t row_bytes, void* stream);
 
+/* Local evidence of the decoder: for each clip b and class c in {0, 1}, the scores
+ * float(local[b, t, c]) with frames t >= fine_lengths[b] at -inf, their k = min(25, time)
+ * largest (ties at the k-th value resolve to the earliest frames), and
+ * top[b, c, :] = sum over the first min(fine_lengths[b], k) picks of float(features[b, t, :])
+ * divided by that count (NaN when it is 0, like the reference). `local` BF16 rows of pitch
+ * local_pitch elements (classes in columns 0 and 1), `features` BF16 rows of pitch
+ * feat_pitch (256 used), both [batch, time, pitch] contiguous over rows; writes
+ * local_f32 [batch, time, 2] (the FP32 copy of `local`) and top [batch, 2, 256] FP32.
+ * time <= 12288 (else TF_ERR_SIZE). Replaces decoder.py:65-76 (`local.float()`, the
+ * masked_fill, topk, gather and masked mean); the selection is exact, the mean equal up
+ * to FP32 summation order. */
+int tf_local_topk_fwd(const void* local, int64_t local_pitch, const void* features, int64_t feat_pitch,
+                      const int64_t* fine_lengths, float* local_f32, float* top, int batch, int time,
+                      void* stream);
+
+/* Decoder heads: voice = silu(voice_lat(cat(deep_q[0], fine_q[0], global, top[:, 0], memory))),
+ * music likewise (query group 1, top[:, 1]), file = silu(file_head[0](cat(deep_q[2], fine_q[2],
+ * global, memory, voice, music))), and logits [batch, 5] FP32 = [f, v0, m0, v1, m1] with
+ * v = voice_head(voice), m = music_head(music), f = file_head[2](file). deep_rows and
+ * fine_rows are the query reads' BF16 out-projection rows [batch, 10, 256]; deep_q[g] and
+ * fine_q[g] are their group means over rows 0-3, 4-7 and 8-9 (rounded once to BF16);
+ * global_feature and memory are BF16 [batch, 256], top FP32 [batch, 2, 256] (rounded to
+ * BF16 as autocast does for the concatenation). Weights are the BF16 Linear weights
+ * ([out, in] row-major, 16-byte aligned) and biases: voice/music lat [256, 1280] + [256],
+ * voice/music head [2, 256] + [2], file_head[0] [256, 1536] + [256], file_head[2] [1, 256] + [1].
+ * Every projection accumulates in FP32, adds the bias and rounds to BF16; SiLU rounds again.
+ * `scratch` holds tf_decoder_heads_scratch_bytes(batch) bytes (16-byte aligned). Three
+ * launches. Replaces decoder.py:77-89 (five concatenations, five projections, two SiLUs,
+ * the logits concatenation and cast); equal to the reference up to FP32 summation order. */
+int64_t tf_decoder_heads_scratch_bytes(int batch);
+int tf_decoder_heads_fwd(const void* deep_rows, const void* fine_rows, const void* global_feature,
+                         const void* memory, const float* top, const void* w_voice, const void* b_voice,
+                         const void* w_music, const void* b_music, const void* w_vhead, const void* b_vhead,
+                         const void* w_mhead, const void* b_mhead, const void* w_file1, const void* b_file1,
+                         const void* w_file2, const void* b_file2, void* scratch, int64_t scratch_bytes,
+                         float* logits, int batch, void* stream);
+
 /* RMSNorm as tf_rms_fwd with the output type chosen (`y_dtype` TF_F32 or TF_BF16):
  * a BF16 result is the FP32 result rounded once, i.e. what autocast would feed the
  * next projection. Replaces `RMSNorm` (kernels/__init__.py:23-27) followed by the
@@ -382,6 +419,14 @@ int tf_depthwise_masked_fwd(const void* x, int dtype, const void* w, const void*
  * autocast before the merge projection). */
 int tf_depthwise_residual_fwd(const void* x, int dtype, const void* w, const void* bias, const int64_t* lengths,
                               void* y, int batch, int seqlen, int channels, int taps, void* stream);
+
+/* As tf_depthwise_masked_fwd on the GLU of x: x [batch, seqlen, 2 * channels] BF16 (the
+ * local branch's up projection, 8-byte aligned), conv input h = bf16(a * (1 / (1 + e^-g)))
+ * with a = x[.., c], g = x[.., channels + c] (PyTorch's glu on a BF16 tensor), output
+ * BF16 [batch, seqlen, channels]. Replaces model.py:122 `F.glu(self.up(x))` and the
+ * depthwise conv that reads its result (model.py:123-124); bit-exact against the two. */
+int tf_glu_depthwise_fwd(const void* x, const void* w, const void* bias, const int64_t* lengths, void* y,
+                         int batch, int seqlen, int channels, int taps, void* stream);
 
 /* Rotary q/k of the attention branch: x [B, T, 3, H, D] BF16 (the qkv projection)
  * -> y [3, B, H, T, D] FP32 holding BF16-rounded values; q and k pairs rotated by

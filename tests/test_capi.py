@@ -29,6 +29,15 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
 
 
+def test_ctypes_table_matches_header_arity():
+    """Every ctypes argument list has as many entries as the header's prototype."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for name, params in re.findall(r"\b(tf_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text):
+        params = params.strip()
+        count = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(_lib.SIGNATURES[name]) == count, (name, len(_lib.SIGNATURES[name]), count)
+
+
 def test_status_strings_and_version():
     lib = _lib.lib()
     assert lib.tf_status_string(0) == b"ok"

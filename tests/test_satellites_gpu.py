@@ -279,6 +279,21 @@ def test_depthwise_masked_matches_conv1d(dtype, taps, width):
     assert (y.masked_select(~valid.expand_as(y)) == 0).all()
 
 
+@pytest.mark.parametrize("taps,width", [(7, 384), (3, 64)])
+def test_glu_depthwise_equals_glu_then_depthwise(taps, width):
+    """The GLU formed inside the depthwise pass equals PyTorch's glu followed by the
+    depthwise kernel, bit for bit (model.py:122-124)."""
+    from trifusion_b200.kernels.buffers import depthwise_masked, glu_depthwise
+
+    b, t = 3, 77
+    u = (seeded((b, t, 2 * width), 31) * 3).to(BF).to(DEV)
+    torch.manual_seed(32)
+    conv = torch.nn.Conv1d(width, width, taps, padding=taps // 2, groups=width).to(DEV).to(BF)
+    lengths = torch.tensor([77, 40, 0], device=DEV)
+    fused = glu_depthwise(u, conv, lengths)
+    assert torch.equal(fused, depthwise_masked(torch.nn.functional.glu(u, dim=-1), conv, lengths))
+
+
 def test_rotary_qkv_bit_exact_with_formula():
     from trifusion_b200.kernels.buffers import RotaryQKV
     from trifusion_b200.masking import rotary_table

@@ -431,12 +431,16 @@ __global__ void __launch_bounds__(kThreads) masked_mean_kernel(const T* __restri
 // as in the reference kernel, and the result is BF16. Four channels per thread.
 // kResidual: y = bf16(x + bf16(conv)) instead (model.py:188-189 `v + conv` before the
 // merge projection, whose autocast input is that sum rounded to BF16).
-template <typename TI, int K, bool kResidual = false>
+// kGlu: x holds [B, T, 2C] rows (the local branch's up projection, model.py:122) and the
+// conv input is their GLU, bf16(a * (1 / (1 + e^-g))) with a = x[.., c], g = x[.., C + c]
+// (PyTorch's glu on a BF16 tensor: FP32 math, one rounding), so h is never written.
+template <typename TI, int K, bool kResidual = false, bool kGlu = false>
 __global__ void __launch_bounds__(kThreads) depthwise_kernel(const TI* __restrict__ x,
                                                              const bf16* __restrict__ w,
                                                              const bf16* __restrict__ bias,
                                                              const int64_t* __restrict__ lengths,
                                                              bf16* __restrict__ y, int B, int T, int C) {
+  const int64_t pitch = kGlu ? 2 * static_cast<int64_t>(C) : C;
   const int quads = C / 4;
   const int64_t total = static_cast<int64_t>(B) * T * quads;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
@@ -452,7 +456,12 @@ __global__ void __launch_bounds__(kThreads) depthwise_kernel(const TI* __restric
       for (int k = 0; k < K; ++k) {
         const int src = t + k - K / 2;
         if (src < 0 || src >= T) continue;
-        const float4 xv = load4(x + (static_cast<int64_t>(b) * T + src) * C + c);
+        float4 xv = load4(x + (static_cast<int64_t>(b) * T + src) * pitch + c);
+        if constexpr (kGlu) {
+          const float4 gv = load4(x + (static_cast<int64_t>(b) * T + src) * pitch + C + c);
+          auto glu = [](float a, float g) { return a * (1.f / (1.f + expf(-g))); };
+          xv = make_float4(glu(xv.x, gv.x), glu(xv.y, gv.y), glu(xv.z, gv.z), glu(xv.w, gv.w));
+        }
         const float xs[4] = {bf16_round(xv.x), bf16_round(xv.y), bf16_round(xv.z), bf16_round(xv.w)};
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(xs[j], __bfloat162float(w[(c + j) * K + k])));
@@ -475,15 +484,15 @@ __global__ void __launch_bounds__(kThreads) depthwise_kernel(const TI* __restric
 
 }  // namespace
 
-template <typename TI, bool kResidual = false>
+template <typename TI, bool kResidual = false, bool kGlu = false>
 int launch_depthwise(const void* x, const bf16* w, const bf16* bias, const int64_t* lengths, bf16* y,
                      int B, int T, int C, int K, cudaStream_t s) {
   const int grid = grid_for(static_cast<int64_t>(B) * T * (C / 4), kThreads);
   auto X = static_cast<const TI*>(x);
   switch (K) {
-    case 3: depthwise_kernel<TI, 3, kResidual><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
-    case 5: depthwise_kernel<TI, 5, kResidual><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
-    case 7: depthwise_kernel<TI, 7, kResidual><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 3: depthwise_kernel<TI, 3, kResidual, kGlu><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 5: depthwise_kernel<TI, 5, kResidual, kGlu><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
+    case 7: depthwise_kernel<TI, 7, kResidual, kGlu><<<grid, kThreads, 0, s>>>(X, w, bias, lengths, y, B, T, C); break;
     default: return TF_ERR_ARG;
   }
   return launch_status();
@@ -1083,6 +1092,22 @@ int tf_depthwise_residual_fwd(const void* x, int dtype, const void* w, const voi
   if (dtype == TF_F32)
     return tf::launch_depthwise<float, true>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
   return tf::launch_depthwise<tf::bf16, true>(x, W, Bs, lengths, Y, batch, seqlen, channels, taps, s);
+}
+
+int tf_glu_depthwise_fwd(const void* x, const void* w, const void* bias, const int64_t* lengths, void* y,
+                         int batch, int seqlen, int channels, int taps, void* stream) {
+  if (batch < 0 || seqlen < 0 || channels < 0) return TF_ERR_ARG;
+  if (taps != 3 && taps != 5 && taps != 7) return TF_ERR_ARG;
+  if (channels % 4) return TF_ERR_LAYOUT;
+  if (batch == 0 || seqlen == 0 || channels == 0) return TF_OK;
+  if (!x || !w || !lengths || !y) return TF_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) % 8 || reinterpret_cast<uintptr_t>(y) % 8) return TF_ERR_LAYOUT;
+  const int st = tf::check_device();
+  if (st != TF_OK) return st;
+  return tf::launch_depthwise<tf::bf16, false, true>(x, static_cast<const tf::bf16*>(w),
+                                                     static_cast<const tf::bf16*>(bias), lengths,
+                                                     static_cast<tf::bf16*>(y), batch, seqlen, channels, taps,
+                                                     static_cast<cudaStream_t>(stream));
 }
 
 int tf_end_gather_fwd(const void* x, const int64_t* lengths, void* y, int batch, int seqlen,

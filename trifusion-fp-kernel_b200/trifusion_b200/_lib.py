@@ -78,11 +78,16 @@ SIGNATURES = {
     "tf_pool4_out_fwd": [_p, _i, _p, _p, _i, _i, _i, _i, _p],
     "tf_front_residual_fwd": [_p, _p, _i, _p, _p, _i, _i, _i, _i, _p],
     "tf_bands_fwd": [_p, _i, _p, _i, _i, _i, _i, _p],
+    "tf_glu_depthwise_fwd": [_p, _p, _p, _p, _p, _i, _i, _i, _i, _p],
+    "tf_local_topk_fwd": [_p, _q, _p, _q, _p, _p, _p, _i, _i, _p],
+    "tf_decoder_heads_scratch_bytes": [_i],
+    "tf_decoder_heads_fwd": [_p] * 18 + [_q, _p, _i, _p],
 }
 _RESTYPES = {"tf_status_string": ctypes.c_char_p, "tf_last_cuda_error": ctypes.c_char_p,
              "tf_recurrence_workspace_size": ctypes.c_size_t,
              "tf_recurrence_workspace_size_multi": ctypes.c_size_t,
-             "tf_query_read_state_floats": ctypes.c_int64}
+             "tf_query_read_state_floats": ctypes.c_int64,
+             "tf_decoder_heads_scratch_bytes": ctypes.c_int64}
 
 
 class RecurrenceIO(ctypes.Structure):

@@ -1,7 +1,9 @@
 """Classification decoder with the reference's parameter layout (reference
-``decoder.py``). The masked time mean and the last-valid-row read of the
-forward Mamba output run on the CUDA kernels of ``libtrifusion_b200.so``;
-the small projections, attention reads and top-k stay PyTorch/cuBLAS.
+``decoder.py``). On the GPU the masked time mean, the last-valid-row read of the
+forward Mamba output and the two query reads run on kernels of
+``libtrifusion_b200.so``; under BF16 autocast so does the tail (top-k local
+evidence, the voice/music/file heads and the logits row). The projections
+before the tail are cuBLAS GEMMs.
 """
 
 from __future__ import annotations
@@ -43,6 +45,18 @@ class QueryRead(nn.Module):
         self.q = nn.Linear(256, 256, bias=False)
         self.out = nn.Linear(256, 256, bias=False)
 
+    def _native_rows(self, qp, kv, lengths, keys_per_length):
+        if kv.is_cuda and kv.dtype == torch.bfloat16 and qp.dtype == torch.bfloat16:
+            from .kernels.native import query_read
+
+            return self.out(query_read(qp, kv, lengths, keys_per_length))
+        return None
+
+    def rows(self, query, x, lengths, keys_per_length=1):
+        """The out projection's ``[B, 10, 256]`` rows (before the 4/4/2 group means) when
+        the split-key kernel applies (GPU, BF16 projections), else None."""
+        return self._native_rows(self.q(query), self.kv(x), lengths, keys_per_length)
+
     def forward(self, query, x, mask, lengths=None, keys_per_length=1):
         """``mask`` [B, T] bool, or None with ``lengths`` given (key j valid when
         ``j < lengths * keys_per_length``). With ``lengths`` on the GPU under BF16
@@ -50,10 +64,8 @@ class QueryRead(nn.Module):
         rows (``native.query_read``)."""
         b, t, _ = x.shape
         kv, qp = self.kv(x), self.q(query)
-        if lengths is not None and x.is_cuda and kv.dtype == torch.bfloat16 and qp.dtype == torch.bfloat16:
-            from .kernels.native import query_read
-
-            h = self.out(query_read(qp, kv, lengths, keys_per_length))
+        h = self._native_rows(qp, kv, lengths, keys_per_length) if lengths is not None else None
+        if h is not None:
             return h[:, :4].mean(1), h[:, 4:8].mean(1), h[:, 8:].mean(1)
         if mask is None:
             mask = time_mask(lengths * keys_per_length, t)
@@ -78,6 +90,9 @@ class Decoder(nn.Module):
         self.voice_head, self.music_head = nn.Linear(256, 2), nn.Linear(256, 2)
         self.file_head = nn.Sequential(nn.Linear(1536, 256), nn.SiLU(), nn.Linear(256, 1))
         self.native_kernels = False
+        # With native kernels under BF16 autocast: the tail after the query reads as this
+        # library's kernels (False keeps the PyTorch tail, e.g. to compare the two).
+        self.fused_tail = True
 
     def _pooled(self, x, mf, lengths, mask):
         if self.native_kernels and x.is_cuda:
@@ -91,7 +106,8 @@ class Decoder(nn.Module):
         b, tf_, _, _ = fine.shape
         fine_mask = time_mask(fine_lengths, tf_)
         native = self.native_kernels and x.is_cuda
-        deep_q = self.deep_read(self.query, x, grids.mask, grids.lengths if native else None)
+        bf16_autocast = (x.is_cuda and torch.is_autocast_enabled("cuda")
+                         and torch.get_autocast_dtype("cuda") == torch.bfloat16)
         if native:
             from .kernels.buffers import _param_bf16
 
@@ -100,17 +116,51 @@ class Decoder(nn.Module):
         else:
             fp = (fine + sin_position(tf_, 64, fine.device)[None, :, None, :].to(fine.dtype)
                   + self.band.to(fine.dtype)[None, None, :, :])
-        if native:  # key t * 8 + band is valid when t < fine_lengths
-            fine_q = self.fine_read(self.query, fp.flatten(1, 2), None, fine_lengths, keys_per_length=8)
-        else:
-            fine_q = self.fine_read(self.query, fp.flatten(1, 2),
-                                    fine_mask[:, :, None].expand(b, tf_, 8).reshape(b, -1))
+        # The query reads' out-projection rows, from the split-key kernel (GPU, BF16).
+        deep_h = fine_h = None
+        if native and bf16_autocast:
+            deep_h = self.deep_read.rows(self.query, x, grids.lengths)
+            fine_h = self.fine_read.rows(self.query, fp.flatten(1, 2), fine_lengths, keys_per_length=8)
         mean, end = self._pooled(x, mf, grids.lengths, grids.mask)
         global_feature = self.global_proj(mean)
         memory = self.memory_proj(torch.cat((end, mb[:, 0]), -1))
         flat = fine.flatten(2)
-        local = self.local_logits(flat)
-        features = self.local_features(flat)
+        if native and bf16_autocast and flat.dtype == torch.bfloat16:
+            import torch.nn.functional as F
+
+            from .kernels.buffers import concat_linear
+
+            # local_logits and local_features as one GEMM over the shared input.
+            w, bias, offs = concat_linear([self.local_logits, self.local_features], torch.bfloat16)
+            both = F.linear(flat, w, bias)
+            local, features = both[..., offs[0]:offs[0] + 2], both[..., offs[1]:offs[1] + 256]
+        else:
+            local, features = self.local_logits(flat), self.local_features(flat)
+        if (self.fused_tail and deep_h is not None and fine_h is not None and local.dtype == torch.bfloat16
+                and global_feature.dtype == torch.bfloat16 and memory.dtype == torch.bfloat16):
+            from .kernels.native import decoder_heads, local_topk
+
+            # The rest is four launches instead of ~40: the top-k evidence over the GEMM's
+            # rows, and the heads with the logits row (group means and concatenations read
+            # in place).
+            local_f32, top = local_topk(local, features, fine_lengths)
+            return {
+                "logits": decoder_heads(deep_h, fine_h, global_feature, memory, top, self),
+                "local_logits": local_f32,
+                "local_mask": fine_mask,
+                "features": x,
+                "feature_mask": grids.mask,
+                "embedding": global_feature.float(),
+            }
+        if deep_h is not None:
+            deep_q = (deep_h[:, :4].mean(1), deep_h[:, 4:8].mean(1), deep_h[:, 8:].mean(1))
+        else:
+            deep_q = self.deep_read(self.query, x, grids.mask)
+        if fine_h is not None:
+            fine_q = (fine_h[:, :4].mean(1), fine_h[:, 4:8].mean(1), fine_h[:, 8:].mean(1))
+        else:
+            fine_q = self.fine_read(self.query, fp.flatten(1, 2),
+                                    fine_mask[:, :, None].expand(b, tf_, 8).reshape(b, -1))
         k = min(25, tf_)
         scores = local.float().masked_fill(~fine_mask.unsqueeze(-1), -torch.inf)
         idx = scores.transpose(1, 2).topk(k, -1).indices

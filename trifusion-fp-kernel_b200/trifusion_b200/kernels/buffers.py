@@ -103,6 +103,35 @@ def stacked_linear(layers, dtype, multiple=1):
     return _STACKED.get(key, params, build)
 
 
+def concat_linear(layers, dtype, multiple=8):
+    """The weights and biases of Linear ``layers`` of any widths that share an input,
+    stacked into one ``[sum of padded widths, in]`` matrix (and bias) of ``dtype``: layer
+    i's rows start at ``offsets[i]``, each width rounded up to ``multiple`` with zero rows,
+    so one GEMM computes every layer and each layer's output columns start on an aligned
+    boundary. Every layer must have a bias. Cached like ``stacked_linear``. Returns
+    (weight, bias, offsets)."""
+    params = [p for layer in layers for p in (layer.weight, layer.bias)]
+    key = ("concat",) + (tuple(id(p) for p in params), dtype, multiple)
+
+    def build():
+        dim = layers[0].weight.shape[1]
+        if any(layer.weight.shape[1] != dim or layer.bias is None for layer in layers):
+            raise ValueError("concat_linear: the layers must share the input width and have biases")
+        offsets, rows = [], 0
+        for layer in layers:
+            offsets.append(rows)
+            rows += (layer.weight.shape[0] + multiple - 1) // multiple * multiple
+        dev = layers[0].weight.device
+        w = torch.zeros(rows, dim, dtype=dtype, device=dev)
+        b = torch.zeros(rows, dtype=dtype, device=dev)
+        for off, layer in zip(offsets, layers):
+            w[off:off + layer.weight.shape[0]] = layer.weight.detach().to(dtype)
+            b[off:off + layer.weight.shape[0]] = layer.bias.detach().to(dtype)
+        return w, b, tuple(offsets)
+
+    return _STACKED.get(key, params, build)
+
+
 def _mask_bytes(mask):
     """The mask as one byte per row, without a conversion pass for bool masks."""
     m = mask.contiguous()
@@ -264,6 +293,28 @@ def depthwise_masked(x, layer, lengths, residual=False):
                 _lib.dtype_code(x, "depthwise_masked"),
                 w.data_ptr(), None if bias is None else bias.data_ptr(), lengths.data_ptr(), y.data_ptr(),
                 b, t, c, k)
+    return y
+
+
+def glu_depthwise(u, layer, lengths):
+    """``depthwise_masked(F.glu(u, -1), layer, lengths)`` in one pass over the BF16
+    ``[B, T, 2C]`` up-projection rows ``u`` (reference ``model.py:122-124``): the GLU is
+    formed per tap as PyTorch's glu rounds it, never written. BF16 ``[B, T, C]``."""
+    u = u.contiguous()
+    dev = _lib.require_cuda("glu_depthwise", u, lengths, layer.weight)
+    b, t, c2 = u.shape
+    c = c2 // 2
+    k = layer.weight.shape[-1]
+    if u.dtype != torch.bfloat16 or c2 % 2:
+        raise ValueError("glu_depthwise: u must be BF16 [B, T, 2C]")
+    if layer.groups != c or layer.weight.shape[0] != c or 2 * layer.padding[0] + 1 != k:
+        raise ValueError("glu_depthwise: expected a depthwise Conv1d with 'same' padding over C channels")
+    w = _param_bf16(layer.weight, (c, k))
+    bias = None if layer.bias is None else _param_bf16(layer.bias, (c,))
+    lengths = lengths.to(torch.int64).contiguous()
+    y = torch.empty((b, t, c), device=dev, dtype=torch.bfloat16)
+    _lib.launch("tf_glu_depthwise_fwd", dev, u.data_ptr(), w.data_ptr(), None if bias is None else bias.data_ptr(),
+                lengths.data_ptr(), y.data_ptr(), b, t, c, k)
     return y
 
 

@@ -230,6 +230,72 @@ def query_read(q, kv, lengths, keys_per_length=1):
     return y
 
 
+def local_topk(local, features, fine_lengths):
+    """The decoder's local evidence (reference ``decoder.py:65-76``): ``local`` the BF16
+    ``[B, T, 2]`` local logits and ``features`` the BF16 ``[B, T, 256]`` local features
+    (either may be a column slice of wider rows, such as one GEMM's output over both
+    layers). Returns ``(local.float(), top)``: the FP32 logits and the FP32 ``[B, 2, 256]``
+    masked mean of the features at the ``min(25, T)`` highest-scoring valid frames of each
+    class (frames ``t >= fine_lengths[b]`` score -inf; ties at the k-th score resolve to the
+    earliest frames)."""
+    dev = _lib.require_cuda("local_topk", local, features, fine_lengths)
+    if local.dtype != torch.bfloat16 or features.dtype != torch.bfloat16:
+        raise ValueError("local_topk: local and features must be BF16")
+    if local.dim() != 3 or local.shape[-1] != 2 or features.dim() != 3 or features.shape[-1] != 256:
+        raise ValueError("local_topk: local must be [B, T, 2] and features [B, T, 256]")
+    if local.shape[:2] != features.shape[:2]:
+        raise ValueError("local_topk: local and features must share [B, T]")
+    b, t = local.shape[:2]
+
+    def pitch_of(x, width):  # rows evenly spaced (a column slice of wider rows), else a copy
+        try:
+            return x, _row_pitch(x, width, "local_topk")
+        except ValueError:
+            return x.contiguous(), width
+
+    local, lp = pitch_of(local, 2)
+    features, fp = pitch_of(features, 256)
+    fine_lengths = fine_lengths.to(torch.int64).contiguous()
+    local_f32 = torch.empty((b, t, 2), device=dev, dtype=torch.float32)
+    top = torch.empty((b, 2, 256), device=dev, dtype=torch.float32)
+    _lib.launch("tf_local_topk_fwd", dev, local.data_ptr(), lp, features.data_ptr(), fp, fine_lengths.data_ptr(),
+                local_f32.data_ptr(), top.data_ptr(), b, t)
+    return local_f32, top
+
+
+def decoder_heads(deep_rows, fine_rows, global_feature, memory, top, decoder):
+    """The decoder's heads and logits row (reference ``decoder.py:77-89``) in three
+    launches: ``deep_rows``/``fine_rows`` the query reads' BF16 ``[B, 10, 256]``
+    out-projection rows (their 4/4/2 group means are taken inside), ``global_feature``
+    and ``memory`` BF16 ``[B, 256]``, ``top`` FP32 ``[B, 2, 256]``, ``decoder`` the module
+    holding ``voice_lat``, ``music_lat``, ``voice_head``, ``music_head`` and
+    ``file_head``. Returns the FP32 ``[B, 5]`` logits ``[f, v0, m0, v1, m1]``; every
+    projection rounds to BF16 as under BF16 autocast."""
+    from .buffers import _param_bf16
+
+    dev = _lib.require_cuda("decoder_heads", deep_rows, fine_rows, global_feature, memory, top)
+    b = deep_rows.shape[0]
+    shapes = ((deep_rows, (b, 10, 256), torch.bfloat16), (fine_rows, (b, 10, 256), torch.bfloat16),
+              (global_feature, (b, 256), torch.bfloat16), (memory, (b, 256), torch.bfloat16),
+              (top, (b, 2, 256), torch.float32))
+    for x, shape, dtype in shapes:
+        if tuple(x.shape) != shape or x.dtype != dtype:
+            raise ValueError(f"decoder_heads: expected {dtype} {list(shape)}, got {x.dtype} {list(x.shape)}")
+    deep_rows, fine_rows = deep_rows.contiguous(), fine_rows.contiguous()
+    global_feature, memory, top = global_feature.contiguous(), memory.contiguous(), top.contiguous()
+    layers = (decoder.voice_lat[0], decoder.music_lat[0], decoder.voice_head, decoder.music_head,
+              decoder.file_head[0], decoder.file_head[2])
+    params = []
+    for layer in layers:
+        params += [_param_bf16(layer.weight, tuple(layer.weight.shape)), _param_bf16(layer.bias, tuple(layer.bias.shape))]
+    scratch = torch.empty(max(int(_lib.lib().tf_decoder_heads_scratch_bytes(b)), 16), device=dev, dtype=torch.uint8)
+    logits = torch.empty((b, 5), device=dev, dtype=torch.float32)
+    _lib.launch("tf_decoder_heads_fwd", dev, deep_rows.data_ptr(), fine_rows.data_ptr(), global_feature.data_ptr(),
+                memory.data_ptr(), top.data_ptr(), *[t.data_ptr() for t in params], scratch.data_ptr(),
+                scratch.numel(), logits.data_ptr(), b)
+    return logits
+
+
 def end_gather(x, lengths):
     """``x[arange(B), lengths - 1]`` — the last valid row of each batch entry
     (reference ``decoder.py:63``); bit-exact."""

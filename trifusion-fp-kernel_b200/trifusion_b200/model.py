@@ -119,10 +119,17 @@ class LocalCNN(nn.Module):
         self.out = nn.Linear(c.dim, c.dim, bias=False)
 
     def forward(self, x, mask, lengths):
-        h = F.glu(self.up(x), dim=-1)
-        if self.backend == "reference":
-            h = masked(h, mask)
-        h = _depthwise(h, self.dw, mask, lengths, self.backend != "reference")
+        u = self.up(x)
+        if (self.backend != "reference" and _bf16_autocast(u) and u.dtype == torch.bfloat16
+                and u.shape[-1] % 8 == 0):
+            from .kernels.buffers import glu_depthwise
+
+            h = glu_depthwise(u, self.dw, lengths)  # the GLU formed inside the depthwise pass
+        else:
+            h = F.glu(u, dim=-1)
+            if self.backend == "reference":
+                h = masked(h, mask)
+            h = _depthwise(h, self.dw, mask, lengths, self.backend != "reference")
         if self.backend != "reference" and h.is_cuda:
             from .kernels import native
 

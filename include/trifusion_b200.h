@@ -319,7 +319,8 @@ int tf_local_topk_fwd(const void* local, int64_t local_pitch, const void* featur
  * fine_rows are the query reads' BF16 out-projection rows [batch, 10, 256]; deep_q[g] and
  * fine_q[g] are their group means over rows 0-3, 4-7 and 8-9 (rounded once to BF16);
  * global_feature and memory are BF16 [batch, 256], top FP32 [batch, 2, 256] (rounded to
- * BF16 as autocast does for the concatenation). Weights are the BF16 Linear weights
+ * BF16 as autocast does for the concatenation), all contiguous and 16-byte aligned
+ * (else TF_ERR_LAYOUT). Weights are the BF16 Linear weights
  * ([out, in] row-major, 16-byte aligned) and biases: voice/music lat [256, 1280] + [256],
  * voice/music head [2, 256] + [2], file_head[0] [256, 1536] + [256], file_head[2] [1, 256] + [1].
  * Every projection accumulates in FP32, adds the bias and rounds to BF16; SiLU rounds again.

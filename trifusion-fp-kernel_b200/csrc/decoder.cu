@@ -177,6 +177,24 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Masked mean of the chosen rows, in rank order; invalid ranks add 0 * x. All k rows
+// are loaded before the sum, so their latencies overlap.
+__device__ __forceinline__ void topk_mean(const bf16* __restrict__ features, int64_t feat_pitch, int b, int c,
+                                          int T, int k, int valid, const int* sorted_idx, float* __restrict__ top) {
+  const int count = valid < k ? valid : k;
+  for (int j = threadIdx.x; j < kFeature; j += kTopThreads) {
+    float xr[kTopMax];
+#pragma unroll
+    for (int r = 0; r < kTopMax; ++r)
+      xr[r] = r < k ? bf2f(features[(static_cast<int64_t>(b) * T + sorted_idx[r]) * feat_pitch + j]) : 0.f;
+    float acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < kTopMax; ++r)
+      if (r < k) acc += xr[r] * (r < count ? 1.f : 0.f);
+    top[(static_cast<int64_t>(b) * 2 + c) * kFeature + j] = acc / static_cast<float>(count);
+  }
+}
+
 __global__ void __launch_bounds__(kTopThreads) local_topk_kernel(const bf16* __restrict__ local, int64_t local_pitch,
                                                                  const bf16* __restrict__ features,
                                                                  int64_t feat_pitch,
@@ -276,16 +294,7 @@ __global__ void __launch_bounds__(kTopThreads) local_topk_kernel(const bf16* __r
     sorted_idx[rank] = ti;
   }
   __syncthreads();
-  // Masked mean of the chosen rows, in rank order; invalid ranks add 0 * x.
-  const int count = valid < k ? valid : k;
-  for (int j = tid; j < kFeature; j += kTopThreads) {
-    float acc = 0.f;
-    for (int r = 0; r < k; ++r) {
-      const float x = bf2f(features[(static_cast<int64_t>(b) * T + sorted_idx[r]) * feat_pitch + j]);
-      acc += x * (r < count ? 1.f : 0.f);
-    }
-    top[(static_cast<int64_t>(b) * 2 + c) * kFeature + j] = acc / static_cast<float>(count);
-  }
+  topk_mean(features, feat_pitch, b, c, T, k, valid, sorted_idx, top);
 }
 
 // ---------------------------------------------------------------------------
@@ -305,7 +314,7 @@ __global__ void __launch_bounds__(kTopThreads) local_topk_kernel(const bf16* __r
 // ---------------------------------------------------------------------------
 constexpr int kHeadWidth = 256;   // every hidden layer and input part is 256 wide
 constexpr int kHeadRows = 8;      // batch rows per CTA
-constexpr int kHeadCols = 32;     // output columns per CTA (4 per warp)
+constexpr int kHeadCols = 8;      // output columns per CTA (one per warp)
 constexpr int kHeadThreads = 256;
 constexpr int kHeadMaxParts = 6;
 
@@ -326,77 +335,110 @@ struct HeadLayers {
   HeadLayer layer[2];
 };
 
-__device__ __forceinline__ float head_input(const HeadPart& pt, int b, int i) {
+// Raw 16-byte loads of one 8-feature chunk of part `pt` for batch row b (chunk q):
+// `rows` loads for BF16 parts (the rows averaged), two for an FP32 part.
+__device__ __forceinline__ void head_chunk_load(const HeadPart& pt, int b, int q, uint4 (&raw)[4]) {
   if (pt.dtype == TF_F32) {
-    const float* x = static_cast<const float*>(pt.ptr) + b * pt.batch_stride;
-    if (pt.rows == 1) return bf16_round(x[i]);
-    float s = 0.f;
-    for (int r = 0; r < pt.rows; ++r) s += x[r * kHeadWidth + i];
-    return bf16_round(s / static_cast<float>(pt.rows));
+    const float* x = static_cast<const float*>(pt.ptr) + b * pt.batch_stride + 8 * q;
+    raw[0] = *reinterpret_cast<const uint4*>(x);
+    raw[1] = *reinterpret_cast<const uint4*>(x + 4);
+    return;
   }
-  const bf16* x = static_cast<const bf16*>(pt.ptr) + b * pt.batch_stride;
-  if (pt.rows == 1) return bf2f(x[i]);
-  float s = 0.f;
-  for (int r = 0; r < pt.rows; ++r) s += bf2f(x[r * kHeadWidth + i]);
-  return bf16_round(s / static_cast<float>(pt.rows));
+  const bf16* x = static_cast<const bf16*>(pt.ptr) + b * pt.batch_stride + 8 * q;
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+    if (r < pt.rows) raw[r] = *reinterpret_cast<const uint4*>(x + r * kHeadWidth);
+}
+// The chunk's 8 values as the projection reads them (see above).
+__device__ __forceinline__ void head_chunk_values(const HeadPart& pt, const uint4 (&raw)[4], float (&v)[8]) {
+  if (pt.dtype == TF_F32) {
+    const float* f = reinterpret_cast<const float*>(raw);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = bf16_round(f[e]);
+    return;
+  }
+  bf16x8_to_f(raw[0], v);
+  if (pt.rows == 1) return;
+#pragma unroll
+  for (int r = 1; r < 4; ++r) {
+    if (r < pt.rows) {
+      float w[8];
+      bf16x8_to_f(raw[r], w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] += w[e];
+    }
+  }
+  const float inv = static_cast<float>(pt.rows);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = bf16_round(v[e] / inv);
 }
 
-// grid (256 / kHeadCols, ceil(batch / kHeadRows), layers); dynamic shared memory
-// kHeadRows * nparts * 256 floats (the CTA's input rows).
+// grid (256 / kHeadCols, ceil(batch / kHeadRows), layers), every layer of the launch
+// with kParts parts; dynamic shared memory kHeadRows * kParts * 256 floats (the CTA's
+// input rows).
+template <int kParts>
 __global__ void __launch_bounds__(kHeadThreads) head_layer_kernel(const __grid_constant__ HeadLayers L, int batch) {
-  extern __shared__ float xs[];  // [kHeadRows][K]
+  extern __shared__ __align__(16) float xs[];  // [kHeadRows][K]
+  constexpr int K = kParts * kHeadWidth;
+  constexpr int kChunks = kHeadRows * kParts * (kHeadWidth / 8);
+  constexpr int kPerThread = (kChunks + kHeadThreads - 1) / kHeadThreads;
   const HeadLayer& ly = L.layer[blockIdx.z];
-  const int K = ly.nparts * kHeadWidth;
   const int row0 = blockIdx.y * kHeadRows;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int e = tid; e < kHeadRows * K; e += kHeadThreads) {
-    const int r = e / K, i = e - r * K;
-    const int b = row0 + r;
-    xs[e] = b < batch ? head_input(ly.part[i / kHeadWidth], b, i % kHeadWidth) : 0.f;
+  // The warp's weight row (one output column) and every load of the thread's input
+  // chunks are issued before any is used.
+  const int col = blockIdx.x * kHeadCols + warp;
+  const bf16* wrow = ly.w + static_cast<int64_t>(col) * K;
+  uint4 wv[kParts];
+#pragma unroll
+  for (int it = 0; it < kParts; ++it) wv[it] = *reinterpret_cast<const uint4*>(wrow + it * 256 + 8 * lane);
+  uint4 raw[kPerThread][4];
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const int e = tid + j * kHeadThreads;
+    const int r = e / (kParts * 32), pq = e % (kParts * 32);
+    if (e < kChunks && row0 + r < batch) head_chunk_load(ly.part[pq / 32], row0 + r, pq % 32, raw[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const int e = tid + j * kHeadThreads;
+    if (e >= kChunks) continue;
+    const int r = e / (kParts * 32), pq = e % (kParts * 32);
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (row0 + r < batch) head_chunk_values(ly.part[pq / 32], raw[j], v);
+    float* dst = xs + r * K + 8 * pq;
+    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
   }
   __syncthreads();
-  const int col0 = blockIdx.x * kHeadCols + warp * 4;
-  float acc[4][kHeadRows];
+  float acc[kHeadRows];
 #pragma unroll
-  for (int cc = 0; cc < 4; ++cc)
+  for (int r = 0; r < kHeadRows; ++r) acc[r] = 0.f;
 #pragma unroll
-    for (int r = 0; r < kHeadRows; ++r) acc[cc][r] = 0.f;
-  for (int k0 = 8 * lane; k0 < K; k0 += 256) {
-    float xv[kHeadRows][8];
+  for (int it = 0; it < kParts; ++it) {
+    const int k0 = it * 256 + 8 * lane;
+    float wf[8];
+    bf16x8_to_f(wv[it], wf);
 #pragma unroll
     for (int r = 0; r < kHeadRows; ++r) {
       const float4 a = *reinterpret_cast<const float4*>(xs + r * K + k0);
       const float4 c = *reinterpret_cast<const float4*>(xs + r * K + k0 + 4);
-      xv[r][0] = a.x; xv[r][1] = a.y; xv[r][2] = a.z; xv[r][3] = a.w;
-      xv[r][4] = c.x; xv[r][5] = c.y; xv[r][6] = c.z; xv[r][7] = c.w;
-    }
+      const float xv[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
 #pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(ly.w + static_cast<int64_t>(col0 + cc) * K + k0);
-      float wf[8];
-      bf16x8_to_f(wv, wf);
-#pragma unroll
-      for (int r = 0; r < kHeadRows; ++r)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[cc][r] = fmaf(wf[e], xv[r][e], acc[cc][r]);
+      for (int e = 0; e < 8; ++e) acc[r] = fmaf(wf[e], xv[e], acc[r]);
     }
   }
 #pragma unroll
-  for (int cc = 0; cc < 4; ++cc)
+  for (int r = 0; r < kHeadRows; ++r)
 #pragma unroll
-    for (int r = 0; r < kHeadRows; ++r)
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[cc][r] += __shfl_xor_sync(0xffffffffu, acc[cc][r], o);
-  // Lane l stores column col0 + l / 8 of row row0 + l % 8.
-  const int cc = lane >> 3, r = lane & 7;
+    for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+  // Lane r stores row row0 + r.
   float v = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < kHeadRows; ++j)
-      if (i == cc && j == r) v = acc[i][j];
-  const int b = row0 + r, col = col0 + cc;
-  if (b < batch) {
+  for (int r = 0; r < kHeadRows; ++r)
+    if (lane == r) v = acc[r];
+  const int b = row0 + lane;
+  if (lane < kHeadRows && b < batch) {
     const float a = bf16_round(v + bf2f(ly.bias[col]));
     ly.out[static_cast<int64_t>(b) * kHeadWidth + col] = __float2bfloat16_rn(a / (1.f + expf(-a)));
   }
@@ -515,7 +557,8 @@ int tf_decoder_heads_fwd(const void* deep_rows, const void* fine_rows, const voi
   for (const void* p : ptrs)
     if (!p) return TF_ERR_ARG;
   if (scratch_bytes < tf_decoder_heads_scratch_bytes(batch)) return TF_ERR_SIZE;
-  const void* vec[] = {w_voice, w_music, w_vhead, w_mhead, w_file1, w_file2, scratch};
+  const void* vec[] = {deep_rows, fine_rows, global_feature, memory, top,   w_voice, w_music,
+                       w_vhead,   w_mhead,   w_file1,        w_file2, scratch};
   for (const void* p : vec)
     if (!tf::aligned16(p)) return TF_ERR_LAYOUT;
   const int st = tf::check_device();
@@ -549,7 +592,7 @@ int tf_decoder_heads_fwd(const void* deep_rows, const void* fine_rows, const voi
     ly.out = g == 0 ? voice : music;
   }
   const dim3 grid_lat(tf::kHeadWidth / tf::kHeadCols, (batch + tf::kHeadRows - 1) / tf::kHeadRows, 2);
-  tf::head_layer_kernel<<<grid_lat, tf::kHeadThreads, tf::kHeadRows * 5 * tf::kHeadWidth * sizeof(float), s>>>(L,
+  tf::head_layer_kernel<5><<<grid_lat, tf::kHeadThreads, tf::kHeadRows * 5 * tf::kHeadWidth * sizeof(float), s>>>(L,
                                                                                                             batch);
   int e = tf::launch_status();
   if (e != TF_OK) return e;
@@ -568,7 +611,7 @@ int tf_decoder_heads_fwd(const void* deep_rows, const void* fine_rows, const voi
     ly.out = fileh;
   }
   const dim3 grid_file(tf::kHeadWidth / tf::kHeadCols, (batch + tf::kHeadRows - 1) / tf::kHeadRows, 1);
-  tf::head_layer_kernel<<<grid_file, tf::kHeadThreads, tf::kHeadRows * 6 * tf::kHeadWidth * sizeof(float), s>>>(
+  tf::head_layer_kernel<6><<<grid_file, tf::kHeadThreads, tf::kHeadRows * 6 * tf::kHeadWidth * sizeof(float), s>>>(
       F, batch);
   e = tf::launch_status();
   if (e != TF_OK) return e;

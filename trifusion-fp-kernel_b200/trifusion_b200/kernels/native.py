@@ -281,8 +281,13 @@ def decoder_heads(deep_rows, fine_rows, global_feature, memory, top, decoder):
     for x, shape, dtype in shapes:
         if tuple(x.shape) != shape or x.dtype != dtype:
             raise ValueError(f"decoder_heads: expected {dtype} {list(shape)}, got {x.dtype} {list(x.shape)}")
-    deep_rows, fine_rows = deep_rows.contiguous(), fine_rows.contiguous()
-    global_feature, memory, top = global_feature.contiguous(), memory.contiguous(), top.contiguous()
+
+    def aligned(x):  # contiguous and 16-byte aligned (the kernels read 16-byte vectors)
+        x = x.contiguous()
+        return x if x.data_ptr() % 16 == 0 else x.clone()
+
+    deep_rows, fine_rows, global_feature, memory, top = (aligned(x) for x in
+                                                         (deep_rows, fine_rows, global_feature, memory, top))
     layers = (decoder.voice_lat[0], decoder.music_lat[0], decoder.voice_head, decoder.music_head,
               decoder.file_head[0], decoder.file_head[2])
     params = []

@@ -1119,17 +1119,42 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       auto fold_predecessors = [&]() {
         int start = 0;
         if (lookback) {
-          // Nearest predecessor with a published outgoing state (one thread decides).
-          if (et == 0) {
-            int y = c - 1;
-            for (; y >= 0; --y) {
-              uint32_t seen = 0;
-              const int ub = unit_index(shp, y, dir, b, h);
-              ok &= wait_flag(reinterpret_cast<const uint32_t*>(uws_of(ub) + kUnitFlag), epoch, kFlagAgg, seen,
-                              p0.flag_wait_ns);
-              if (static_cast<int>(seen - epoch) >= static_cast<int>(kFlagIncl)) break;
+          // Nearest predecessor y with a published outgoing state such that every unit
+          // after it has published its dS (y = -1: none, start from chunk 0). One warp
+          // reads the flags of 32 predecessors at once (lane l: chunk base - l) and
+          // re-reads the window until the nearest published state is reached through
+          // published dS; a window of published dS without a state moves 32 chunks back.
+          if (et < 32) {
+            int base = c - 1, y = -1;
+            const uint64_t t0 = global_timer_ns();
+            for (;;) {
+              const int x = base - lane;
+              int rel = static_cast<int>(kFlagIncl);  // chunk -1 acts as a published zero state
+              if (x >= 0)
+                rel = static_cast<int>(
+                    ld_acquire_u32(reinterpret_cast<const uint32_t*>(uws_of(unit_index(shp, x, dir, b, h)) + kUnitFlag)) -
+                    epoch);
+              const uint32_t incl = __ballot_sync(0xffffffffu, x < 0 || rel >= static_cast<int>(kFlagIncl));
+              const uint32_t agg = __ballot_sync(0xffffffffu, x < 0 || rel >= static_cast<int>(kFlagAgg));
+              if (incl) {
+                const int j = __ffs(static_cast<int>(incl)) - 1;  // nearest published state
+                const uint32_t need = (1u << j) - 1u;              // the dS after it
+                if ((agg & need) == need) {
+                  y = base - j;
+                  break;
+                }
+              } else if (agg == 0xffffffffu) {
+                base -= 32;
+                continue;
+              }
+              if (global_timer_ns() - t0 > p0.flag_wait_ns) {
+                ok = false;
+                y = -1;
+                break;
+              }
+              __nanosleep(64);
             }
-            mi.lookback_start = y;  // -1: none
+            if (lane == 0) mi.lookback_start = y;
           }
           bar_sync_n(kBarEpilogue, kEpilogueThreads);
           const int y = mi.lookback_start;

@@ -80,6 +80,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-box", action="store_true",
                     help="cfg1: skip the box-level audio-seconds/s sweep (cfg4) recorded under 'box'")
+    ap.add_argument("--reference-gpu", action="store_true",
+                    help="cfg1/cfg2, one GPU: also time the reference's own Triton fused_mamba "
+                         "(installed in baseline/_ref) on this GPU, as 'reference_gpu'")
     ap.add_argument("--profile-eager", type=int, default=0, metavar="K",
                     help="model workloads: run K untimed eager forwards and exit (for ncu launch lists)")
     args = ap.parse_args()
@@ -469,6 +472,10 @@ def run_recurrence(args, wl):
         cpu = {"value": b * t * n / el, "unit": "tokens/s", "cores": host_threads(), "torch_threads": _torch_threads(), "kind": "port",
                "sample": f"{n} full {args.workload} batches through the numpy oracle (FP32), {el:.1f} s"}
 
+    ref_gpu = None
+    if args.reference_gpu and world == 1:
+        ref_gpu = reference_gpu_record(sets, qw, kw, dev, ms_per_step * 1e3)
+
     box = None
     if args.workload == "cfg1" and not args.no_box:
         # The box-level sweep of the metric's audio-seconds/s (cfg4), on the same ranks:
@@ -504,9 +511,68 @@ def run_recurrence(args, wl):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
     if box is not None:
         line["box"] = dict(workload="cfg4", scaling="strong", **box)
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_record(sets, qw, kw, dev, ours_us):
+    """The reference's own GPU path on the same inputs and GPU: its Triton RMSNorm on q
+    and k, then its Triton ``fused_mamba`` (``mamba_fused.py:155-191``), timed the same
+    way as our step (one CUDA graph over every input set, CUDA events). The reference
+    has no length mask inside the recurrence (it masks afterwards, ``model.py:174``),
+    so its step covers all T steps of every row. Also reports the relative L2 distance
+    between the two outputs over the valid rows (the reference rounds its operands to
+    BF16, ours to FP16 with exponents). Needs the reference installed under
+    ``baseline/_ref`` (``pip install --no-index --no-deps --target baseline/_ref``)."""
+    import torch
+
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "trifusion_l4").is_dir():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    sys.path.insert(0, str(ref_root))
+    try:
+        import trifusion_l4.mamba_fused as ref_fused
+        import trifusion_l4.kernels.native as ref_native
+    except Exception as exc:  # noqa: BLE001 - reported, not raised
+        return {"unavailable": f"import of the reference failed: {exc!r}"[:200]}
+
+    def ref_step(st):
+        a = st["args"]
+        return ref_fused.fused_mamba(ref_native.rms(a[0], qw), ref_native.rms(a[1], kw), *a[2:])
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        y_ref = ref_step(sets[0]).float()
+        torch.cuda.synchronize(dev)
+        y_our = sets[0]["out"].float()
+        lengths = sets[0]["lengths"]
+        valid = (torch.arange(y_ref.shape[1], device=dev)[None, :] < lengths[:, None])[:, :, None, None]
+        diff = (y_ref - y_our) * valid
+        rel = float(diff.norm() / (y_ref * valid).norm())
+        for i in range(3):
+            ref_step(sets[i % len(sets)])
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for st in sets:
+                ref_step(st)
+        graph.replay()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / (reps * len(sets))
+    del graph
+    return {"us_per_step": us, "ours_us_per_step": ours_us, "ours_speedup": us / ours_us,
+            "rel_l2_vs_ours_valid_rows": rel,
+            "what": "reference Triton RMSNorm(q), RMSNorm(k) + fused_mamba, graph replays over the same input sets"}
 
 
 def _student(dev, tmpdir, optimized=True):

@@ -93,3 +93,16 @@ def test_host_model_matches_reference_with_oracle_recurrence(case, tmp_path, mon
         out = model(audio, lengths, channels)
     np.testing.assert_allclose(out["logits"].numpy(), g["logits"], rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(out["embedding"].numpy(), g["embedding"], rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("case", ["small", "cfg3"])
+def test_reference_gpu_goldens_are_consistent(case):
+    """The reference's FP32 path run on the GPU (``make_model_golden_gpu.py``) reproduces
+    its CPU FP32 goldens, and its deployed BF16 path stays within 1e-2 of them: the
+    GPU fixture is the same model on the same audio."""
+    sig = lambda x: 1 / (1 + np.exp(-np.asarray(x, np.float64)))  # noqa: E731
+    g = np.load(GOLDEN / f"model_{case}.npz")
+    r = np.load(GOLDEN / f"model_{case}_ref_gpu.npz")
+    assert r["logits_portable"].shape == g["logits"].shape == r["logits_deployed"].shape
+    assert np.abs(sig(r["logits_portable"]) - sig(g["logits"])).max() <= 1e-3
+    assert np.abs(sig(r["logits_deployed"]) - sig(g["logits"])).max() <= 1e-2

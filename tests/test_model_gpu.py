@@ -14,6 +14,13 @@ Bounds, on sigmoid probabilities (measured values in brackets: small, cfg3):
   logits [6.8e-3, 5.4e-3] and its BF16-autocast logits [2.9e-3, 5.2e-3]. BF16
   GEMM/convolution operands alone move this randomly initialised network by
   6-7e-3 (the reference's FP32 against its own BF16 autocast).
+* the reference's own deployed path (its fused Triton kernels under BF16 autocast,
+  ``load_student(optimized=True)`` + ``InferenceEngine``, run on a B200 by
+  ``tests/golden/make_model_golden_gpu.py``) is itself [4.9e-3, 8.0e-3] from its FP32
+  logits on these synthetic models, so the north star's 2e-3 is out of reach for the
+  reference as well. This library's model is held to that gap: against the FP32 logits
+  within the reference's worst deployed gap over the cases (8.05e-3) [6.8e-3, 5.4e-3],
+  and against the reference's deployed logits within 1.2e-2 [1.9e-3, 9.7e-3].
 * with FP32 GEMMs and no autocast, against the reference's FP32 logits: 1.2e-2 with
   the oracle recurrence on FP32 operands [3.5e-3, 9.4e-3] and 1.5e-2 with the CUDA
   recurrence [4.0e-3, 1.1e-2]. This library's norm, front-end and attention kernels
@@ -44,6 +51,7 @@ PROB_TOL = 2.5e-3      # the recurrence's share (CUDA vs oracle recurrence in th
 PROB_TOL_BF16 = 8e-3   # whole model (BF16 autocast) vs the reference's FP32 / BF16-autocast logits
 PROB_TOL_FP32_REST = 1.2e-2  # FP32 GEMMs, oracle recurrence on FP32 operands, vs reference FP32 logits
 PROB_TOL_FP32 = 1.5e-2       # FP32 GEMMs, CUDA recurrence, vs reference FP32 logits
+PROB_TOL_DEPLOYED = 1.2e-2   # optimized model vs the reference's deployed (GPU, BF16) logits
 
 
 def case_inputs(case, tmp_path):
@@ -75,6 +83,28 @@ def test_optimized_model_matches_reference_probabilities(case, tmp_path):
     second = graph_engine(*inputs)
     assert graph_engine.graph_hits == 2 and not graph_engine.disabled_shapes
     assert torch.equal(first, eager) and torch.equal(second, eager)
+
+
+def reference_deployed_gap():
+    """The largest probability difference, over the golden cases, between the
+    reference's deployed logits (GPU, fused Triton, BF16 autocast) and its FP32 logits."""
+    return max(np.abs(probabilities(np.load(GOLDEN / f"model_{c}_ref_gpu.npz")["logits_deployed"])
+                      - probabilities(np.load(GOLDEN / f"model_{c}.npz")["logits"])).max()
+               for c in ("small", "cfg3"))
+
+
+@pytest.mark.parametrize("case", ["small", "cfg3"])
+def test_model_within_the_reference_deployed_gap(case, tmp_path):
+    g, path, inputs = case_inputs(case, tmp_path)
+    deployed = np.load(GOLDEN / f"model_{case}_ref_gpu.npz")["logits_deployed"]
+    model = load_student(path, optimized=True)
+    ours = probabilities(InferenceEngine(model, graphs=False)(*inputs))
+    gap = np.abs(ours - probabilities(g["logits"])).max()
+    bound = reference_deployed_gap()
+    direct = np.abs(ours - probabilities(deployed)).max()
+    print(case, "vs reference FP32", gap, "(reference deployed gap", bound, ") vs reference deployed", direct)
+    assert gap <= bound, (gap, bound)
+    assert direct <= PROB_TOL_DEPLOYED, direct
 
 
 def _oracle_multi(bf16_io):

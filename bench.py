@@ -81,8 +81,9 @@ def parse():
     ap.add_argument("--no-box", action="store_true",
                     help="cfg1: skip the box-level audio-seconds/s sweep (cfg4) recorded under 'box'")
     ap.add_argument("--reference-gpu", action="store_true",
-                    help="cfg1/cfg2, one GPU: also time the reference's own Triton fused_mamba "
-                         "(installed in baseline/_ref) on this GPU, as 'reference_gpu'")
+                    help="one GPU: also time the reference's own GPU path (installed in baseline/_ref) "
+                         "on this GPU, as 'reference_gpu': its Triton fused_mamba for cfg1/cfg2, its "
+                         "deployed InferenceEngine(graphs=True) for cfg3")
     ap.add_argument("--profile-eager", type=int, default=0, metavar="K",
                     help="model workloads: run K untimed eager forwards and exit (for ncu launch lists)")
     args = ap.parse_args()
@@ -608,6 +609,9 @@ def run_model(args, wl):
     audio, lengths, channels = synthetic_audio(b, n, lengths=lengths, seed=rank)
     with tempfile.TemporaryDirectory() as tmp:
         model = _student(dev, tmp)
+        ref_model = None
+        if args.reference_gpu and world == 1:
+            ref_model = _reference_student(dev, tmp)
     inputs = tuple(x.to(dev) for x in (audio, lengths, channels))
     if args.profile_eager:
         eager = InferenceEngine(model, graphs=False)
@@ -672,6 +676,9 @@ def run_model(args, wl):
     torch.cuda.synchronize(dev)
     e_ms = e0.elapsed_time(e1) / max(n_e2e, 1)
     e_ms = max_over_ranks(e_ms, world, dev)
+    ref_gpu = None
+    if ref_model is not None:
+        ref_gpu = reference_model_gpu_record(ref_model, engine, inputs, flush, args, audio_s, ms_per_step)
     if world > 1:
         dist.barrier()
         engine.clear()
@@ -694,7 +701,64 @@ def run_model(args, wl):
                 "pipeline": "HostPipeline depth 2 (copies overlap the forward; L2 flush timed)"},
         "clocks": sampler.summary(tl0, tw1),
     }
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
     print(json.dumps(line), flush=True)
+
+
+def _reference_student(dev, tmpdir):
+    """The reference's own deployed model (``baseline/_ref``) on the same synthetic
+    checkpoint, or a string saying why it is unavailable."""
+    from trifusion_b200.synthetic import student_checkpoint
+
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "trifusion_l4").is_dir():
+        return "the reference is not installed under baseline/_ref"
+    sys.path.insert(0, str(ref_root))
+    try:
+        from trifusion_l4.runtime import load_student as ref_load
+    except Exception as exc:  # noqa: BLE001 - reported, not raised
+        return f"import of the reference failed: {exc!r}"[:200]
+    path = student_checkpoint(Path(tmpdir) / "reference_student.pt", STUDENT, seed=0)
+    return ref_load(path, optimized=True, device=dev)
+
+
+def reference_model_gpu_record(ref_model, engine, inputs, flush, args, audio_s, ours_ms):
+    """The reference's deployed path on the same GPU, batch and weights: its
+    ``InferenceEngine(graphs=True)`` (fused Triton kernels, BF16 autocast, CUDA graph
+    replay; ``runtime.py:67-138``), timed like our step (an L2 flush before every step,
+    outside the CUDA events). Also the largest difference between the two engines'
+    sigmoid probabilities on this batch."""
+    import torch
+
+    if isinstance(ref_model, str):
+        return {"unavailable": ref_model}
+    from trifusion_l4.runtime import InferenceEngine as RefEngine
+
+    ref_engine = RefEngine(ref_model, graphs=True, max_graphs=1, max_reserved_gib=BENCH_RESERVED_GIB)
+    dev = inputs[0].device
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 1)):
+        ref_logits = ref_engine(*inputs)
+    ours = engine(*inputs)
+    torch.cuda.synchronize(dev)
+    diff = float((ours.float().sigmoid() - ref_logits.float().sigmoid()).abs().max())
+    steps = max(1, min(args.steps, 50))
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in events:
+        flush.fill_(1)
+        e0.record(stream)
+        ref_engine(*inputs)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in events) / steps
+    ref_engine.clear()
+    return {"ms_per_step": ms, "value": audio_s / (ms / 1e3), "unit": AUDIO_METRIC_UNIT, "steps": steps,
+            "graph_hits": ref_engine.graph_hits, "disabled_shapes": len(ref_engine.disabled_shapes),
+            "ours_ms_per_step": ours_ms, "ours_speedup": ms / ours_ms,
+            "max_probability_difference_vs_ours": diff,
+            "what": "reference load_student(optimized=True) + InferenceEngine(graphs=True) on the same "
+                    "synthetic checkpoint and batch"}
 
 
 def box_sweep(wl, steps, warmup, world, rank, local, dev):

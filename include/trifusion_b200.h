@@ -496,6 +496,22 @@ int tf_front_residual_fwd(const void* h, const void* skip, int dtype, const int6
 int tf_bands_fwd(const void* x, int dtype, void* y, int batch, int time, int freq, int channels,
                  void* stream);
 
+/* Valid-row transfer between padded device tensors and a packed buffer (raw
+ * bytes, either direction). No counterpart kernel in the reference, which
+ * copies whole padded tensors to the device (audio.py:52-66 pads every batch to
+ * its longest clip); rows at or past a clip's length carry nothing the
+ * recurrence reads, so a host-fed pipeline moves only the valid ones.
+ * Tensor i is `dense[i]`, laid out [batch][groups[i]][steps[i]][step_bytes[i]]
+ * contiguously; `lengths` (device, int64 [batch]) gives each clip's valid
+ * steps (clamped to [0, steps[i]]). The packed buffer holds, tensor after
+ * tensor, for each clip b and group g the valid steps of (b, g) back to back;
+ * each tensor's region starts at a 16-byte-aligned offset. `to_dense` = 1
+ * copies packed -> dense (the padding rows are left as they are), 0 copies
+ * dense -> packed. At most 16 tensors and 65535 clips per call. */
+int tf_ragged_copy_fwd(void* packed, void* const* dense, const int64_t* groups, const int64_t* steps,
+                       const int64_t* step_bytes, int ntensors, const int64_t* lengths, int batch,
+                       int to_dense, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,6 +78,7 @@ SIGNATURES = {
     "tf_pool4_out_fwd": [_p, _i, _p, _p, _i, _i, _i, _i, _p],
     "tf_front_residual_fwd": [_p, _p, _i, _p, _p, _i, _i, _i, _i, _p],
     "tf_bands_fwd": [_p, _i, _p, _i, _i, _i, _i, _p],
+    "tf_ragged_copy_fwd": [_p, _p, _p, _p, _p, _i, _p, _i, _i, _p],
     "tf_glu_depthwise_fwd": [_p, _p, _p, _p, _p, _i, _i, _i, _i, _p],
     "tf_local_topk_fwd": [_p, _q, _p, _q, _p, _p, _p, _i, _i, _p],
     "tf_decoder_heads_scratch_bytes": [_i],

@@ -141,23 +141,30 @@ def recurrence_config(workload, wl, base, lengths, world):
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons in the background."""
+    """Samples nvidia-smi SM clocks and throttle reasons in the background.
+
+    One sampler per node, on rank 0, covers the GPUs of every local rank (indices
+    0..world-1) at the profiling recipe's 200 ms interval; the other ranks sample
+    nothing, so N ranks do not start N pollers of the driver while they are timed."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, rank=0, world=1):
+        self.active = rank == 0
+        self.ids = list(range(max(world, 1)))
         self.samples = []
         self.proc = None
         self.thread = None
 
     def start(self):
+        if not self.active:
+            return
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                ["nvidia-smi", "--id=" + ",".join(str(i) for i in self.ids), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -181,25 +188,31 @@ class ClockSampler:
             self.thread.join(timeout=2)
 
     def summary(self, t0, t1):
+        """Median SM clock of the slowest sampled GPU, the union of throttle reasons and
+        each GPU's median (None on ranks that do not sample)."""
+        if not self.active:
+            return None
         rows = [s for ts, s in self.samples if t0 <= ts <= t1]
-        if not rows:  # region shorter than the sampling interval: nearest samples
-            rows = [s for ts, s in sorted(self.samples, key=lambda x: abs(x[0] - (t0 + t1) / 2))[:3]]
-        mhz, max_mhz, reasons = [], None, set()
+        if len(rows) < len(self.ids):  # region shorter than the sampling interval: nearest samples
+            rows = [s for ts, s in sorted(self.samples, key=lambda x: abs(x[0] - (t0 + t1) / 2))[:3 * len(self.ids)]]
+        mhz, max_mhz, reasons = {}, None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for row in rows:
             f = [x.strip() for x in row.split(",")]
             if len(f) < 9:
                 continue
             try:
-                mhz.append(float(f[1]))
+                mhz.setdefault(int(f[0]), []).append(float(f[1]))
                 max_mhz = float(f[2])
             except ValueError:
                 continue
             for name, flag in zip(names, f[5:9]):
                 if flag.lower().startswith("active"):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz,
-                "reasons": sorted(reasons), "samples": len(mhz)}
+        per_gpu = {i: statistics.median(v) for i, v in sorted(mhz.items())}
+        return {"sm_mhz": min(per_gpu.values()) if per_gpu else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples": sum(len(v) for v in mhz.values()),
+                "per_gpu_sm_mhz": per_gpu}
 
 
 def cpu_port_time(workload, inputs_np, lengths_np, qw, kw, budget_s=12.0):
@@ -305,14 +318,20 @@ def setup_dist():
 
 
 def max_over_ranks(value, world, dev):
+    return max(per_rank(value, world, dev))
+
+
+def per_rank(value, world, dev):
+    """Every rank's value (all-gathered), in rank order."""
     if world == 1:
-        return value
+        return [value]
     import torch
     import torch.distributed as dist
 
     t = torch.tensor([value], device=dev, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
 
 
 def main():
@@ -334,7 +353,9 @@ def run_recurrence(args, wl):
     world, rank, local, dev = setup_dist()
 
     b, t, h = wl["batch"], wl["time"], wl["heads"]
-    lengths_cpu = make_lengths(wl["lengths"], b, seed=rank)
+    # Weak scaling: every rank gets the same shape and lengths (the per-GPU work of the
+    # printed config), its own input values.
+    lengths_cpu = make_lengths(wl["lengths"], b, seed=0)
     base = recurrence_inputs(b, t, h, kind="baseline", seed=rank)
     qw_cpu, kw_cpu = norm_weight(128, 1), norm_weight(128, 2)
     qw, kw = qw_cpu.to(dev), kw_cpu.to(dev)
@@ -372,7 +393,7 @@ def run_recurrence(args, wl):
                     step(i)
             tail.replay()
         # load phase so clock samples reflect a busy GPU
-        sampler = ClockSampler(local)
+        sampler = ClockSampler(rank, world)
         sampler.start()
         tl0 = time.time()
         while time.time() - tl0 < 0.6:
@@ -396,6 +417,7 @@ def run_recurrence(args, wl):
             dist.barrier()
         sampler.stop()
     ms = ev0.elapsed_time(ev1)
+    rank_ms = per_rank(ms / max(args.steps, 1), world, dev)
     # L2-warm reference figure (not the headline): the same launch repeated on one input set, which
     # then stays resident in the 126 MB L2. Timed after, and outside, the measured region.
     with torch.cuda.stream(stream):
@@ -412,11 +434,7 @@ def run_recurrence(args, wl):
         w1.record(stream)
         torch.cuda.synchronize(dev)
         warm_ms_per_step = w0.elapsed_time(w1) / (20 * nsets)
-    if world > 1:
-        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-    ms_per_step = ms / max(args.steps, 1)
+    ms_per_step = max(rank_ms)
     value = world * b * t / (ms_per_step / 1e3)
     hbm_peak, peak_kind = peaks()
     achieved = step_bytes / (ms_per_step / 1e3) / 1e9
@@ -544,6 +562,7 @@ def run_recurrence(args, wl):
                             "output rows back; copies overlap kernels; the device work of a step (row scatter, "
                             "fused_recurrence, row gather) replayed as a CUDA graph", "dense": dense_e2e},
         "gpu_launches": args.steps,
+        "rank_ms_per_step": rank_ms,
         "clocks": clocks,
     }
     if cpu is not None:
@@ -641,7 +660,7 @@ def run_model(args, wl):
     world, rank, local, dev = setup_dist()
     configure_runtime()
     b, n = wl["batch"], wl["samples"]
-    lengths = make_lengths(wl["lengths"], b, seed=rank)
+    lengths = make_lengths(wl["lengths"], b, seed=0)  # every rank: the config's lengths, its own audio
     audio, lengths, channels = synthetic_audio(b, n, lengths=lengths, seed=rank)
     with tempfile.TemporaryDirectory() as tmp:
         model = _student(dev, tmp)
@@ -661,7 +680,7 @@ def run_model(args, wl):
     for _ in range(max(args.warmup, 1)):
         engine(*inputs)
     torch.cuda.synchronize(dev)
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(rank, world)
     sampler.start()
     tl0 = time.time()
     while time.time() - tl0 < 0.6:
@@ -845,7 +864,7 @@ def box_sweep(wl, steps, warmup, world, rank, local, dev):
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(rank, world)
     sampler.start()
     tl0 = time.time()
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -857,8 +876,8 @@ def box_sweep(wl, steps, warmup, world, rank, local, dev):
     torch.cuda.synchronize(dev)
     tw1 = time.time()
     sampler.stop()
-    ms = max_over_ranks(sum(a.elapsed_time(c) for a, c in events), world, dev)
-    ms_per_step = ms / max(steps, 1)
+    rank_ms = per_rank(sum(a.elapsed_time(c) for a, c in events) / max(steps, 1), world, dev)
+    ms_per_step = max(rank_ms)
     assert idx.numel() == len(records) and bool(torch.isfinite(logits).all())
 
     h2d = sum(x.numel() * x.element_size() for h in host for x in h)
@@ -885,7 +904,7 @@ def box_sweep(wl, steps, warmup, world, rank, local, dev):
     engine.clear()
     return {
         "value": total_audio_s / (ms_per_step / 1e3), "unit": AUDIO_METRIC_UNIT, "steps": steps,
-        "warmup": max(warmup, 1), "ms_per_step": ms_per_step,
+        "warmup": max(warmup, 1), "ms_per_step": ms_per_step, "rank_ms_per_step": rank_ms,
         "config": {"student": STUDENT, "clips": len(records), "audio_seconds": total_audio_s,
                    "batches": len(plan), "batches_on_rank0": len(mine) if rank == 0 else None,
                    "graph_shapes_on_rank0": len(shapes) if rank == 0 else None,

@@ -3,9 +3,13 @@
 //
 // Work units. A unit is one 64-step chunk c of one (batch b, head h) row. Units
 // are numbered chunk-major, u = ((c*ndir + dir)*B + b)*H + h, and handed out in
-// increasing order by an atomic ticket, so a unit only ever depends on units
+// chunk-major order by an atomic ticket, so a unit only ever depends on units
 // already held by running CTAs: the kernel cannot deadlock, whether or not every
-// CTA of the grid is resident. A CTA takes at most ceil(non-empty units / CTAs)
+// CTA of the grid is resident. Tickets count only non-empty units (chunks that
+// start before their row's length): within chunk c, ticket r is head r % H of the
+// (r / H)-th row in order of decreasing length, so no CTA spends an iteration on
+// a chunk past its row's end (launches of more than kMapRows rows or kMapChunks
+// chunks per row hand out every unit instead and skip the empty ones). A CTA takes at most ceil(non-empty units / CTAs)
 // non-empty units (tickets are claimed one unit ahead; without the quota a CTA
 // whose first units were cheap would take one more than the rest), and chunks
 // wholly past their row's length are zeroed by a static share per CTA.
@@ -101,7 +105,12 @@ constexpr uint32_t kStageTmaBytes = 53248;
 constexpr uint32_t kOffPhase = kOffStage + kStageBytes;  // FP32 [64][33]
 constexpr uint32_t kOffTeff = kOffPhase + 64 * 33 * 4;   // int [2][kTeffTable]: valid length of every row
 constexpr int kTeffTable = 1024;                          // batches beyond this read lengths[] directly
-constexpr uint32_t kOffMisc = kOffTeff + 2 * kTeffTable * 4;
+// Ticket map (launches of at most kMapRows rows and kMapChunks chunks per row): the rows
+// ordered by valid length, longest first (short), and per chunk c the number of
+// non-empty units of the chunks before c (int, kMapChunks + 1 entries).
+constexpr int kMapRows = 256, kMapChunks = 512;
+constexpr uint32_t kOffMap = kOffTeff + 2 * kTeffTable * 4;
+constexpr uint32_t kOffMisc = kOffMap + ((kMapRows * 2 + (kMapChunks + 1) * 4 + 15) & ~15u);
 
 struct SlotHeader {
   int unit;  // -1: no more work
@@ -495,6 +504,44 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
   const uint32_t epoch = mi.epoch;
   bool ok = true;
 
+  // ---- ticket map: tickets -> non-empty units -------------------------------------
+  const bool use_map = p0.B <= kTeffTable && kDirs * p0.B <= kMapRows && nck <= kMapChunks;
+  short* map_order = reinterpret_cast<short*>(smem + kOffMap);
+  int* map_pref = reinterpret_cast<int*>(smem + kOffMap + kMapRows * 2);
+  if (use_map) {
+    const int nrows = kDirs * p0.B;
+    auto teff_row = [&](int i) { return i < p0.B ? teff_tab[i] : teff_tab[kTeffTable + i - p0.B]; };
+    for (int i = tid; i < nrows; i += kThreads) {  // rank of row i: longer rows first, ties by index
+      const int ti = teff_row(i);
+      int rank = 0;
+      for (int j = 0; j < nrows; ++j) {
+        const int tj = teff_row(j);
+        rank += (tj > ti) | ((tj == ti) & (j < i));
+      }
+      map_order[rank] = static_cast<short>(i);
+    }
+    for (int c = tid; c <= nck; c += kThreads) {  // non-empty units of the chunks before c
+      int before = 0;
+      for (int j = 0; j < nrows; ++j) before += min((teff_row(j) + kChunk - 1) / kChunk, c);
+      map_pref[c] = before * p0.H;
+    }
+    __syncthreads();
+  }
+  // The unit of ticket tk (shp.units once every non-empty unit is handed out).
+  auto ticket_unit = [&](int tk) -> int {
+    if (!use_map) return tk;
+    if (tk >= map_pref[nck]) return shp.units;
+    int lo = 0, hi = nck;  // map_pref[lo] <= tk < map_pref[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (map_pref[mid] <= tk) lo = mid; else hi = mid;
+    }
+    const int r = tk - map_pref[lo];
+    const int row = map_order[r / p0.H];
+    const int dd = row >= p0.B ? 1 : 0;
+    return unit_index(shp, lo, dd, row - dd * p0.B, r % p0.H);
+  };
+
   if (warp < 8) {
     // =========================== producer ===========================
     const int t = tid >> 2, s4 = tid & 3;  // row, sub-slot (4 threads per row)
@@ -608,6 +655,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       if (lane == 0) {
         const long long g = gridDim.x;
         mi.quota = p0.B <= kTeffTable ? static_cast<int>((nonempty + g - 1) / g) : 0x7fffffff;
+        mi.next_ticket = ticket_unit(mi.next_ticket);  // the first ticket, claimed at set-up
       }
     }
     bar_sync_n(kBarProducer, kProducerThreads);
@@ -657,12 +705,12 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       // Short rows claim at once; long rows once the unit's tiles are under way (below):
       // the later a unit is claimed, the fewer of its row's predecessors are still
       // unpublished when its epilogue looks back.
-      if (!kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
+      if (!kLook && tid == kClaimThread && held < quota) my_next = ticket_unit(atomicAdd(ws_ticket, 1));
       if (nv == 0) {
         // Whole chunk past the length: no tensor work, no slot; its rows are
         // zeroed after the loop. (Every later chunk of this row is empty too,
         // so nobody reads its state.)
-        if (kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
+        if (kLook && tid == kClaimThread && held < quota) my_next = ticket_unit(atomicAdd(ws_ticket, 1));
         if (tid == kClaimThread) mi.next_ticket = my_next;
         bar_sync_n(kBarProducer, kProducerThreads);
         stage_unit(mi.next_ticket);
@@ -868,7 +916,7 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       }
       bar_sync_n(kBarProducer, kProducerThreads);
       // Long rows: the next unit is claimed here and staged at the end of the iteration.
-      if (kLook && tid == kClaimThread && held < quota) my_next = atomicAdd(ws_ticket, 1);
+      if (kLook && tid == kClaimThread && held < quota) my_next = ticket_unit(atomicAdd(ws_ticket, 1));
       const float total = hd.cs[kChunk - 1];
       // Decay reference of the unit: mu near the middle of the cumsum's range, with
       // E = total - mu an integer, so that the decay-weighted values vs below are

@@ -466,6 +466,33 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
     return p0.B <= kTeffTable ? teff_tab[dd * kTeffTable + bb] : row_length(pr, bb);
   };
 
+  // ---- ticket map: tickets -> non-empty units -------------------------------------
+  // Built by warps 1-15 while warp 0 allocates TMEM and sets up the barriers.
+  const bool use_map = p0.B <= kTeffTable && kDirs * p0.B <= kMapRows && nck <= kMapChunks;
+  short* map_order = reinterpret_cast<short*>(smem + kOffMap);
+  int* map_pref = reinterpret_cast<int*>(smem + kOffMap + kMapRows * 2);
+  if (use_map) {
+    __syncthreads();  // the length table is complete
+    if (warp > 0) {
+      const int nrows = kDirs * p0.B;
+      auto teff_row = [&](int i) { return i < p0.B ? teff_tab[i] : teff_tab[kTeffTable + i - p0.B]; };
+      for (int i = tid - 32; i < nrows; i += kThreads - 32) {  // rank of row i: longer rows first, ties by index
+        const int ti = teff_row(i);
+        int rank = 0;
+        for (int j = 0; j < nrows; ++j) {
+          const int tj = teff_row(j);
+          rank += (tj > ti) | ((tj == ti) & (j < i));
+        }
+        map_order[rank] = static_cast<short>(i);
+      }
+      for (int c = tid - 32; c <= nck; c += kThreads - 32) {  // non-empty units of the chunks before c
+        int before = 0;
+        for (int j = 0; j < nrows; ++j) before += min((teff_row(j) + kChunk - 1) / kChunk, c);
+        map_pref[c] = before * p0.H;
+      }
+    }
+  }
+
   if (warp == 0) {
     tmem_alloc(&mi.tmem_base, kTmemCols);
     tmem_relinquish();
@@ -504,29 +531,6 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
   const uint32_t epoch = mi.epoch;
   bool ok = true;
 
-  // ---- ticket map: tickets -> non-empty units -------------------------------------
-  const bool use_map = p0.B <= kTeffTable && kDirs * p0.B <= kMapRows && nck <= kMapChunks;
-  short* map_order = reinterpret_cast<short*>(smem + kOffMap);
-  int* map_pref = reinterpret_cast<int*>(smem + kOffMap + kMapRows * 2);
-  if (use_map) {
-    const int nrows = kDirs * p0.B;
-    auto teff_row = [&](int i) { return i < p0.B ? teff_tab[i] : teff_tab[kTeffTable + i - p0.B]; };
-    for (int i = tid; i < nrows; i += kThreads) {  // rank of row i: longer rows first, ties by index
-      const int ti = teff_row(i);
-      int rank = 0;
-      for (int j = 0; j < nrows; ++j) {
-        const int tj = teff_row(j);
-        rank += (tj > ti) | ((tj == ti) & (j < i));
-      }
-      map_order[rank] = static_cast<short>(i);
-    }
-    for (int c = tid; c <= nck; c += kThreads) {  // non-empty units of the chunks before c
-      int before = 0;
-      for (int j = 0; j < nrows; ++j) before += min((teff_row(j) + kChunk - 1) / kChunk, c);
-      map_pref[c] = before * p0.H;
-    }
-    __syncthreads();
-  }
   // The unit of ticket tk (shp.units once every non-empty unit is handed out).
   auto ticket_unit = [&](int tk) -> int {
     if (!use_map) return tk;
@@ -1039,6 +1043,11 @@ __device__ __forceinline__ void recurrence_body(const RecurrenceParams& pd0, con
       bar_sync_n(kBarProducer, kProducerThreads);
       if constexpr (kLook) stage_unit(mi.next_ticket);
       pend = slot;  // MMA 1 is issued at the top of the next iteration
+      if (mi.next_ticket >= shp.units) {
+        // No next unit: issue it now (nothing in this CTA waits behind warp 6 any more).
+        if (tid == kMmaThread) issue_mma1(pend);
+        pend = -1;
+      }
       ++k;
     }
     // Units wholly past their row's length: zero their output rows. A static

@@ -169,6 +169,22 @@ def test_length_edge_cases():
     assert_recurrence_close(out, ref, "length edges")
 
 
+@pytest.mark.parametrize("batch,time,heads", [(260, 70, 1), (1, 64 * 513 + 5, 1)])
+def test_launches_beyond_the_ticket_map(batch, time, heads):
+    """Launches with more rows (260 > 256) or more chunks per row (514 > 512) than the
+    kernel's ticket map holds hand out every unit and skip the empty ones; both
+    against the oracle, with empty and partial rows."""
+    args = list(recurrence_inputs(batch, time, heads, kind="reftest", device=DEV))
+    if batch > 1:
+        lengths = lengths_uniform(batch, 0, time, seed=5)
+        lengths[:3] = torch.tensor([0, time, 1])
+    else:
+        lengths = torch.tensor([time - 100])
+    out = fused_recurrence(*args, lengths=lengths.to(DEV))
+    ref = O.mask_rows(oracle_out(args), lengths.numpy())
+    assert_recurrence_close(out, ref, f"beyond the ticket map {batch}x{time}")
+
+
 def test_padding_rows_zeroed_into_a_dirty_buffer():
     """Chunks wholly past a row's length are zeroed apart from the ticketed
     units; the caller's output buffer starts full of NaN, and most chunks of the

@@ -1,7 +1,7 @@
 """Benchmark of the fused Mamba-3 recurrence hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg1|cfg2]
+                    [--workload cfg1|cfg2|cfg3|cfg4] [--no-box] [--reference-gpu]
 
 One step is one pass of the hot path over one batch: at the default
 ``cfg1`` (B=16 clips, T=200, H=12, Hq=1, N=128, P=64, R=32) that is the
@@ -19,6 +19,10 @@ The default line also carries ``box``: the box-level sweep of the metric's
 audio-seconds/s (1024 synthetic clips through ``InferenceEngine(graphs=True)``,
 batches partitioned over the ranks, one logits all-gather; strong scaling), so a
 run at N = 1, 2, 4, 8 GPUs measures both halves of the metric (``--no-box`` skips it).
+
+``e2e`` runs the same call from pinned host buffers with the copies inside the
+timed region (``RaggedHostPipeline``: only the rows before each clip's length
+cross the host link; ``e2e.dense`` moves the whole padded tensors).
 
 ``--impl reference`` times the reference's arithmetic on the host CPU (the
 oracle port under ``oracle/``, all host threads) on the same workload.
